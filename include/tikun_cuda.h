@@ -1,0 +1,174 @@
+/*
+ * tikun-cuda: B200 (sm_100a) optimizer-step engine behind a C ABI.
+ *
+ * Plain C: pointers, sizes and enums only.  Every entry point returns an int
+ * status (TK_OK == 0); on failure tk_last_error() returns a message for the
+ * calling thread.  No entry point aborts the process.
+ *
+ * Buffers are owned by the caller.  p, m, v (and the Newton-Schulz matrix) are
+ * updated in place; g is read only.  Device pointers and host pointers are
+ * both accepted by tk_step_buffers (all leaves of one call must be of one
+ * kind): host leaves are staged through device memory, so a caller of the
+ * reference's CPU engine keeps its buffers where they are.
+ *
+ * Streams are passed as void* (a cudaStream_t; NULL is the legacy default
+ * stream).  Calls are stream-ordered; the synchronous variants return after
+ * the result they report is on the host.
+ */
+#ifndef TIKUN_CUDA_H
+#define TIKUN_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TK_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TK_API __attribute__((visibility("default")))
+#else
+#define TK_API
+#endif
+
+/* status codes */
+enum {
+  TK_OK = 0,
+  TK_ERR_INVALID = 1,     /* bad argument: null pointer, size, dtype, aliasing */
+  TK_ERR_VERIFY = 2,      /* static verification of the schedule failed */
+  TK_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  TK_ERR_ALLOC = 4,       /* device or pinned memory could not be obtained */
+  TK_ERR_UNSUPPORTED = 5, /* combination not implemented */
+  TK_ERR_DEVICE = 6       /* a kernel reported an error status (bounded wait expired) */
+};
+
+/* element types */
+enum { TK_F32 = 0, TK_BF16 = 1, TK_F16 = 2 };
+
+/* pointwise optimizers: the reference's PointwiseOp
+ * (crates/tikun-core/src/ir.rs:74-97; CustomDAG is not executed) */
+enum { TK_ADAMW = 0, TK_LION = 1, TK_SGD = 2 };
+
+/* schedule roles: WorkloadRole (crates/tikun-core/src/ir.rs:5-12) */
+enum { TK_ROLE_LOAD = 0, TK_ROLE_COMPUTE = 1, TK_ROLE_STORE = 2 };
+
+/* Newton-Schulz tensor-core operand type (accumulation is always f32) */
+enum { TK_NS_F16 = 0, TK_NS_BF16 = 1 };
+
+/* One schedule node: ScheduleIRNode (crates/tikun-core/src/ir.rs:16-36). */
+typedef struct {
+  const char* name;
+  int32_t role;
+  uint64_t tile_size;
+  uint64_t unroll_factor;
+  uint64_t vector_width;
+  uint64_t prefetch_distance;
+} tk_schedule_node;
+
+/* SchedulePipeline (crates/tikun-core/src/ir.rs:101-110).  max_norm > 0 means
+ * the pipeline carries GlobalReduction::GlobalL2Norm { max_norm }. */
+typedef struct {
+  const tk_schedule_node* nodes;
+  size_t n_nodes;
+  float max_norm;
+} tk_pipeline;
+
+/* One leaf: TensorBuffer (crates/tikun-cpu/src/lib.rs:25-32) with element
+ * types.  m and v are f32.  v may be NULL unless the optimizer is AdamW
+ * (tikun-py/src/lib.rs:178 passes 0 when the m2 list is empty). */
+typedef struct {
+  void* p;
+  const void* g;
+  float* m;
+  float* v;
+  uint64_t n;
+  int32_t p_dtype; /* TK_F32 or TK_BF16 */
+  int32_t g_dtype; /* TK_F32 or TK_BF16 */
+} tk_leaf;
+
+/* Pointwise hyperparameters (PointwiseOp fields).  For SGD, beta1 is the
+ * momentum (tikun-py/src/lib.rs:201-205); Lion ignores eps. */
+typedef struct {
+  float lr;
+  float beta1;
+  float beta2;
+  float eps;
+  float decay;
+} tk_hparams;
+
+/* ---------------------------------------------------------------------- */
+/* library                                                                 */
+/* ---------------------------------------------------------------------- */
+
+/* Message of the last failing call on this thread ("" if none). */
+TK_API const char* tk_last_error(void);
+
+/* TK_ABI_VERSION of the loaded library. */
+TK_API int tk_abi_version(void);
+
+/* Static verification: Verifier::verify (crates/tikun-core/src/verifier.rs:14-45).
+ * Empty pipeline, tile_size % 64 != 0, vector_width not a power of two or < 4
+ * fail with TK_ERR_VERIFY and the message "Static verification failed: [...]"
+ * (crates/tikun-cpu/src/lib.rs:74). */
+TK_API int tk_verify(const tk_pipeline* pipeline);
+
+/* LayoutPlan::from_shapes (crates/tikun-core/src/arena.rs:34-57): f32 leaves
+ * packed at 64-byte-aligned byte offsets. */
+TK_API int tk_layout_from_shapes(const uint64_t* num_elements, size_t n_leaves,
+                          uint64_t* byte_offsets, uint64_t* total_bytes);
+
+/* ---------------------------------------------------------------------- */
+/* two-tier pointwise step (Tier 1 global L2 norm, Tier 2 update)          */
+/* ---------------------------------------------------------------------- */
+
+/* CpuLowering::step_two_tier (crates/tikun-cpu/src/lib.rs:68-445): verify the
+ * pipeline, compute the clip scale if it carries a GlobalL2Norm, apply the
+ * optimizer to every leaf.  step is the AdamW step count (clamped to >= 1,
+ * lib.rs:152).  *clip_scale_out (host) receives the scale; the call returns
+ * after it is known. */
+TK_API int tk_step_two_tier(const tk_pipeline* pipeline, const tk_leaf* leaves, size_t n_leaves,
+                     int32_t kind, const tk_hparams* hp, uint64_t step,
+                     float* clip_scale_out, void* stream);
+
+/* step_fast_buffers (crates/tikun-py/src/lib.rs:155-222): builds the
+ * reference's three-node pipeline (load_g / fma_opt / store_p, vector width 8)
+ * with a GlobalL2Norm when max_norm > 0 and runs tk_step_two_tier.  Accepts
+ * device leaves or host leaves.  clip_scale_out may be NULL. */
+TK_API int tk_step_buffers(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                    const tk_hparams* hp, uint64_t step, float max_norm,
+                    float* clip_scale_out, void* stream);
+
+/* As tk_step_buffers for device leaves, without waiting: the clip scale is
+ * written to clip_scale_dev (device memory, may be NULL) in stream order. */
+TK_API int tk_step_buffers_async(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                          const tk_hparams* hp, uint64_t step, float max_norm,
+                          float* clip_scale_dev, void* stream);
+
+/* The pieces of the step, for callers that shard it (ZeRO-1 over ranks):
+ *   tk_grad_sumsq       sum over the leaves of g*g in f64 -> *sumsq_dev
+ *   tk_clip_scale       *scale_dev = clip scale of *sumsq_dev (lib.rs:117-122)
+ *   tk_apply_pointwise  Tier 2 over the leaves with the scale at scale_dev
+ *                       (NULL: no clipping)
+ * The caller may all-reduce *sumsq_dev between the first two. */
+TK_API int tk_grad_sumsq(const tk_leaf* leaves, size_t n_leaves, double* sumsq_dev, void* stream);
+TK_API int tk_clip_scale(const double* sumsq_dev, float max_norm, float* scale_dev, void* stream);
+TK_API int tk_apply_pointwise(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                       const tk_hparams* hp, uint64_t step, const float* scale_dev,
+                       void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* measurement                                                             */
+/* ---------------------------------------------------------------------- */
+
+/* While set (two cudaEvent_t handles), every step call made by this thread
+ * records start_event on its stream just before its first Tier-2 (update)
+ * launch and stop_event just after its last, so a caller can time the update
+ * kernels alone inside a running loop.  Pass NULLs to clear. */
+TK_API int tk_set_update_events(void* start_event, void* stop_event);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TIKUN_CUDA_H */

@@ -1,0 +1,108 @@
+"""C-ABI checks that need no GPU: the library loads, exports every entry point
+include/*.h declares, and the host-only entry points (verifier, layout plan)
+behave like the reference's."""
+import glob
+import os
+import re
+
+import pytest
+
+from tikun_b200 import _native
+from tikun_b200.universal import _flatten_pytree, _extract_pointer_and_len
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(REPO, "include", "*.h")):
+        src = open(h).read()
+        names.update(re.findall(r"TK_API\s+[\w\s\*]*?\b(tk_\w+)\s*\(", src))
+    return sorted(names)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.lib()
+    syms = declared_symbols()
+    assert "tk_step_buffers" in syms and "tk_last_error" in syms
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_abi_version():
+    assert _native.lib().tk_abi_version() == 1
+
+
+def test_library_is_the_in_tree_build():
+    assert os.path.realpath(_native.LIB_PATH).startswith(os.path.join(REPO, "tikun_b200"))
+
+
+# -- verifier: crates/tikun-core/src/verifier.rs:14-45 ----------------------
+def test_verify_accepts_reference_pipeline():
+    nodes = [("load_g", 0, 64, 4, 8, 2), ("fma_opt", 1, 64, 4, 8, 2), ("store_p", 2, 64, 4, 8, 2)]
+    _native.verify(nodes)
+
+
+def test_verify_empty_pipeline():
+    with pytest.raises(_native.TikunError) as e:
+        _native.verify([])
+    assert str(e.value) == "Static verification failed: [EmptyPipeline]"
+    assert e.value.status == _native.TK_ERR_VERIFY
+
+
+def test_verify_reports_every_violation_in_order():
+    nodes = [("a", 0, 100, 4, 3, 2), ("b", 1, 64, 4, 8, 2), ("c", 2, 128, 4, 2, 2)]
+    with pytest.raises(_native.TikunError) as e:
+        _native.verify(nodes)
+    assert str(e.value) == (
+        'Static verification failed: [MisalignedCacheLine { node_name: "a", tile_size: 100 }, '
+        'InvalidVectorWidth { node_name: "a", width: 3 }, '
+        'InvalidVectorWidth { node_name: "c", width: 2 }]')
+
+
+@pytest.mark.parametrize("width,ok", [(0, False), (1, False), (2, False), (4, True), (6, False),
+                                      (8, True), (64, True), (1 << 20, True)])
+def test_verify_vector_width_rule(width, ok):
+    nodes = [("n", 1, 64, 4, width, 2)]
+    if ok:
+        _native.verify(nodes)
+    else:
+        with pytest.raises(_native.TikunError):
+            _native.verify(nodes)
+
+
+# -- layout: crates/tikun-core/src/arena.rs:34-57, tests :219-228 -------------
+def test_layout_matches_oracle_and_alignment():
+    import oracle
+
+    for shapes in ([100, 513, 2048, 17], [1, 1, 1], [16, 16], [], [38597376, 786432, 768, 768]):
+        offs, total = _native.layout_from_shapes(shapes)
+        assert all(o % 64 == 0 for o in offs)
+        assert (offs, total) == oracle.layout_from_shapes(shapes)
+
+
+# -- host-side argument handling (no CUDA call is reached) ---------------------
+def test_mismatched_list_lengths_raise_value_error():
+    with pytest.raises(ValueError):
+        _native.step_fast_buffers([1, 2], [3], [4, 5], [6, 7], [1, 1], 0.0, "adamw", 1, 1e-3,
+                                  0.9, 0.999, 1e-8, 0.0)
+
+
+def test_opt_kind_dispatch_matches_reference():
+    # tikun-py/src/lib.rs:194-214: exact "lion"/"sgd", anything else AdamW
+    assert _native.opt_kind("lion") == _native.TK_LION
+    assert _native.opt_kind("sgd") == _native.TK_SGD
+    assert _native.opt_kind("adamw") == _native.TK_ADAMW
+    assert _native.opt_kind("Lion") == _native.TK_ADAMW
+    assert _native.opt_kind("anything") == _native.TK_ADAMW
+
+
+def test_pytree_flattening_order():
+    import numpy as np
+
+    a, b, c = np.zeros(3, np.float32), np.zeros(4, np.float32), np.zeros(5, np.float32)
+    tree = {"x": a, "y": [b, (c,)], "raw": (1234, 7)}
+    flat = _flatten_pytree(tree)
+    assert flat[0] is a and flat[1] is b and flat[2] is c and flat[3] == (1234, 7)
+    assert _extract_pointer_and_len(flat[3]) == (1234, 7)
+    assert _extract_pointer_and_len(b) == (b.ctypes.data, 4)

@@ -1,0 +1,262 @@
+"""Parity of the CUDA Tier 1 / Tier 2 step with the oracle (tikun-cpu's x86
+scalar arithmetic), through the reference-facing C ABI.
+
+Bar: max relative error <= 1e-6 per element on p, m, v after 10 steps (stated
+in helpers.POINTWISE_RTOL); the kernels are written to be bit-identical and the
+tests check bit-identity.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import (POINTWISE_RTOL, Leaves, assert_bitexact, gpt2_small_init, gpt2_small_sizes,
+                     max_rel_err, tk_dtype, to_np)
+from tikun_b200 import _native
+
+pytestmark = pytest.mark.gpu
+
+
+def test_flat_adamw_ten_steps_no_clip():
+    """Flat-buffer AdamW, fresh N(0, 1e-3) grads each step, lr 1e-3, betas
+    (0.9, 0.999), eps 1e-8, decay 0.01, no clip: the flat-leaf workload at 1e6+3
+    elements (ragged tail)."""
+    L = Leaves([1_000_003])
+    for step in range(1, 11):
+        L.new_grads(1e-3)
+        s_gpu = L.gpu_step(step, 0.0)
+        s_ref = L.oracle_step(step, 0.0)
+        assert s_gpu == s_ref == 1.0
+    L.check("flat adamw")
+    assert max_rel_err(to_np(L.p[0]), L.np_p[0]) <= POINTWISE_RTOL
+
+
+@pytest.mark.parametrize("scale_down", [True, False], ids=["d128", "gpt2-small-full"])
+def test_gpt2_clipped_adamw(scale_down):
+    """Clipped AdamW (global norm 1.0) over the GPT-2-small leaf table: 148
+    leaves; grads N(0, 1e-2) so the clip triggers.  Full size is the
+    124,439,808-parameter table (3 steps there to bound the oracle's time)."""
+    d, vocab, ctx, steps = (128, 1000, 256, 10) if scale_down else (768, 50257, 1024, 3)
+    sizes = gpt2_small_sizes(d=d, vocab=vocab, ctx=ctx)
+    assert len(sizes) == 148
+    if not scale_down:
+        assert sum(sizes) == 124_439_808
+    L = Leaves(sizes)
+    L.p = gpt2_small_init(sizes, d)
+    L.np_p = [to_np(t) for t in L.p]
+    for step in range(1, steps + 1):
+        L.new_grads(1e-2)
+        s_gpu = L.gpu_step(step, 1.0)
+        s_ref = L.oracle_step(step, 1.0)
+        assert s_ref < 1.0, "clip must trigger"
+        assert s_gpu == s_ref
+    L.check("gpt2 clip")
+
+
+@pytest.mark.parametrize("kind", ["adamw", "lion", "sgd"])
+def test_mixed_dtypes_and_ragged_sizes(kind):
+    sizes = [1, 3, 15, 17, 4097, 0, 65536 + 5, 777]
+    pdt = [torch.float32, torch.bfloat16, torch.float32, torch.bfloat16, torch.bfloat16,
+           torch.float32, torch.float32, torch.bfloat16]
+    gdt = [torch.float32, torch.bfloat16, torch.bfloat16, torch.float32, torch.bfloat16,
+           torch.float32, torch.float32, torch.bfloat16]
+    L = Leaves(sizes, pdt, gdt, kind=kind)
+    for step in range(1, 6):
+        L.new_grads(0.05)
+        kw = dict(lr=1e-2, b1=0.9, b2=0.99 if kind == "lion" else 0.999, decay=0.01)
+        s_gpu = L.gpu_step(step, 0.5, **kw)
+        s_ref = L.oracle_step(step, 0.5, **kw)
+        assert s_gpu == s_ref
+    L.check(kind)
+
+
+def test_unaligned_views_take_the_scalar_path():
+    base = [torch.randn(5000, device="cuda") * 0.02 for _ in range(4)]
+    L = Leaves([4999, 4998])
+    # offsets of 1 and 2 floats: not 16-byte aligned
+    L.p = [base[0][1:], base[1][2:]]
+    L.m = [torch.zeros(5000, device="cuda")[1:], torch.zeros(5000, device="cuda")[2:]]
+    L.v = [torch.zeros(5001, device="cuda")[2:], torch.zeros(5001, device="cuda")[3:]]
+    L.np_p = [to_np(t) for t in L.p]
+    L.np_m = [to_np(t) for t in L.m]
+    L.np_v = [to_np(t) for t in L.v]
+    for step in range(1, 4):
+        L.new_grads(1e-2)
+        L.g = [torch.cat([torch.zeros(1, device="cuda"), g])[1:] for g in L.g]
+        assert L.gpu_step(step, 1.0) == L.oracle_step(step, 1.0)
+    L.check("unaligned")
+
+
+def test_many_leaves_span_several_launches():
+    rng = np.random.default_rng(0)
+    sizes = [int(x) for x in rng.integers(1, 3000, size=500)]
+    L = Leaves(sizes)
+    for step in range(1, 4):
+        L.new_grads(0.1)
+        assert L.gpu_step(step, 1.0) == L.oracle_step(step, 1.0)
+    L.check("500 leaves")
+
+
+def test_nonfinite_gradients_follow_reference_clip_rule():
+    for bad, want in ((float("nan"), 1.0), (float("inf"), 0.0)):
+        L = Leaves([1000, 33])
+        L.new_grads(0.1)
+        L.g[0][17] = bad
+        L.np_g[0][17] = bad
+        s_gpu = L.gpu_step(1, 1.0)
+        s_ref = L.oracle_step(1, 1.0)
+        assert s_gpu == s_ref == want
+        L.check(f"nonfinite {bad}")
+
+
+def test_step_zero_is_clamped_to_one():
+    L = Leaves([4096])
+    L.new_grads()
+    L.gpu_step(0, 0.0)
+    L.oracle_step(0, 0.0)
+    L.check("step 0")
+
+
+def test_empty_call_returns_unit_scale():
+    assert _native.step_fast_buffers([], [], [], [], [], 1.0, "adamw", 1, 1e-3, 0.9, 0.999,
+                                     1e-8, 0.0) == 1.0
+
+
+def test_host_buffers_are_staged():
+    """numpy (pageable) leaves through the same entry point, as a caller of the
+    CPU engine would pass them."""
+    rng = np.random.default_rng(3)
+    sizes = [10000, 17, 4096]
+    p = [(rng.standard_normal(n) * 0.02).astype(np.float32) for n in sizes]
+    m = [np.zeros(n, np.float32) for n in sizes]
+    v = [np.zeros(n, np.float32) for n in sizes]
+    rp, rm, rv = [x.copy() for x in p], [x.copy() for x in m], [x.copy() for x in v]
+    for step in range(1, 4):
+        g = [(rng.standard_normal(n) * 0.1).astype(np.float32) for n in sizes]
+        s = _native.step_fast_buffers([a.ctypes.data for a in p], [a.ctypes.data for a in g],
+                                      [a.ctypes.data for a in m], [a.ctypes.data for a in v],
+                                      sizes, 1.0, "adamw", step, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+        r = oracle.step_two_tier(rp, g, rm, rv, oracle.ADAMW, 1e-3, 0.9, 0.999, 1e-8, 0.01,
+                                 step, 1.0)
+        assert s == r
+    for a, b in zip(p + m + v, rp + rm + rv):
+        assert_bitexact(a, b, "host")
+
+
+def test_pinned_host_buffers():
+    n = 1 << 16
+    p = (torch.randn(n) * 0.02).pin_memory()
+    g = (torch.randn(n) * 0.1).pin_memory()
+    m, v = torch.zeros(n).pin_memory(), torch.zeros(n).pin_memory()
+    rp, rg, rm, rv = p.numpy().copy(), g.numpy().copy(), m.numpy().copy(), v.numpy().copy()
+    s = _native.step_fast_buffers([p.data_ptr()], [g.data_ptr()], [m.data_ptr()],
+                                  [v.data_ptr()], [n], 1.0, "adamw", 1, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+    r = oracle.step_two_tier([rp], [rg], [rm], [rv], oracle.ADAMW, 1e-3, 0.9, 0.999, 1e-8,
+                             0.01, 1, 1.0)
+    assert s == r
+    assert_bitexact(p.numpy(), rp, "pinned p")
+
+
+def test_rejects_aliased_leaves():
+    t = torch.zeros(100, device="cuda")
+    g = torch.zeros(100, device="cuda")
+    m1, m2 = torch.zeros(100, device="cuda"), torch.zeros(100, device="cuda")
+    w1, w2 = torch.zeros(100, device="cuda"), torch.zeros(100, device="cuda")
+    with pytest.raises(ValueError, match="overlap"):
+        _native.step_fast_buffers([t.data_ptr(), t.data_ptr()], [g.data_ptr(), g.data_ptr()],
+                                  [m1.data_ptr(), m2.data_ptr()], [w1.data_ptr(), w2.data_ptr()],
+                                  [100, 100], 0.0, "adamw", 1, 1e-3, 0.9, 0.999, 1e-8, 0.0)
+    with pytest.raises(ValueError, match="overlap"):  # p overlaps its own m
+        _native.step_fast_buffers([t.data_ptr()], [g.data_ptr()], [t.data_ptr() + 200],
+                                  [w1.data_ptr()], [100], 0.0, "adamw", 1, 1e-3, 0.9, 0.999,
+                                  1e-8, 0.0)
+
+
+def test_adamw_without_second_moment_is_an_error():
+    t, g, m = (torch.zeros(10, device="cuda") for _ in range(3))
+    with pytest.raises(ValueError, match="second-moment"):
+        _native.step_fast_buffers([t.data_ptr()], [g.data_ptr()], [m.data_ptr()], [], [10], 0.0,
+                                  "adamw", 1, 1e-3, 0.9, 0.999, 1e-8, 0.0)
+    # Lion and SGD take an empty m2 list (tikun-py/src/lib.rs:178)
+    _native.step_fast_buffers([t.data_ptr()], [g.data_ptr()], [m.data_ptr()], [], [10], 0.0,
+                              "sgd", 1, 1e-3, 0.9, 0.999, 1e-8, 0.0)
+
+
+def test_mixed_host_and_device_is_an_error():
+    t, m, v = (torch.zeros(10, device="cuda") for _ in range(3))
+    g = np.zeros(10, np.float32)
+    with pytest.raises(ValueError, match="mixed"):
+        _native.step_fast_buffers([t.data_ptr()], [g.ctypes.data], [m.data_ptr()],
+                                  [v.data_ptr()], [10], 0.0, "adamw", 1, 1e-3, 0.9, 0.999, 1e-8, 0.0)
+
+
+def test_step_two_tier_runs_the_verifier():
+    t, g, m, v = (torch.zeros(10, device="cuda") for _ in range(4))
+    leaves, n = _native.make_leaves([t.data_ptr()], [g.data_ptr()], [m.data_ptr()],
+                                    [v.data_ptr()], [10])
+    nodes = (_native.TkScheduleNode * 1)(_native.TkScheduleNode(b"bad", 1, 65, 4, 8, 2))
+    pl = _native.TkPipeline(nodes, 1, 0.0)
+    hp = _native.TkHParams(1e-3, 0.9, 0.999, 1e-8, 0.0)
+    out = ctypes.c_float()
+    st = _native.lib().tk_step_two_tier(ctypes.byref(pl), leaves, n, 0, ctypes.byref(hp), 1,
+                                        ctypes.byref(out), None)
+    assert st == _native.TK_ERR_VERIFY
+    assert _native.lib().tk_last_error().decode() == (
+        'Static verification failed: [MisalignedCacheLine { node_name: "bad", tile_size: 65 }]')
+
+
+def test_sharded_pieces_compose_to_the_full_step():
+    """tk_grad_sumsq -> tk_clip_scale -> tk_apply_pointwise gives the same bits
+    as tk_step_buffers (the ZeRO-1 path all-reduces the sum in between)."""
+    sizes = [12345, 678, 90000]
+    A = Leaves(sizes, seed=9)
+    B = Leaves(sizes, seed=9)
+    A.new_grads(0.1)
+    B.g = [g.clone() for g in A.g]
+    sA = A.gpu_step(1, 1.0)
+    leaves, n = _native.make_leaves([t.data_ptr() for t in B.p], [t.data_ptr() for t in B.g],
+                                    [t.data_ptr() for t in B.m], [t.data_ptr() for t in B.v],
+                                    sizes)
+    ss = torch.zeros(1, dtype=torch.float64, device="cuda")
+    sc = torch.zeros(1, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    L = _native.lib()
+    _native.check(L.tk_grad_sumsq(leaves, n, ss.data_ptr(), stream))
+    _native.check(L.tk_clip_scale(ss.data_ptr(), 1.0, sc.data_ptr(), stream))
+    hp = _native.TkHParams(1e-3, 0.9, 0.999, 1e-8, 0.01)
+    _native.check(L.tk_apply_pointwise(leaves, n, 0, ctypes.byref(hp), 1, sc.data_ptr(), stream))
+    assert float(sc.item()) == sA
+    ref_sum = sum(float(np.sum(t.astype(np.float64) ** 2)) for t in A.np_g)
+    assert abs(float(ss.item()) - ref_sum) <= 1e-12 * ref_sum
+    for a, b in zip(A.p + A.m + A.v, B.p + B.m + B.v):
+        assert_bitexact(to_np(b), to_np(a), "sharded")
+
+
+# -- front-end: the reference's Python optimizers on CUDA tensors ------------
+@pytest.mark.parametrize("case", ["adamw_clip", "adamw", "lion", "sgd"])
+def test_frontend_matches_reference_frontend(golden_dir, case):
+    """tikun_b200.AdamW/Lion/SGD on CUDA tensors against the reference's own
+    front-end (python/tikun/universal.py) run over the oracle: bit-identical."""
+    import tikun_b200
+
+    z = np.load(os.path.join(golden_dir, "frontend_reference.npz"))
+    keys = ["w", "b", "ln", "emb"]
+    params = {k: torch.tensor(z[f"{case}/init/{k}"], device="cuda", requires_grad=True)
+              for k in keys}
+    make = {
+        "adamw_clip": lambda ps: tikun_b200.AdamW(ps, lr=1e-3, max_norm=1.0),
+        "adamw": lambda ps: tikun_b200.AdamW(ps, lr=1e-3),
+        "lion": lambda ps: tikun_b200.Lion(ps, lr=1e-4, max_norm=0.5),
+        "sgd": lambda ps: tikun_b200.SGD(ps, lr=1e-2, momentum=0.9, weight_decay=0.01),
+    }[case]
+    opt = make(params)
+    for s in range(3):
+        for k in keys:
+            params[k].grad = torch.tensor(z[f"{case}/grad{s}/{k}"], device="cuda")
+        opt.step()
+    torch.cuda.synchronize()
+    for k in keys:
+        assert_bitexact(to_np(params[k]), z[f"{case}/final/{k}"], f"{case}/{k}")

@@ -1,0 +1,551 @@
+// C-ABI entry points of the pointwise step (include/tikun_cuda.h): the static
+// verifier, the layout plan, leaf validation and the Tier 1 / Tier 2
+// orchestration over the CUDA kernels in tk_pointwise.cu.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "tk_internal.h"
+
+namespace tk {
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(TK_ERR_CUDA, "CUDA error %s (%s) in %s", cudaGetErrorName(e),
+                   cudaGetErrorString(e), what);
+}
+
+// ------------------------------------------------------------------ device info
+int sm_count(int* out) {
+  static int cached[64] = {0};
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  if (cached[dev] == 0) {
+    int n = 0;
+    TK_CUDA_TRY(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    cached[dev] = n;
+  }
+  *out = cached[dev];
+  return TK_OK;
+}
+
+// ------------------------------------------------------------------ scratch pool
+static std::mutex g_pool_mu;
+static cudaMemPool_t g_pools[64] = {};
+
+static int device_pool(cudaMemPool_t* out) {
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  if (g_pools[dev] == nullptr) {
+    cudaMemPoolProps props;
+    std::memset(&props, 0, sizeof(props));
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool;
+    TK_CUDA_TRY(cudaMemPoolCreate(&pool, &props));
+    uint64_t keep = UINT64_MAX;  // keep freed scratch cached for the next step
+    TK_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    g_pools[dev] = pool;
+  }
+  *out = g_pools[dev];
+  return TK_OK;
+}
+
+Scratch::~Scratch() {
+  if (ptr_ != nullptr) cudaFreeAsync(ptr_, stream_);
+}
+
+int Scratch::alloc(size_t bytes, cudaStream_t s) {
+  if (ptr_ != nullptr) return set_error(TK_ERR_INVALID, "scratch allocated twice");
+  cudaMemPool_t pool;
+  TK_TRY(device_pool(&pool));
+  stream_ = s;
+  cudaError_t e = cudaMallocFromPoolAsync(&ptr_, bytes ? bytes : 16, pool, s);
+  if (e != cudaSuccess) {
+    ptr_ = nullptr;
+    return set_error(TK_ERR_ALLOC, "could not allocate %zu bytes of device scratch: %s", bytes,
+                     cudaGetErrorString(e));
+  }
+  return TK_OK;
+}
+
+// ------------------------------------------------------------------ verifier
+// Verifier::verify, crates/tikun-core/src/verifier.rs:14-45, with the error
+// text of `format!("Static verification failed: {:?}", violations)`
+// (crates/tikun-cpu/src/lib.rs:74).
+static bool is_pow2(uint64_t x) { return x != 0 && (x & (x - 1)) == 0; }
+
+static std::string rust_debug_str(const char* s) {
+  std::string out = "\"";
+  for (const char* c = s ? s : ""; *c; ++c) {
+    if (*c == '"' || *c == '\\') out += '\\';
+    out += *c;
+  }
+  return out + "\"";
+}
+
+static int verify_pipeline(const tk_pipeline* pl) {
+  if (pl == nullptr) return set_error(TK_ERR_INVALID, "pipeline is NULL");
+  if (pl->n_nodes == 0) return set_error(TK_ERR_VERIFY, "Static verification failed: [EmptyPipeline]");
+  if (pl->nodes == nullptr) return set_error(TK_ERR_INVALID, "pipeline nodes are NULL");
+  std::vector<std::string> errs;
+  for (size_t i = 0; i < pl->n_nodes; ++i) {
+    const tk_schedule_node& n = pl->nodes[i];
+    if (n.tile_size % 64 != 0)
+      errs.push_back("MisalignedCacheLine { node_name: " + rust_debug_str(n.name) +
+                     ", tile_size: " + std::to_string(n.tile_size) + " }");
+    if (!is_pow2(n.vector_width) || n.vector_width < 4)
+      errs.push_back("InvalidVectorWidth { node_name: " + rust_debug_str(n.name) +
+                     ", width: " + std::to_string(n.vector_width) + " }");
+  }
+  if (errs.empty()) return TK_OK;
+  std::string msg = "Static verification failed: [";
+  for (size_t i = 0; i < errs.size(); ++i) msg += (i ? ", " : "") + errs[i];
+  msg += "]";
+  return set_error(TK_ERR_VERIFY, "%s", msg.c_str());
+}
+
+// ------------------------------------------------------------------ leaves
+static size_t esize(int dt) { return dt == TK_F32 ? 4 : 2; }
+
+enum class Residency { kNone, kDevice, kHost };
+
+static int classify(const void* ptr, Residency* r, int dev) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(TK_ERR_INVALID, "cannot classify pointer %p: %s", ptr, cudaGetErrorString(e));
+  }
+  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+    if (a.type == cudaMemoryTypeDevice && a.device != dev)
+      return set_error(TK_ERR_INVALID, "pointer %p lives on device %d, the current device is %d",
+                       ptr, a.device, dev);
+    *r = Residency::kDevice;
+  } else {
+    *r = Residency::kHost;
+  }
+  return TK_OK;
+}
+
+struct Range {
+  uintptr_t lo, hi;
+  bool writable;
+};
+
+// Rejects null or mismatched fields, bad dtypes, any overlap between a range
+// the step writes (p, m, v) and any other range, and a mix of host and device
+// leaves.  Reports where the leaves live.
+static int validate_leaves(const tk_leaf* leaves, size_t n, int kind, Residency* where) {
+  *where = Residency::kNone;
+  if (n == 0) return TK_OK;
+  if (leaves == nullptr) return set_error(TK_ERR_INVALID, "leaves is NULL with n_leaves=%zu", n);
+  if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD)
+    return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  std::vector<Range> ranges;
+  ranges.reserve(n * 4);
+  for (size_t i = 0; i < n; ++i) {
+    const tk_leaf& L = leaves[i];
+    if (L.p_dtype != TK_F32 && L.p_dtype != TK_BF16)
+      return set_error(TK_ERR_INVALID, "leaf %zu: p_dtype %d is not f32 or bf16", i, L.p_dtype);
+    if (L.g_dtype != TK_F32 && L.g_dtype != TK_BF16)
+      return set_error(TK_ERR_INVALID, "leaf %zu: g_dtype %d is not f32 or bf16", i, L.g_dtype);
+    if (L.n == 0) continue;
+    if (L.p == nullptr || L.g == nullptr || L.m == nullptr)
+      return set_error(TK_ERR_INVALID, "leaf %zu: null p, g or m pointer", i);
+    if (kind == TK_ADAMW && L.v == nullptr)
+      return set_error(TK_ERR_INVALID, "leaf %zu: AdamW needs a second-moment (m2) buffer", i);
+    const uintptr_t p = (uintptr_t)L.p, g = (uintptr_t)L.g, m = (uintptr_t)L.m;
+    ranges.push_back({p, p + L.n * esize(L.p_dtype), true});
+    ranges.push_back({g, g + L.n * esize(L.g_dtype), false});
+    ranges.push_back({m, m + L.n * 4, true});
+    if (kind == TK_ADAMW) ranges.push_back({(uintptr_t)L.v, (uintptr_t)L.v + L.n * 4, true});
+    const void* ptrs[4] = {L.p, L.g, L.m, kind == TK_ADAMW ? (const void*)L.v : nullptr};
+    for (const void* ptr : ptrs) {
+      if (ptr == nullptr) continue;
+      Residency r;
+      TK_TRY(classify(ptr, &r, dev));
+      if (*where == Residency::kNone) *where = r;
+      else if (*where != r)
+        return set_error(TK_ERR_INVALID,
+                         "leaf %zu: host and device buffers are mixed in one call", i);
+    }
+  }
+  std::sort(ranges.begin(), ranges.end(),
+            [](const Range& a, const Range& b) { return a.lo < b.lo; });
+  uintptr_t max_any = 0, max_w = 0;
+  for (const Range& r : ranges) {
+    if ((r.writable && max_any > r.lo) || max_w > r.lo)
+      return set_error(TK_ERR_INVALID,
+                       "leaf buffers overlap at %p: a buffer the step writes (p, m or v) "
+                       "shares memory with another buffer",
+                       (void*)r.lo);
+    max_any = std::max(max_any, r.hi);
+    if (r.writable) max_w = std::max(max_w, r.hi);
+  }
+  return TK_OK;
+}
+
+static bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
+
+// Splits the non-empty leaves with one (p, g) dtype pair into launch tables.
+static void build_tables(const tk_leaf* leaves, size_t n, int kind, int pdt, int gdt,
+                         std::vector<LeafTable>* out) {
+  LeafTable* t = nullptr;
+  for (size_t i = 0; i < n; ++i) {
+    const tk_leaf& L = leaves[i];
+    if (L.n == 0 || L.p_dtype != pdt || L.g_dtype != gdt) continue;
+    if (t == nullptr || t->n_leaves == kMaxLeavesPerLaunch) {
+      out->emplace_back();
+      t = &out->back();
+      std::memset(t, 0, sizeof(*t));
+    }
+    LeafDesc& d = t->leaf[t->n_leaves++];
+    d.p = L.p;
+    d.g = L.g;
+    d.m = L.m;
+    d.v = kind == TK_ADAMW ? L.v : nullptr;
+    d.n = L.n;
+    d.q_begin = t->total_quads;
+    d.vec_ok = aligned(L.p, 4 * esize(pdt)) && aligned(L.g, 4 * esize(gdt)) &&
+               aligned(L.m, 16) && (kind != TK_ADAMW || aligned(L.v, 16));
+    t->total_quads += (L.n + 3) / 4;
+  }
+}
+
+// Rust f32::powi with a runtime exponent: binary exponentiation in f32.
+static float powi_f32(float a, int32_t b) {
+  const bool recip = b < 0;
+  uint32_t e = recip ? (uint32_t)(-(int64_t)b) : (uint32_t)b;
+  float r = 1.0f;
+  for (;;) {
+    if (e & 1u) r *= a;
+    e >>= 1;
+    if (e == 0) break;
+    a *= a;
+  }
+  return recip ? 1.0f / r : r;
+}
+
+static PointwiseConsts make_consts(int kind, const tk_hparams& hp, uint64_t step) {
+  PointwiseConsts c;
+  c.lr = hp.lr;
+  c.b1 = hp.beta1;
+  c.b2 = hp.beta2;
+  c.eps = hp.eps;
+  c.decay = hp.decay;
+  volatile float one = 1.0f;  // keep 1 - b in f32, as the reference does
+  c.omb1 = one - hp.beta1;
+  c.omb2 = one - hp.beta2;
+  c.bc1 = c.bc2 = 1.0f;
+  if (kind == TK_ADAMW) {
+    // lib.rs:152-154
+    const int32_t step_val = (int32_t)(step < 1 ? 1 : (step > INT32_MAX ? INT32_MAX : step));
+    c.bc1 = one - powi_f32(hp.beta1, step_val);
+    c.bc2 = one - powi_f32(hp.beta2, step_val);
+  }
+  return c;
+}
+
+struct Plan {
+  std::vector<LeafTable> tables;
+  std::vector<int> pdt, gdt;
+};
+
+static void make_plan(const tk_leaf* leaves, size_t n, int kind, Plan* plan) {
+  const int dts[2] = {TK_F32, TK_BF16};
+  for (int pd : dts)
+    for (int gd : dts) {
+      size_t before = plan->tables.size();
+      build_tables(leaves, n, kind, pd, gd, &plan->tables);
+      for (size_t i = before; i < plan->tables.size(); ++i) {
+        plan->pdt.push_back(pd);
+        plan->gdt.push_back(gd);
+      }
+    }
+}
+
+// Tier 1 partials for every table into one buffer; returns the block count.
+static int launch_norm(const Plan& plan, Scratch* scratch, double** partials, int* n_partials,
+                       cudaStream_t s) {
+  std::vector<int> blocks;
+  int total = 0;
+  for (const LeafTable& t : plan.tables) {
+    const int b = sumsq_blocks_for(t.total_quads);
+    if (b <= 0) return set_error(TK_ERR_CUDA, "could not size the norm grid");
+    blocks.push_back(b);
+    total += b;
+  }
+  TK_TRY(scratch->alloc(sizeof(double) * (size_t)std::max(total, 1) + 64, s));
+  double* base = static_cast<double*>(scratch->get());
+  int off = 0;
+  for (size_t i = 0; i < plan.tables.size(); ++i) {
+    TK_TRY(launch_sumsq_partials(plan.tables[i], plan.gdt[i], base + off, blocks[i], s));
+    off += blocks[i];
+  }
+  *partials = base;
+  *n_partials = total;
+  return TK_OK;
+}
+
+// Measurement hook (tk_set_update_events).
+static thread_local cudaEvent_t g_update_start = nullptr;
+static thread_local cudaEvent_t g_update_stop = nullptr;
+
+// The device-resident step.  scale_dev (may be null) receives the clip scale.
+static int step_device(const tk_leaf* leaves, size_t n, int kind, const tk_hparams& hp,
+                       uint64_t step, float max_norm, float* scale_dev, bool* scale_written,
+                       cudaStream_t s) {
+  *scale_written = false;
+  Plan plan;
+  make_plan(leaves, n, kind, &plan);
+  if (plan.tables.empty()) return TK_OK;  // nothing to update; the scale is 1
+  const PointwiseConsts c = make_consts(kind, hp, step);
+  Scratch norm_scratch;
+  double* partials = nullptr;
+  int n_partials = 0;
+  if (max_norm > 0.0f) TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s));
+  if (g_update_start) TK_CUDA_TRY(cudaEventRecord(g_update_start, s));
+  for (size_t i = 0; i < plan.tables.size(); ++i) {
+    TK_TRY(launch_pointwise(plan.tables[i], kind, plan.pdt[i], plan.gdt[i], c, partials,
+                            n_partials, max_norm, nullptr, i == 0 ? scale_dev : nullptr, s));
+  }
+  if (g_update_stop) TK_CUDA_TRY(cudaEventRecord(g_update_stop, s));
+  *scale_written = partials != nullptr && scale_dev != nullptr;
+  return TK_OK;
+}
+
+// Host leaves: copy everything the step touches into device scratch, run the
+// device step there and copy p, m, v back.  Synchronous.
+static int step_host(const tk_leaf* leaves, size_t n, int kind, const tk_hparams& hp,
+                     uint64_t step, float max_norm, float* clip_scale_out, cudaStream_t s) {
+  size_t bytes = 64;
+  for (size_t i = 0; i < n; ++i) {
+    const tk_leaf& L = leaves[i];
+    if (L.n == 0) continue;
+    bytes += (L.n * esize(L.p_dtype) + 255) / 256 * 256;
+    bytes += (L.n * esize(L.g_dtype) + 255) / 256 * 256;
+    bytes += (L.n * 4 + 255) / 256 * 256 * (kind == TK_ADAMW ? 2 : 1);
+  }
+  Scratch stage;
+  TK_TRY(stage.alloc(bytes, s));
+  char* cur = static_cast<char*>(stage.get());
+  float* scale_dev = reinterpret_cast<float*>(cur);
+  cur += 64;
+  std::vector<tk_leaf> dev(leaves, leaves + n);
+  for (size_t i = 0; i < n; ++i) {
+    const tk_leaf& L = leaves[i];
+    if (L.n == 0) continue;
+    auto take = [&](size_t b) {
+      char* r = cur;
+      cur += (b + 255) / 256 * 256;
+      return r;
+    };
+    char* gdev = take(L.n * esize(L.g_dtype));
+    dev[i].p = take(L.n * esize(L.p_dtype));
+    dev[i].g = gdev;
+    dev[i].m = reinterpret_cast<float*>(take(L.n * 4));
+    dev[i].v = kind == TK_ADAMW ? reinterpret_cast<float*>(take(L.n * 4)) : nullptr;
+    TK_CUDA_TRY(cudaMemcpyAsync(gdev, L.g, L.n * esize(L.g_dtype), cudaMemcpyHostToDevice, s));
+    TK_CUDA_TRY(cudaMemcpyAsync(dev[i].p, L.p, L.n * esize(L.p_dtype), cudaMemcpyHostToDevice, s));
+    TK_CUDA_TRY(cudaMemcpyAsync(dev[i].m, L.m, L.n * 4, cudaMemcpyHostToDevice, s));
+    if (kind == TK_ADAMW)
+      TK_CUDA_TRY(cudaMemcpyAsync(dev[i].v, L.v, L.n * 4, cudaMemcpyHostToDevice, s));
+  }
+  bool written = false;
+  TK_TRY(step_device(dev.data(), n, kind, hp, step, max_norm, scale_dev, &written, s));
+  for (size_t i = 0; i < n; ++i) {
+    const tk_leaf& L = leaves[i];
+    if (L.n == 0) continue;
+    TK_CUDA_TRY(cudaMemcpyAsync(L.p, dev[i].p, L.n * esize(L.p_dtype), cudaMemcpyDeviceToHost, s));
+    TK_CUDA_TRY(cudaMemcpyAsync(L.m, dev[i].m, L.n * 4, cudaMemcpyDeviceToHost, s));
+    if (kind == TK_ADAMW)
+      TK_CUDA_TRY(cudaMemcpyAsync(L.v, dev[i].v, L.n * 4, cudaMemcpyDeviceToHost, s));
+  }
+  float scale = 1.0f;
+  if (written) TK_CUDA_TRY(cudaMemcpyAsync(&scale, scale_dev, 4, cudaMemcpyDeviceToHost, s));
+  TK_CUDA_TRY(cudaStreamSynchronize(s));
+  if (clip_scale_out) *clip_scale_out = scale;
+  return TK_OK;
+}
+
+static int step_entry(const tk_leaf* leaves, size_t n, int kind, const tk_hparams* hp,
+                      uint64_t step, float max_norm, float* clip_scale_out, float* scale_dev,
+                      bool sync, cudaStream_t s) {
+  if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
+  Residency where;
+  TK_TRY(validate_leaves(leaves, n, kind, &where));
+  if (where == Residency::kHost) {
+    if (!sync)
+      return set_error(TK_ERR_INVALID, "the asynchronous step takes device buffers only");
+    return step_host(leaves, n, kind, *hp, step, max_norm, clip_scale_out, s);
+  }
+  if (!sync) {
+    bool written = false;
+    TK_TRY(step_device(leaves, n, kind, *hp, step, max_norm, scale_dev, &written, s));
+    if (scale_dev != nullptr && !written) {
+      const float one = 1.0f;
+      TK_CUDA_TRY(cudaMemcpyAsync(scale_dev, &one, 4, cudaMemcpyHostToDevice, s));
+    }
+    return TK_OK;
+  }
+  Scratch sc;
+  float* dscale = nullptr;
+  if (clip_scale_out != nullptr && max_norm > 0.0f) {
+    TK_TRY(sc.alloc(64, s));
+    dscale = static_cast<float*>(sc.get());
+  }
+  bool written = false;
+  TK_TRY(step_device(leaves, n, kind, *hp, step, max_norm, dscale, &written, s));
+  float scale = 1.0f;
+  if (written) TK_CUDA_TRY(cudaMemcpyAsync(&scale, dscale, 4, cudaMemcpyDeviceToHost, s));
+  TK_CUDA_TRY(cudaStreamSynchronize(s));
+  if (clip_scale_out) *clip_scale_out = scale;
+  return TK_OK;
+}
+
+}  // namespace tk
+
+using namespace tk;
+
+extern "C" {
+
+const char* tk_last_error(void) { return g_last_error.c_str(); }
+
+int tk_abi_version(void) { return TK_ABI_VERSION; }
+
+int tk_verify(const tk_pipeline* pipeline) {
+  g_last_error.clear();
+  return verify_pipeline(pipeline);
+}
+
+int tk_layout_from_shapes(const uint64_t* num_elements, size_t n_leaves, uint64_t* byte_offsets,
+                          uint64_t* total_bytes) {
+  g_last_error.clear();
+  if (n_leaves > 0 && (num_elements == nullptr || byte_offsets == nullptr))
+    return set_error(TK_ERR_INVALID, "null shape or offset array");
+  if (total_bytes == nullptr) return set_error(TK_ERR_INVALID, "total_bytes is NULL");
+  // arena.rs:34-57: pad each offset up to a 64-byte cache line
+  uint64_t cur = 0;
+  for (size_t i = 0; i < n_leaves; ++i) {
+    const uint64_t rem = cur % 64;
+    if (rem) cur += 64 - rem;
+    byte_offsets[i] = cur;
+    cur += num_elements[i] * 4;
+  }
+  *total_bytes = cur;
+  return TK_OK;
+}
+
+int tk_step_two_tier(const tk_pipeline* pipeline, const tk_leaf* leaves, size_t n_leaves,
+                     int32_t kind, const tk_hparams* hp, uint64_t step, float* clip_scale_out,
+                     void* stream) {
+  g_last_error.clear();
+  TK_TRY(verify_pipeline(pipeline));
+  return step_entry(leaves, n_leaves, kind, hp, step, pipeline->max_norm, clip_scale_out,
+                    nullptr, true, static_cast<cudaStream_t>(stream));
+}
+
+// The pipeline step_fast_buffers builds (crates/tikun-py/src/lib.rs:183-192).
+static const tk_schedule_node kFastNodes[3] = {
+    {"load_g", TK_ROLE_LOAD, 64, 4, 8, 2},
+    {"fma_opt", TK_ROLE_COMPUTE, 64, 4, 8, 2},
+    {"store_p", TK_ROLE_STORE, 64, 4, 8, 2},
+};
+
+int tk_step_buffers(const tk_leaf* leaves, size_t n_leaves, int32_t kind, const tk_hparams* hp,
+                    uint64_t step, float max_norm, float* clip_scale_out, void* stream) {
+  const tk_pipeline pl = {kFastNodes, 3, max_norm > 0.0f ? max_norm : 0.0f};
+  return tk_step_two_tier(&pl, leaves, n_leaves, kind, hp, step, clip_scale_out, stream);
+}
+
+int tk_step_buffers_async(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                          const tk_hparams* hp, uint64_t step, float max_norm,
+                          float* clip_scale_dev, void* stream) {
+  g_last_error.clear();
+  const tk_pipeline pl = {kFastNodes, 3, max_norm};
+  TK_TRY(verify_pipeline(&pl));
+  return step_entry(leaves, n_leaves, kind, hp, step, max_norm > 0.0f ? max_norm : 0.0f,
+                    nullptr, clip_scale_dev, false, static_cast<cudaStream_t>(stream));
+}
+
+int tk_set_update_events(void* start_event, void* stop_event) {
+  g_last_error.clear();
+  if ((start_event == nullptr) != (stop_event == nullptr))
+    return set_error(TK_ERR_INVALID, "set both events or neither");
+  g_update_start = static_cast<cudaEvent_t>(start_event);
+  g_update_stop = static_cast<cudaEvent_t>(stop_event);
+  return TK_OK;
+}
+
+int tk_grad_sumsq(const tk_leaf* leaves, size_t n_leaves, double* sumsq_dev, void* stream) {
+  g_last_error.clear();
+  if (sumsq_dev == nullptr) return set_error(TK_ERR_INVALID, "sumsq_dev is NULL");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  Residency where;
+  TK_TRY(validate_leaves(leaves, n_leaves, TK_SGD, &where));
+  if (where == Residency::kHost) return set_error(TK_ERR_INVALID, "tk_grad_sumsq takes device buffers");
+  Plan plan;
+  make_plan(leaves, n_leaves, TK_SGD, &plan);
+  if (plan.tables.empty()) {
+    TK_CUDA_TRY(cudaMemsetAsync(sumsq_dev, 0, sizeof(double), s));
+    return TK_OK;
+  }
+  Scratch sc;
+  double* partials = nullptr;
+  int n_partials = 0;
+  TK_TRY(launch_norm(plan, &sc, &partials, &n_partials, s));
+  return launch_sumsq_reduce(partials, n_partials, sumsq_dev, s);
+}
+
+int tk_clip_scale(const double* sumsq_dev, float max_norm, float* scale_dev, void* stream) {
+  g_last_error.clear();
+  if (sumsq_dev == nullptr || scale_dev == nullptr)
+    return set_error(TK_ERR_INVALID, "null sumsq or scale pointer");
+  return launch_clip_scale(sumsq_dev, 1, max_norm, scale_dev, static_cast<cudaStream_t>(stream));
+}
+
+int tk_apply_pointwise(const tk_leaf* leaves, size_t n_leaves, int32_t kind, const tk_hparams* hp,
+                       uint64_t step, const float* scale_dev, void* stream) {
+  g_last_error.clear();
+  if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
+  Residency where;
+  TK_TRY(validate_leaves(leaves, n_leaves, kind, &where));
+  if (where == Residency::kHost)
+    return set_error(TK_ERR_INVALID, "tk_apply_pointwise takes device buffers");
+  Plan plan;
+  make_plan(leaves, n_leaves, kind, &plan);
+  const PointwiseConsts c = make_consts(kind, *hp, step);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (size_t i = 0; i < plan.tables.size(); ++i)
+    TK_TRY(launch_pointwise(plan.tables[i], kind, plan.pdt[i], plan.gdt[i], c, nullptr, 0, 0.f,
+                            scale_dev, nullptr, s));
+  return TK_OK;
+}
+
+}  // extern "C"

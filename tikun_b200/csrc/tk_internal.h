@@ -1,0 +1,91 @@
+// Internal declarations shared by the C-ABI layer (tk_api.cpp) and the CUDA
+// kernels.  Nothing here is part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "../../include/tikun_cuda.h"
+
+namespace tk {
+
+// ---------------------------------------------------------------- errors
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+
+#define TK_CUDA_TRY(expr)                                     \
+  do {                                                        \
+    cudaError_t _e = (expr);                                  \
+    if (_e != cudaSuccess) return ::tk::cuda_error(_e, #expr); \
+  } while (0)
+
+#define TK_TRY(expr)               \
+  do {                             \
+    int _s = (expr);               \
+    if (_s != TK_OK) return _s;    \
+  } while (0)
+
+// ---------------------------------------------------------------- scratch
+// Stream-ordered device scratch from a per-device memory pool that keeps its
+// memory cached between calls.  Freed (stream-ordered) by the destructor.
+class Scratch {
+ public:
+  Scratch() = default;
+  ~Scratch();
+  Scratch(const Scratch&) = delete;
+  Scratch& operator=(const Scratch&) = delete;
+  int alloc(size_t bytes, cudaStream_t s);
+  void* get() const { return ptr_; }
+
+ private:
+  void* ptr_ = nullptr;
+  cudaStream_t stream_ = nullptr;
+};
+
+int sm_count(int* out);
+
+// ---------------------------------------------------------------- pointwise
+constexpr int kMaxLeavesPerLaunch = 224;
+
+struct LeafDesc {
+  void* p;
+  const void* g;
+  float* m;
+  float* v;
+  uint64_t n;        // elements
+  uint64_t q_begin;  // first quad (4-element group) of this leaf in the launch
+  uint32_t vec_ok;   // p, g, m, v aligned for vector access of a whole quad
+  uint32_t reserved;
+};
+
+struct LeafTable {
+  int32_t n_leaves;
+  int32_t reserved;
+  uint64_t total_quads;
+  LeafDesc leaf[kMaxLeavesPerLaunch];
+};
+
+struct PointwiseConsts {
+  float lr, b1, b2, eps, decay;
+  float omb1, omb2;  // 1 - b1, 1 - b2 in f32
+  float bc1, bc2;    // AdamW bias corrections
+};
+
+// Launchers (tk_pointwise.cu).  Tables hold leaves of one (p, g) dtype pair.
+int launch_sumsq_partials(const LeafTable& t, int g_dtype, double* partials, int n_blocks,
+                          cudaStream_t s);
+int sumsq_blocks_for(uint64_t total_quads);
+int launch_sumsq_reduce(const double* partials, int n_partials, double* total,
+                        cudaStream_t s);
+int launch_clip_scale(const double* sumsq, int n_partials, float max_norm, float* scale_out,
+                      cudaStream_t s);
+// Tier 2.  If partials != nullptr every CTA folds partials[0..n_partials) into
+// the clip scale itself (same order in every CTA); else scale_dev (or 1.0).
+int launch_pointwise(const LeafTable& t, int kind, int p_dtype, int g_dtype,
+                     const PointwiseConsts& c, const double* partials, int n_partials,
+                     float max_norm, const float* scale_dev, float* scale_out,
+                     cudaStream_t s);
+
+}  // namespace tk

@@ -1,0 +1,387 @@
+// Tier 1 (global L2 norm -> clip scale) and Tier 2 (AdamW / Lion / SGD) for
+// sm_100a.  Memory-bound streaming kernels over a table of leaves.
+//
+// Work split: the leaves of one launch form one index space of "quads"
+// (4-element groups, a leaf's last quad may be partial).  Every CTA takes an
+// equal contiguous slice of that space, so the grid is balanced whatever the
+// leaf sizes (a 38.6M-element embedding next to 768-element LayerNorms), and
+// each CTA streams contiguous memory.  A quad is one 128-bit access per f32
+// array (64-bit for bf16) when the leaf's pointers are aligned for it.
+//
+// Arithmetic follows the reference's x86 scalar code element by element
+// (crates/tikun-cpu/src/lib.rs:258-270, :347-358, :419-427): every multiply,
+// add, divide and square root is a separately rounded IEEE f32 operation
+// (__fmul_rn & co. are never contracted into FMAs), denormals are kept, so the
+// results are bit-identical to tikun-cpu's.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "tk_internal.h"
+
+namespace tk {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 2;
+
+// ------------------------------------------------------------------ dtypes
+__device__ __forceinline__ float bf16_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+__device__ __forceinline__ uint32_t f32_to_bf16(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return ((u >> 16) | 0x40u) & 0xffffu;  // quiet NaN
+  u += 0x7fffu + ((u >> 16) & 1u);                                              // nearest even
+  return u >> 16;
+}
+
+template <int DT>
+__device__ __forceinline__ void load_quad(const void* base, uint64_t e, float (&x)[4]) {
+  if constexpr (DT == TK_F32) {
+    const float4 q = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + e);
+    x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
+  } else {
+    const uint2 q = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + e);
+    x[0] = bf16_to_f32(q.x & 0xffffu); x[1] = bf16_to_f32(q.x >> 16);
+    x[2] = bf16_to_f32(q.y & 0xffffu); x[3] = bf16_to_f32(q.y >> 16);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ void store_quad(void* base, uint64_t e, const float (&x)[4]) {
+  if constexpr (DT == TK_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(base) + e) = make_float4(x[0], x[1], x[2], x[3]);
+  } else {
+    uint2 q;
+    q.x = f32_to_bf16(x[0]) | (f32_to_bf16(x[1]) << 16);
+    q.y = f32_to_bf16(x[2]) | (f32_to_bf16(x[3]) << 16);
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(base) + e) = q;
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ float load1(const void* base, uint64_t e) {
+  if constexpr (DT == TK_F32) return static_cast<const float*>(base)[e];
+  else return bf16_to_f32(static_cast<const uint16_t*>(base)[e]);
+}
+
+template <int DT>
+__device__ __forceinline__ void store1(void* base, uint64_t e, float x) {
+  if constexpr (DT == TK_F32) static_cast<float*>(base)[e] = x;
+  else static_cast<uint16_t*>(base)[e] = static_cast<uint16_t>(f32_to_bf16(x));
+}
+
+// ------------------------------------------------------------------ update rules
+// AdamW, crates/tikun-cpu/src/lib.rs:258-270 (g already scaled by the caller).
+__device__ __forceinline__ void adamw(float& p, float g, float& m, float& v,
+                                      const PointwiseConsts& k) {
+  m = __fadd_rn(__fmul_rn(k.b1, m), __fmul_rn(k.omb1, g));
+  v = __fadd_rn(__fmul_rn(k.b2, v), __fmul_rn(__fmul_rn(k.omb2, g), g));
+  const float m_hat = __fdiv_rn(m, k.bc1);
+  const float m_hat2 = __fdiv_rn(v, k.bc2);
+  const float step_update =
+      __fadd_rn(__fdiv_rn(m_hat, __fadd_rn(__fsqrt_rn(m_hat2), k.eps)), __fmul_rn(k.decay, p));
+  p = __fsub_rn(p, __fmul_rn(k.lr, step_update));
+}
+
+// Lion, lib.rs:347-358.
+__device__ __forceinline__ void lion(float& p, float g, float& m, const PointwiseConsts& k) {
+  const float c = __fadd_rn(__fmul_rn(k.b1, m), __fmul_rn(k.omb1, g));
+  const float sign_c = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : 0.0f);
+  p = __fsub_rn(p, __fmul_rn(k.lr, __fadd_rn(sign_c, __fmul_rn(k.decay, p))));
+  m = __fadd_rn(__fmul_rn(k.b2, m), __fmul_rn(k.omb2, g));
+}
+
+// SGD with momentum, lib.rs:419-427 (momentum carried in b1).
+__device__ __forceinline__ void sgd(float& p, float g, float& m, const PointwiseConsts& k) {
+  m = __fadd_rn(__fmul_rn(k.b1, m), g);
+  const float update = __fadd_rn(m, __fmul_rn(k.decay, p));
+  p = __fsub_rn(p, __fmul_rn(k.lr, update));
+}
+
+template <int KIND>
+__device__ __forceinline__ void apply(float& p, float g, float& m, float& v,
+                                      const PointwiseConsts& k) {
+  if constexpr (KIND == TK_ADAMW) adamw(p, g, m, v, k);
+  else if constexpr (KIND == TK_LION) lion(p, g, m, k);
+  else sgd(p, g, m, k);
+}
+
+// ------------------------------------------------------------------ reductions
+// Deterministic block sum: fixed shuffle tree per warp, then warp 0 adds the
+// warp totals in warp order.  Result valid in thread 0.
+__device__ __forceinline__ double block_sum(double x) {
+  __shared__ double warp_tot[kThreads / 32];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) x += __shfl_down_sync(0xffffffffu, x, off);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  if (lane == 0) warp_tot[wid] = x;
+  __syncthreads();
+  double t = 0.0;
+  if (wid == 0) {
+    t = lane < (kThreads / 32) ? warp_tot[lane] : 0.0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) t += __shfl_down_sync(0xffffffffu, t, off);
+  }
+  __syncthreads();
+  return t;
+}
+
+// lib.rs:117-122: norm rounded to f32, scale only if it exceeds max_norm > 0.
+__device__ __forceinline__ float clip_from_sumsq(double total, float max_norm) {
+  const float norm = __double2float_rn(sqrt(total));
+  if (norm > max_norm && max_norm > 0.0f) return __fdiv_rn(max_norm, __fadd_rn(norm, 1e-6f));
+  return 1.0f;
+}
+
+__device__ __forceinline__ int find_leaf(const LeafTable& t, uint64_t q) {
+  int lo = 0, hi = t.n_leaves - 1;  // last leaf with q_begin <= q
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (t.leaf[mid].q_begin <= q) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ uint64_t leaf_quads(const LeafDesc& L) { return (L.n + 3) >> 2; }
+
+// ------------------------------------------------------------------ Tier 1
+template <int GDT>
+__global__ void __launch_bounds__(kThreads)
+sumsq_partials_kernel(const __grid_constant__ LeafTable t, double* __restrict__ partials) {
+  const uint64_t total = t.total_quads;
+  const uint64_t q0 = total * blockIdx.x / gridDim.x;
+  const uint64_t q1 = total * (blockIdx.x + 1) / gridDim.x;
+  double acc = 0.0;
+  if (q0 < q1) {
+    int li = find_leaf(t, q0);
+    uint64_t q = q0;
+    while (q < q1) {
+      const LeafDesc& L = t.leaf[li];
+      const uint64_t seg_end = min(q1, L.q_begin + leaf_quads(L));
+      const uint64_t a = q - L.q_begin, b = seg_end - L.q_begin;
+      for (uint64_t lq = a + threadIdx.x; lq < b; lq += kThreads) {
+        const uint64_t e = lq * 4;
+        if (L.vec_ok && e + 4 <= L.n) {
+          float x[4];
+          load_quad<GDT>(L.g, e, x);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc = fma((double)x[j], (double)x[j], acc);
+        } else {
+          for (uint64_t j = e; j < min(e + 4, L.n); ++j) {
+            const double x = load1<GDT>(L.g, j);
+            acc = fma(x, x, acc);
+          }
+        }
+      }
+      q = seg_end;
+      ++li;
+    }
+  }
+  // x*x of an f32 value is exact in f64, so fma == multiply-then-add here.
+  const double s = block_sum(acc);
+  if (threadIdx.x == 0) partials[blockIdx.x] = s;
+}
+
+__global__ void __launch_bounds__(kThreads)
+sumsq_reduce_kernel(const double* __restrict__ partials, int n, double* __restrict__ total) {
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < n; i += kThreads) acc += partials[i];
+  const double s = block_sum(acc);
+  if (threadIdx.x == 0) *total = s;
+}
+
+__global__ void __launch_bounds__(kThreads)
+clip_scale_kernel(const double* __restrict__ partials, int n, float max_norm,
+                  float* __restrict__ scale_out) {
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < n; i += kThreads) acc += partials[i];
+  const double s = block_sum(acc);
+  if (threadIdx.x == 0) *scale_out = clip_from_sumsq(s, max_norm);
+}
+
+// ------------------------------------------------------------------ Tier 2
+// SCALE: 0 = no clipping, 1 = fold partials in every CTA, 2 = read scale_dev.
+template <int KIND, int PDT, int GDT, int SCALE>
+__global__ void __launch_bounds__(kThreads)
+pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
+                 const double* __restrict__ partials, int n_partials, float max_norm,
+                 const float* __restrict__ scale_dev, float* __restrict__ scale_out) {
+  float scale = 1.0f;
+  if constexpr (SCALE == 1) {
+    __shared__ float s_scale;
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < n_partials; i += kThreads) acc += partials[i];
+    const double s = block_sum(acc);
+    if (threadIdx.x == 0) {
+      const float sc = clip_from_sumsq(s, max_norm);
+      s_scale = sc;
+      if (blockIdx.x == 0 && scale_out != nullptr) *scale_out = sc;
+    }
+    __syncthreads();
+    scale = s_scale;
+  } else if constexpr (SCALE == 2) {
+    scale = *scale_dev;
+  }
+
+  const uint64_t total = t.total_quads;
+  const uint64_t q0 = total * blockIdx.x / gridDim.x;
+  const uint64_t q1 = total * (blockIdx.x + 1) / gridDim.x;
+  if (q0 >= q1) return;
+  int li = find_leaf(t, q0);
+  uint64_t q = q0;
+  while (q < q1) {
+    const LeafDesc& L = t.leaf[li];
+    const uint64_t nq = leaf_quads(L);
+    const uint64_t seg_end = min(q1, L.q_begin + nq);
+    const uint64_t a = q - L.q_begin, b = seg_end - L.q_begin;
+    // quads [a, full_end) are whole and vector-accessible; the rest go scalar
+    const uint64_t full_end = L.vec_ok ? min(b, L.n >> 2) : a;
+    for (uint64_t lq = a + threadIdx.x; lq < full_end; lq += kThreads * kUnroll) {
+      float P[kUnroll][4], G[kUnroll][4], M[kUnroll][4], V[kUnroll][4];
+      bool act[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const uint64_t qq = lq + (uint64_t)u * kThreads;
+        act[u] = qq < full_end;
+        if (act[u]) {
+          const uint64_t e = qq * 4;
+          load_quad<GDT>(L.g, e, G[u]);
+          load_quad<PDT>(L.p, e, P[u]);
+          load_quad<TK_F32>(L.m, e, M[u]);
+          if constexpr (KIND == TK_ADAMW) load_quad<TK_F32>(L.v, e, V[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        if (!act[u]) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float g = G[u][j];
+          if constexpr (SCALE != 0) g = __fmul_rn(g, scale);
+          apply<KIND>(P[u][j], g, M[u][j], V[u][j], k);
+        }
+        const uint64_t e = (lq + (uint64_t)u * kThreads) * 4;
+        store_quad<PDT>(L.p, e, P[u]);
+        store_quad<TK_F32>(L.m, e, M[u]);
+        if constexpr (KIND == TK_ADAMW) store_quad<TK_F32>(L.v, e, V[u]);
+      }
+    }
+    // ragged tail or unaligned leaf: element by element
+    for (uint64_t lq = max(a, full_end) + threadIdx.x; lq < b; lq += kThreads) {
+      for (uint64_t e = lq * 4; e < min(lq * 4 + 4, L.n); ++e) {
+        float p = load1<PDT>(L.p, e);
+        float g = load1<GDT>(L.g, e);
+        if constexpr (SCALE != 0) g = __fmul_rn(g, scale);
+        float m = L.m[e];
+        float v = 0.0f;
+        if constexpr (KIND == TK_ADAMW) v = L.v[e];
+        apply<KIND>(p, g, m, v, k);
+        store1<PDT>(L.p, e, p);
+        L.m[e] = m;
+        if constexpr (KIND == TK_ADAMW) L.v[e] = v;
+      }
+    }
+    q = seg_end;
+    ++li;
+  }
+}
+
+template <int KIND, int PDT, int GDT, int SCALE>
+int occupancy_grid(uint64_t total_quads) {
+  static int cap = 0;
+  if (cap == 0) {
+    int sms = 0, per_sm = 0;
+    if (sm_count(&sms) != TK_OK) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, pointwise_kernel<KIND, PDT, GDT, SCALE>, kThreads, 0) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+    cap = sms * per_sm;
+  }
+  const uint64_t want = (total_quads + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+  return (int)(want < (uint64_t)cap ? (want ? want : 1) : cap);
+}
+
+template <int KIND, int PDT, int GDT, int SCALE>
+int launch_t(const LeafTable& t, const PointwiseConsts& c, const double* partials,
+             int n_partials, float max_norm, const float* scale_dev, float* scale_out,
+             cudaStream_t s) {
+  const int grid = occupancy_grid<KIND, PDT, GDT, SCALE>(t.total_quads);
+  if (grid <= 0) return set_error(TK_ERR_CUDA, "could not size the pointwise grid");
+  pointwise_kernel<KIND, PDT, GDT, SCALE><<<grid, kThreads, 0, s>>>(
+      t, c, partials, n_partials, max_norm, scale_dev, scale_out);
+  TK_CUDA_TRY(cudaGetLastError());
+  return TK_OK;
+}
+
+template <int KIND, int PDT, int GDT>
+int launch_scale(const LeafTable& t, const PointwiseConsts& c, const double* partials,
+                 int n_partials, float max_norm, const float* scale_dev, float* scale_out,
+                 cudaStream_t s) {
+  if (partials) return launch_t<KIND, PDT, GDT, 1>(t, c, partials, n_partials, max_norm, nullptr, scale_out, s);
+  if (scale_dev) return launch_t<KIND, PDT, GDT, 2>(t, c, nullptr, 0, 0.f, scale_dev, nullptr, s);
+  return launch_t<KIND, PDT, GDT, 0>(t, c, nullptr, 0, 0.f, nullptr, nullptr, s);
+}
+
+template <int KIND>
+int launch_kind(const LeafTable& t, int pdt, int gdt, const PointwiseConsts& c,
+                const double* partials, int n_partials, float max_norm, const float* scale_dev,
+                float* scale_out, cudaStream_t s) {
+  if (pdt == TK_F32 && gdt == TK_F32) return launch_scale<KIND, TK_F32, TK_F32>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+  if (pdt == TK_F32 && gdt == TK_BF16) return launch_scale<KIND, TK_F32, TK_BF16>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+  if (pdt == TK_BF16 && gdt == TK_F32) return launch_scale<KIND, TK_BF16, TK_F32>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+  if (pdt == TK_BF16 && gdt == TK_BF16) return launch_scale<KIND, TK_BF16, TK_BF16>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+  return set_error(TK_ERR_INVALID, "unsupported dtype pair p=%d g=%d", pdt, gdt);
+}
+
+}  // namespace
+
+int sumsq_blocks_for(uint64_t total_quads) {
+  static int cap = 0;
+  if (cap == 0) {
+    int sms = 0, per_sm = 0;
+    if (sm_count(&sms) != TK_OK) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sumsq_partials_kernel<TK_F32>,
+                                                      kThreads, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    cap = sms * per_sm;
+  }
+  const uint64_t want = (total_quads + kThreads - 1) / kThreads;
+  return (int)(want < (uint64_t)cap ? (want ? want : 1) : cap);
+}
+
+int launch_sumsq_partials(const LeafTable& t, int g_dtype, double* partials, int n_blocks,
+                          cudaStream_t s) {
+  if (g_dtype == TK_F32) sumsq_partials_kernel<TK_F32><<<n_blocks, kThreads, 0, s>>>(t, partials);
+  else if (g_dtype == TK_BF16) sumsq_partials_kernel<TK_BF16><<<n_blocks, kThreads, 0, s>>>(t, partials);
+  else return set_error(TK_ERR_INVALID, "unsupported gradient dtype %d", g_dtype);
+  TK_CUDA_TRY(cudaGetLastError());
+  return TK_OK;
+}
+
+int launch_sumsq_reduce(const double* partials, int n_partials, double* total, cudaStream_t s) {
+  sumsq_reduce_kernel<<<1, kThreads, 0, s>>>(partials, n_partials, total);
+  TK_CUDA_TRY(cudaGetLastError());
+  return TK_OK;
+}
+
+int launch_clip_scale(const double* sumsq, int n_partials, float max_norm, float* scale_out,
+                      cudaStream_t s) {
+  clip_scale_kernel<<<1, kThreads, 0, s>>>(sumsq, n_partials, max_norm, scale_out);
+  TK_CUDA_TRY(cudaGetLastError());
+  return TK_OK;
+}
+
+int launch_pointwise(const LeafTable& t, int kind, int p_dtype, int g_dtype,
+                     const PointwiseConsts& c, const double* partials, int n_partials,
+                     float max_norm, const float* scale_dev, float* scale_out, cudaStream_t s) {
+  switch (kind) {
+    case TK_ADAMW: return launch_kind<TK_ADAMW>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+    case TK_LION: return launch_kind<TK_LION>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+    case TK_SGD: return launch_kind<TK_SGD>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+    default: return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
+  }
+}
+
+}  // namespace tk

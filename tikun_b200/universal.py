@@ -1,0 +1,198 @@
+"""Framework-agnostic pointwise optimizer front-end on the B200 engine.
+
+Mirrors the reference's ``UniversalOptimizer`` (python/tikun/universal.py:87-223):
+same constructor arguments, PyTree flattening (dict values in insertion order,
+lists, tuples, iterables, ``(ptr, len)`` pairs), per-parameter first/second
+moment state keyed by the parameter's address, a step counter incremented at
+the top of ``step()``, and the ``in_backward`` mode that steps each leaf from a
+post-accumulate-grad hook.
+
+Differences, all on the device side:
+* CUDA tensors keep their moment state in device memory (the reference holds
+  it in NumPy) and step without a host sync; the clip scale of the last step
+  stays on the device in ``clip_scale``.
+* bf16 parameters and gradients are accepted (updated in f32, rounded to
+  nearest even on store); moments are f32.
+* NumPy arrays and raw host ``(ptr, len)`` pairs step synchronously through the
+  same C ABI, staged through device memory.
+"""
+from __future__ import annotations
+
+from typing import Any
+
+import numpy as np
+
+from . import _native
+
+
+def _extract_pointer_and_len(tensor) -> tuple[int, int]:
+    """universal.py:48-61."""
+    if hasattr(tensor, "data_ptr") and hasattr(tensor, "numel"):
+        return tensor.data_ptr(), tensor.numel()
+    if isinstance(tensor, np.ndarray):
+        return tensor.ctypes.data, tensor.size
+    if hasattr(tensor, "__array__"):
+        arr = np.asarray(tensor)
+        return arr.ctypes.data, arr.size
+    if isinstance(tensor, (tuple, list)) and len(tensor) == 2 and isinstance(tensor[0], int):
+        return int(tensor[0]), int(tensor[1])
+    raise TypeError(f"Unsupported tensor type: {type(tensor)}. Must be PyTorch, JAX, NumPy, or (ptr, len).")
+
+
+def _flatten_pytree(container) -> list:
+    """universal.py:63-85."""
+    if isinstance(container, dict):
+        items = []
+        for v in container.values():
+            items.extend(_flatten_pytree(v))
+        return items
+    if isinstance(container, (list, tuple)):
+        if len(container) == 2 and isinstance(container[0], int) and isinstance(container[1], int):
+            return [container]
+        items = []
+        for item in container:
+            items.extend(_flatten_pytree(item))
+        return items
+    if hasattr(container, "__iter__") and not hasattr(container, "data_ptr") and not isinstance(
+            container, (str, bytes, np.ndarray)):
+        items = []
+        for item in container:
+            items.extend(_flatten_pytree(item))
+        return items
+    return [container]
+
+
+def _tk_dtype(t) -> int:
+    dt = getattr(t, "dtype", None)
+    if dt is None:
+        return _native.TK_F32  # raw (ptr, len): f32 as in the reference
+    name = str(dt)
+    if name in ("torch.float32", "float32"):
+        return _native.TK_F32
+    if name in ("torch.bfloat16", "bfloat16"):
+        return _native.TK_BF16
+    raise TypeError(f"tikun_b200 leaves are float32 or bfloat16, got {dt}")
+
+
+def _is_cuda(t) -> bool:
+    return bool(getattr(t, "is_cuda", False))
+
+
+class UniversalOptimizer:
+    """See the module docstring; arguments as python/tikun/universal.py:93-104."""
+
+    def __init__(self, params, algorithm: str = "adamw", lr: float = 1e-3, beta1: float = 0.9,
+                 beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.01,
+                 max_norm: float = 0.0, in_backward: bool = False):
+        self.params = _flatten_pytree(params)
+        self.algorithm = algorithm.lower()
+        self.lr = lr
+        self.beta1 = beta1
+        self.beta2 = beta2
+        self.eps = eps
+        self.weight_decay = weight_decay
+        self.max_norm = max_norm
+        self.step_count = 0
+        self.in_backward = in_backward
+        self.m1_state: dict[int, Any] = {}
+        self.m2_state: dict[int, Any] = {}
+        self.clip_scale = None  # device f32 tensor (CUDA params) or float (host params)
+        if self.in_backward:
+            self._hooks = []
+            for p in self.params:
+                if hasattr(p, "register_post_accumulate_grad_hook"):
+                    self._hooks.append(p.register_post_accumulate_grad_hook(
+                        self._make_in_backward_hook(p)))
+
+    # -- state ---------------------------------------------------------------
+    def _state_for(self, p, p_ptr: int, length: int):
+        if p_ptr not in self.m1_state:
+            if _is_cuda(p):
+                import torch
+
+                self.m1_state[p_ptr] = torch.zeros(length, dtype=torch.float32, device=p.device)
+                self.m2_state[p_ptr] = torch.zeros(length, dtype=torch.float32, device=p.device)
+            else:
+                self.m1_state[p_ptr] = np.zeros(length, dtype=np.float32)
+                self.m2_state[p_ptr] = np.zeros(length, dtype=np.float32)
+        m1, m2 = self.m1_state[p_ptr], self.m2_state[p_ptr]
+        return _extract_pointer_and_len(m1)[0], _extract_pointer_and_len(m2)[0]
+
+    def _call(self, p_ptrs, g_ptrs, m1_ptrs, m2_ptrs, lengths, p_dt, g_dt, step, on_device,
+              device=None):
+        if on_device:
+            import torch
+
+            if self.clip_scale is None or self.clip_scale.device != device:
+                self.clip_scale = torch.ones((), dtype=torch.float32, device=device)
+            with torch.cuda.device(device):
+                _native.step_fast_buffers_async(
+                    p_ptrs, g_ptrs, m1_ptrs, m2_ptrs, lengths, self.max_norm, self.algorithm,
+                    step, self.lr, self.beta1, self.beta2, self.eps, self.weight_decay,
+                    clip_scale_ptr=self.clip_scale.data_ptr(), p_dtypes=p_dt, g_dtypes=g_dt)
+        else:
+            self.clip_scale = _native.step_fast_buffers(
+                p_ptrs, g_ptrs, m1_ptrs, m2_ptrs, lengths, self.max_norm, self.algorithm, step,
+                self.lr, self.beta1, self.beta2, self.eps, self.weight_decay, p_dtypes=p_dt,
+                g_dtypes=g_dt, stream=0)
+
+    # -- in-backward ---------------------------------------------------------
+    def _make_in_backward_hook(self, p):
+        def _hook(param):
+            if param.grad is None:
+                return
+            self._step_single_tensor(param)
+            param.grad = None
+
+        return _hook
+
+    def _step_single_tensor(self, p):
+        """universal.py:138-163: one leaf, with step max(1, step_count) —
+        the count is read before step() increments it, so the first two
+        backward passes both use step 1, exactly as the reference does."""
+        p_ptr, length = _extract_pointer_and_len(p)
+        g_ptr, _ = _extract_pointer_and_len(p.grad)
+        m1, m2 = self._state_for(p, p_ptr, length)
+        self._call([p_ptr], [g_ptr], [m1], [m2], [length], [_tk_dtype(p)], [_tk_dtype(p.grad)],
+                   max(1, self.step_count), _is_cuda(p), getattr(p, "device", None))
+
+    # -- step ----------------------------------------------------------------
+    def step(self, grads=None):
+        """universal.py:165-218."""
+        self.step_count += 1
+        if self.in_backward:
+            return
+        p_ptrs, g_ptrs, m1_ptrs, m2_ptrs, lengths, p_dt, g_dt = [], [], [], [], [], [], []
+        flat_grads = _flatten_pytree(grads) if grads is not None else None
+        cuda_flags = []
+        device = None
+        for i, p in enumerate(self.params):
+            p_ptr, length = _extract_pointer_and_len(p)
+            if flat_grads is not None:
+                g = flat_grads[i]
+            elif hasattr(p, "grad") and p.grad is not None:
+                g = p.grad
+            else:
+                continue
+            g_ptr, _ = _extract_pointer_and_len(g)
+            m1, m2 = self._state_for(p, p_ptr, length)
+            p_ptrs.append(p_ptr)
+            g_ptrs.append(g_ptr)
+            m1_ptrs.append(m1)
+            m2_ptrs.append(m2)
+            lengths.append(length)
+            p_dt.append(_tk_dtype(p))
+            g_dt.append(_tk_dtype(g))
+            cuda_flags.append(_is_cuda(p))
+            if _is_cuda(p):
+                device = p.device
+        if not p_ptrs:
+            return
+        on_device = all(cuda_flags)
+        self._call(p_ptrs, g_ptrs, m1_ptrs, m2_ptrs, lengths, p_dt, g_dt, self.step_count,
+                   on_device, device)
+
+    def zero_grad(self):
+        for p in self.params:
+            if hasattr(p, "grad") and p.grad is not None:
+                p.grad = None
