@@ -159,6 +159,64 @@ TK_API int tk_apply_pointwise(const tk_leaf* leaves, size_t n_leaves, int32_t ki
                        void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* Newton-Schulz (Muon)                                                    */
+/* ---------------------------------------------------------------------- */
+
+/* TensorEngine::polar_step (crates/tikun-cpu/src/tensor_engine.rs:12-77) in
+ * place on a row-major rows x cols matrix of dtype TK_F32 or TK_BF16:
+ * transpose when rows > cols, divide by max(||X||_F, 1e-7), then `steps`
+ * iterations of A = X X^T, B = b A + c A A, X = a X + B X with
+ * (a, b, c) = (3.4445, -4.7750, 2.0315).  The GEMMs run on the tensor cores
+ * with TK_NS_F16 or TK_NS_BF16 operands and f32 accumulation.  Device or host
+ * pointer; returns after the result is in place (newton_schulz_2d_ffi,
+ * crates/tikun-py/src/lib.rs:224-237). */
+TK_API int tk_newton_schulz_2d(void* matrix, int64_t rows, int64_t cols, int32_t steps,
+                               int32_t dtype, int32_t precision, void* stream);
+
+/* TensorEngine::polar_batched (tensor_engine.rs:79-96): num_heads contiguous
+ * head_dim_out x head_dim_in matrices (newton_schulz_3d_ffi,
+ * crates/tikun-py/src/lib.rs:239-254). */
+TK_API int tk_newton_schulz_3d(void* tensor, int64_t num_heads, int64_t head_dim_out,
+                               int64_t head_dim_in, int32_t steps, int32_t dtype,
+                               int32_t precision, void* stream);
+
+/* One Muon leaf: heads (0 or 1 for a matrix) contiguous rows x cols matrices
+ * of parameters p, gradients g and f32 momentum, all device memory. */
+typedef struct {
+  void* p;
+  const void* g;
+  float* momentum;
+  int64_t heads;
+  int64_t rows;
+  int64_t cols;
+  int32_t p_dtype; /* TK_F32 or TK_BF16 */
+  int32_t g_dtype; /* TK_F32 or TK_BF16 */
+} tk_muon_leaf;
+
+typedef struct {
+  double lr;         /* learning rate */
+  double momentum;   /* mu; (1 - mu) is formed in double, then rounded to f32 */
+  int32_t nesterov;  /* 1: Newton-Schulz of mu*buf + (1-mu)*g, 0: of buf */
+  int32_t ns_steps;  /* Newton-Schulz iterations (5) */
+  int32_t precision; /* TK_NS_F16 or TK_NS_BF16 */
+} tk_muon_hparams;
+
+/* The MuonND update of every 2-D (and head-batched) leaf
+ * (python/tikun/muon_nd.py:104-126, :129-160):
+ *   buf = mu*buf + (1-mu)*g;  U = mu*buf + (1-mu)*g (Nesterov) or buf;
+ *   U = NS(U);  p = p - lr*sqrt(max(1, rows/cols))*U
+ * fused into one prologue kernel pass, the tensor-core iteration, and the
+ * parameter update in the last GEMM's epilogue.  Same-shape matrices are
+ * batched.  Stream-ordered; does not wait.  A kernel that gives up on a
+ * bounded wait sets the device status word (tk_device_status). */
+TK_API int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves,
+                        const tk_muon_hparams* hp, void* stream);
+
+/* Waits for the device, then reads and clears its status word (0: no kernel
+ * reported a problem). */
+TK_API int tk_device_status(int* status_out);
+
+/* ---------------------------------------------------------------------- */
 /* measurement                                                             */
 /* ---------------------------------------------------------------------- */
 

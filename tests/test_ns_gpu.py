@@ -1,0 +1,231 @@
+"""Newton-Schulz and Muon on the tensor cores against the oracle.
+
+Bars (stated here, used below):
+* NS output: relative Frobenius error against the oracle's f32 Newton-Schulz
+  (tensor_engine.rs:12-77) <= 2e-2 with bf16 operands; with f16 operands
+  (the engine's default) the tests hold it to 5e-3.
+* Muon parameters after 10 steps: relative Frobenius error <= 1e-3 for f32
+  parameters (f16 operands).
+* The momentum buffer is element-wise f32 arithmetic: bit-identical.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import assert_bitexact, to_np
+from tikun_b200 import _native
+
+pytestmark = pytest.mark.gpu
+
+NS_TOL = {_native.TK_NS_F16: 5e-3, _native.TK_NS_BF16: 2e-2}
+PRECISIONS = [pytest.param(_native.TK_NS_F16, id="f16"), pytest.param(_native.TK_NS_BF16, id="bf16")]
+
+
+def relf(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def rup(x, a):
+    return (x + a - 1) // a * a
+
+
+# -- the GEMM kernel itself ------------------------------------------------
+@pytest.mark.parametrize("B,M,N,K", [(1, 128, 256, 64), (2, 256, 512, 192), (3, 300, 200, 100),
+                                     (1, 64, 64, 16), (2, 384, 768, 1024)])
+@pytest.mark.parametrize("fmt,dt", [(0, torch.float16), (1, torch.bfloat16)], ids=["f16", "bf16"])
+def test_gemm_tn_matches_torch(B, M, N, K, fmt, dt):
+    g = torch.Generator(device="cpu").manual_seed(B * 1000 + M + N + K)
+    ldp = ldq = rup(K, 64)
+    ldd = rup(N, 8)
+    P = torch.zeros(B, M, ldp, dtype=dt)
+    Q = torch.zeros(B, N, ldq, dtype=dt)
+    P[:, :, :K] = torch.randn(B, M, K, generator=g).to(dt)
+    Q[:, :, :K] = torch.randn(B, N, K, generator=g).to(dt)
+    P, Q = P.cuda(), Q.cuda()
+    D = torch.zeros(B, M, ldd, dtype=dt, device="cuda")
+    _native.check(_native.lib().tk_testing_gemm_tn(P.data_ptr(), Q.data_ptr(), D.data_ptr(), B, M,
+                                                   N, K, ldp, ldq, ldd, 1.0, fmt,
+                                                   torch.cuda.current_stream().cuda_stream))
+    ref = torch.bmm(P[:, :, :K].float(), Q[:, :, :K].float().transpose(1, 2))
+    got = D[:, :, :N].float()
+    err = (got - ref).norm() / ref.norm()
+    assert err.item() < (2e-3 if fmt == 0 else 1e-2), err.item()
+
+
+# -- Newton-Schulz ---------------------------------------------------------
+SHAPES = [(64, 96), (96, 64), (128, 128), (17, 45), (200, 32), (768, 768), (768, 3072),
+          (3072, 768), (1000, 1500)]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
+@pytest.mark.parametrize("prec", PRECISIONS)
+def test_ns_2d_matches_oracle(shape, prec):
+    r, c = shape
+    rng = np.random.default_rng(r * 7 + c)
+    x = (rng.standard_normal((r, c)) * 0.01).astype(np.float32)
+    ref = oracle.polar_step_np(x, 5)
+    t = torch.from_numpy(x.copy()).cuda()
+    _native.newton_schulz_2d_ffi(t.data_ptr(), r, c, 5, precision=prec)
+    assert relf(to_np(t), ref) <= NS_TOL[prec]
+
+
+@pytest.mark.parametrize("prec", PRECISIONS)
+def test_ns_matches_reference_torch_ns(golden_dir, prec):
+    """Against the reference's own torch Newton-Schulz (python/tikun/muon.py:10-32)."""
+    z = np.load(os.path.join(golden_dir, "ns_reference_torch.npz"))
+    for (r, c) in [(64, 96), (96, 64), (128, 128), (32, 200), (200, 32), (17, 45)]:
+        t = torch.from_numpy(z[f"ns_in_{r}x{c}"].copy()).cuda()
+        _native.newton_schulz_2d_ffi(t.data_ptr(), r, c, 5, precision=prec)
+        assert relf(to_np(t), z[f"ns_out_{r}x{c}"]) <= NS_TOL[prec], (r, c)
+
+
+def test_ns_orthogonality_known_answer(golden_dir):
+    """examples/test_muon_core.py:16-37: the relative Frobenius error of
+    X X^T - I on a seeded 768x768 randn matrix, as the reference computes it."""
+    z = np.load(os.path.join(golden_dir, "ns_reference_torch.npz"))
+    torch.manual_seed(42)
+    G = torch.randn(768, 768, dtype=torch.float32).cuda()
+    _native.newton_schulz_2d_ffi(G.data_ptr(), 768, 768, 5)
+    X = G.double()
+    err = ((X @ X.T - torch.eye(768, dtype=torch.float64, device="cuda")).norm() / (768 ** 0.5)).item()
+    assert abs(err - float(z["ortho768_frob"])) <= 5e-3 * max(1.0, float(z["ortho768_frob"]))
+
+
+def test_ns_identity_4x4():
+    """tensor_engine.rs:198-210."""
+    t = torch.eye(4, device="cuda")
+    _native.newton_schulz_2d_ffi(t.data_ptr(), 4, 4, 5)
+    gram = (t @ t.T).cpu()
+    assert gram[0, 0] > 0.5
+
+
+def test_ns_zero_steps_is_the_normalisation():
+    x = (np.random.default_rng(1).standard_normal((33, 70)) * 3).astype(np.float32)
+    ref = oracle.polar_step(x.copy(), 0)
+    t = torch.from_numpy(x.copy()).cuda()
+    _native.newton_schulz_2d_ffi(t.data_ptr(), 33, 70, 0)
+    assert_bitexact(to_np(t), ref, "steps=0")
+
+
+@pytest.mark.parametrize("steps", [1, 2, 7])
+def test_ns_step_counts(steps):
+    x = (np.random.default_rng(steps).standard_normal((256, 384)) * 0.1).astype(np.float32)
+    ref = oracle.polar_step_np(x, steps)
+    t = torch.from_numpy(x.copy()).cuda()
+    _native.newton_schulz_2d_ffi(t.data_ptr(), 256, 384, steps)
+    assert relf(to_np(t), ref) <= 5e-3
+
+
+def test_ns_zero_matrix_and_empty():
+    t = torch.zeros(64, 64, device="cuda")
+    _native.newton_schulz_2d_ffi(t.data_ptr(), 64, 64, 5)
+    assert torch.count_nonzero(t).item() == 0
+    _native.newton_schulz_2d_ffi(t.data_ptr(), 0, 64, 5)  # tensor_engine.rs:13-15: no-op
+
+
+@pytest.mark.parametrize("prec", PRECISIONS)
+def test_ns_bf16_matrix(prec):
+    x = (np.random.default_rng(5).standard_normal((300, 500)) * 0.02).astype(np.float32)
+    xb = torch.from_numpy(x).to(torch.bfloat16)
+    ref = oracle.polar_step_np(xb.float().numpy(), 5)
+    t = xb.cuda()
+    _native.newton_schulz_2d_ffi(t.data_ptr(), 300, 500, 5, dtype=_native.TK_BF16, precision=prec)
+    assert relf(t.float().cpu().numpy(), ref) <= NS_TOL[prec] + 4e-3
+
+
+def test_ns_3d_heads():
+    x = (np.random.default_rng(9).standard_normal((5, 48, 80)) * 0.02).astype(np.float32)
+    ref = oracle.polar_batched_np(x, 5)
+    t = torch.from_numpy(x.copy()).cuda()
+    _native.newton_schulz_3d_ffi(t.data_ptr(), 5, 48, 80, 5)
+    got = to_np(t)
+    for h in range(5):
+        assert relf(got[h], ref[h]) <= 5e-3
+
+
+def test_ns_host_pointer():
+    x = (np.random.default_rng(4).standard_normal((96, 160)) * 0.02).astype(np.float32)
+    ref = oracle.polar_step_np(x, 5)
+    y = x.copy()
+    _native.newton_schulz_2d_ffi(y.ctypes.data, 96, 160, 5)
+    assert relf(y, ref) <= 5e-3
+
+
+# -- fused Muon step -------------------------------------------------------
+def _muon_oracle_step(p, buf, g, lr, mu, rows, cols, heads, p_bf16):
+    u = oracle.muon_momentum(buf, g, mu, True).reshape(heads, rows, cols)
+    o = np.stack([oracle.polar_step_np(u[h], 5) for h in range(heads)]).reshape(p.shape)
+    alpha = np.float32(-lr * oracle.muon_update_scale(rows, cols))
+    if p_bf16:
+        pf = oracle.bf16_to_f32(p)
+        return oracle.f32_to_bf16(pf + alpha * o), o
+    return (p + alpha * o).astype(np.float32), o
+
+
+@pytest.mark.parametrize("rows,cols,heads", [(768, 768, 1), (768, 3072, 1), (3072, 768, 1),
+                                             (96, 40, 1), (16, 24, 3)])
+@pytest.mark.parametrize("p_bf16", [False, True], ids=["p_f32", "p_bf16"])
+def test_muon_step_ten_steps(rows, cols, heads, p_bf16):
+    shape = (heads, rows, cols) if heads > 1 else (rows, cols)
+    rng = np.random.default_rng(rows + cols + heads)
+    p0 = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+    if p_bf16:
+        p_ref = oracle.f32_to_bf16(p0)
+        p = torch.from_numpy(p_ref.view(np.int16).copy()).view(torch.bfloat16).cuda()
+    else:
+        p_ref = p0.copy()
+        p = torch.from_numpy(p0.copy()).cuda()
+    buf_ref = np.zeros(shape, np.float32)
+    mom = torch.zeros(shape, dtype=torch.float32, device="cuda")
+    lr, mu = 0.02, 0.95
+    for step in range(10):
+        g = (rng.standard_normal(shape) * 1e-3).astype(np.float32)
+        gt = torch.from_numpy(g).cuda()
+        prev = p.float().clone()
+        _native.muon_step([(p.data_ptr(), gt.data_ptr(), mom.data_ptr(), heads, rows, cols,
+                            _native.TK_BF16 if p_bf16 else _native.TK_F32, _native.TK_F32)],
+                          lr, mu, nesterov=True, ns_steps=5)
+        p_ref, o_ref = _muon_oracle_step(p_ref, buf_ref, g, lr, mu, rows, cols, heads, p_bf16)
+        if step == 0:
+            assert_bitexact(to_np(mom), buf_ref, "momentum")
+            alpha = -lr * oracle.muon_update_scale(rows, cols)
+            upd = ((p.float() - prev) / alpha).cpu().numpy()
+            if not p_bf16:
+                assert relf(upd, o_ref) <= 5e-3
+    assert_bitexact(to_np(mom), buf_ref, "momentum after 10 steps")
+    assert _native.device_status() == 0
+    got = p.float().cpu().numpy()
+    ref = oracle.bf16_to_f32(p_ref) if p_bf16 else p_ref
+    err = relf(got, ref)
+    print(f"params rel Frobenius after 10 steps: {err:.3e}")
+    assert err <= (1e-3 if not p_bf16 else 3e-3), err
+
+
+def test_muon_nd_frontend_matches_reference_frontend(golden_dir):
+    """tikun_b200.MuonND against the reference's MuonND (python/tikun/muon_nd.py)
+    run over the oracle: 1-D AdamW leaves bit-identical, 2-D/3-D leaves within
+    the Newton-Schulz bar."""
+    import tikun_b200
+
+    z = np.load(os.path.join(golden_dir, "frontend_reference.npz"))
+    keys = ["bias", "w_wide", "w_tall", "heads"]
+    params = {k: torch.tensor(z[f"muon_nd/init/{k}"], device="cuda", requires_grad=True)
+              for k in keys}
+    opt = tikun_b200.MuonND(params, lr=0.02, momentum=0.95, nesterov=True, ns_steps=5)
+    for s in range(3):
+        for k in keys:
+            params[k].grad = torch.tensor(z[f"muon_nd/grad{s}/{k}"], device="cuda")
+        opt.step()
+    torch.cuda.synchronize()
+    assert_bitexact(to_np(params["bias"]), z["muon_nd/final/bias"], "bias")
+    for k in ["w_wide", "w_tall", "heads"]:
+        init = z[f"muon_nd/init/{k}"]
+        d_ref = z[f"muon_nd/final/{k}"] - init
+        d_got = to_np(params[k]) - init
+        assert relf(d_got, d_ref) <= 5e-3, k

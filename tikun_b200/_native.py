@@ -47,6 +47,29 @@ class TkHParams(ctypes.Structure):
     _fields_ = [(k, ctypes.c_float) for k in ("lr", "beta1", "beta2", "eps", "decay")]
 
 
+class TkMuonLeaf(ctypes.Structure):
+    _fields_ = [
+        ("p", ctypes.c_void_p),
+        ("g", ctypes.c_void_p),
+        ("momentum", ctypes.c_void_p),
+        ("heads", ctypes.c_int64),
+        ("rows", ctypes.c_int64),
+        ("cols", ctypes.c_int64),
+        ("p_dtype", ctypes.c_int32),
+        ("g_dtype", ctypes.c_int32),
+    ]
+
+
+class TkMuonHParams(ctypes.Structure):
+    _fields_ = [
+        ("lr", ctypes.c_double),
+        ("momentum", ctypes.c_double),
+        ("nesterov", ctypes.c_int32),
+        ("ns_steps", ctypes.c_int32),
+        ("precision", ctypes.c_int32),
+    ]
+
+
 class TkScheduleNode(ctypes.Structure):
     _fields_ = [
         ("name", ctypes.c_char_p),
@@ -102,7 +125,17 @@ _SIGNATURES = {
     "tk_apply_pointwise": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,
                            _P, _P],
     "tk_set_update_events": [_P, _P],
+    "tk_newton_schulz_2d": [_P, _I64, _I64, _I32, _I32, _I32, _P],
+    "tk_newton_schulz_3d": [_P, _I64, _I64, _I64, _I32, _I32, _I32, _P],
+    "tk_muon_step": [ctypes.POINTER(TkMuonLeaf), _SZ, ctypes.POINTER(TkMuonHParams), _P],
+    "tk_device_status": [ctypes.POINTER(ctypes.c_int)],
+    "tk_testing_gemm_tn": [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                           _I64, _I64, _I64, _F, ctypes.c_int, _P],
 }
+
+# Newton-Schulz operand type used when the caller does not choose: f16 with a
+# power-of-two pre-scale (same tensor-core rate as bf16, 8x smaller rounding).
+DEFAULT_NS_PRECISION = TK_NS_F16
 
 
 def lib() -> ctypes.CDLL:
@@ -194,6 +227,44 @@ def step_fast_buffers_async(param_ptrs, grad_ptrs, m1_ptrs, m2_ptrs, lengths, ma
     check(lib().tk_step_buffers_async(leaves, n, opt_kind(opt_kind_name), ctypes.byref(hp),
                                       int(step_count), max_norm, clip_scale_ptr or None,
                                       current_stream() if stream is None else stream))
+
+
+def newton_schulz_2d_ffi(matrix_ptr: int, rows: int, cols: int, steps: int, *,
+                         dtype: int = TK_F32, precision: int | None = None,
+                         stream: int | None = None) -> None:
+    """The reference's ``newton_schulz_2d_ffi``: in-place polar step of a
+    row-major rows x cols matrix (f32 by default, as the reference takes)."""
+    check(lib().tk_newton_schulz_2d(matrix_ptr, rows, cols, steps, dtype,
+                                    DEFAULT_NS_PRECISION if precision is None else precision,
+                                    current_stream() if stream is None else stream))
+
+
+def newton_schulz_3d_ffi(tensor_ptr: int, num_heads: int, head_dim_out: int, head_dim_in: int,
+                         steps: int, *, dtype: int = TK_F32, precision: int | None = None,
+                         stream: int | None = None) -> None:
+    """The reference's ``newton_schulz_3d_ffi``: polar step of each head."""
+    check(lib().tk_newton_schulz_3d(tensor_ptr, num_heads, head_dim_out, head_dim_in, steps,
+                                    dtype, DEFAULT_NS_PRECISION if precision is None else precision,
+                                    current_stream() if stream is None else stream))
+
+
+def muon_step(leaves: Sequence[tuple], lr: float, momentum: float, nesterov: bool = True,
+              ns_steps: int = 5, precision: int | None = None, stream: int | None = None) -> None:
+    """Fused Muon update over (p_ptr, g_ptr, mom_ptr, heads, rows, cols, p_dtype,
+    g_dtype) leaves (device memory).  Does not wait."""
+    arr = (TkMuonLeaf * max(len(leaves), 1))()
+    for i, L in enumerate(leaves):
+        arr[i] = TkMuonLeaf(*L)
+    hp = TkMuonHParams(lr, momentum, 1 if nesterov else 0, ns_steps,
+                       DEFAULT_NS_PRECISION if precision is None else precision)
+    check(lib().tk_muon_step(arr, len(leaves), ctypes.byref(hp),
+                             current_stream() if stream is None else stream))
+
+
+def device_status() -> int:
+    out = ctypes.c_int(0)
+    check(lib().tk_device_status(ctypes.byref(out)))
+    return int(out.value)
 
 
 def verify(nodes: Sequence[tuple], max_norm: float = 0.0) -> None:

@@ -74,6 +74,23 @@ static int device_pool(cudaMemPool_t* out) {
   return TK_OK;
 }
 
+static int* g_status[64] = {};
+
+int device_status_word(int** out) {
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  if (g_status[dev] == nullptr) {
+    int* p = nullptr;
+    TK_CUDA_TRY(cudaMalloc(&p, 256));
+    TK_CUDA_TRY(cudaMemset(p, 0, 256));
+    g_status[dev] = p;
+  }
+  *out = g_status[dev];
+  return TK_OK;
+}
+
 Scratch::~Scratch() {
   if (ptr_ != nullptr) cudaFreeAsync(ptr_, stream_);
 }
@@ -131,9 +148,7 @@ static int verify_pipeline(const tk_pipeline* pl) {
 // ------------------------------------------------------------------ leaves
 static size_t esize(int dt) { return dt == TK_F32 ? 4 : 2; }
 
-enum class Residency { kNone, kDevice, kHost };
-
-static int classify(const void* ptr, Residency* r, int dev) {
+int classify_pointer(const void* ptr, Residency* r, int dev) {
   cudaPointerAttributes a;
   cudaError_t e = cudaPointerGetAttributes(&a, ptr);
   if (e != cudaSuccess) {
@@ -189,7 +204,7 @@ static int validate_leaves(const tk_leaf* leaves, size_t n, int kind, Residency*
     for (const void* ptr : ptrs) {
       if (ptr == nullptr) continue;
       Residency r;
-      TK_TRY(classify(ptr, &r, dev));
+      TK_TRY(classify_pointer(ptr, &r, dev));
       if (*where == Residency::kNone) *where = r;
       else if (*where != r)
         return set_error(TK_ERR_INVALID,

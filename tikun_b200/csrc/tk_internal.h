@@ -46,6 +46,15 @@ class Scratch {
 
 int sm_count(int* out);
 
+// Where a pointer lives (cudaPointerGetAttributes); device memory of another
+// device is an error.
+enum class Residency { kNone, kDevice, kHost };
+int classify_pointer(const void* ptr, Residency* r, int dev);
+
+// A persistent per-device status word that kernels set when a bounded wait
+// expires (0 = fine).
+int device_status_word(int** out);
+
 // ---------------------------------------------------------------- pointwise
 constexpr int kMaxLeavesPerLaunch = 224;
 

@@ -1,0 +1,234 @@
+// C-ABI entry points of the Newton-Schulz engine (include/tikun_cuda.h):
+// tk_newton_schulz_2d / _3d (the reference's newton_schulz_2d_ffi and
+// newton_schulz_3d_ffi) and tk_muon_step (momentum, Nesterov, Newton-Schulz
+// and the scaled update of python/tikun/muon_nd.py:104-160 in one call).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <map>
+#include <tuple>
+#include <vector>
+
+#include "tk_internal.h"
+#include "tk_ns.h"
+#include "tk_testing.h"
+
+namespace tk {
+
+static size_t ns_scratch_budget() {
+  const char* e = std::getenv("TIKUN_NS_SCRATCH_GB");
+  double gb = e ? std::atof(e) : 8.0;
+  if (!(gb > 0.0)) gb = 8.0;
+  return (size_t)(gb * (1ull << 30));
+}
+
+static int fmt_of(int precision) {
+  return precision == TK_NS_BF16 ? 1 : (precision == TK_NS_F16 ? 0 : -1);
+}
+
+// Reads and clears the device status word after the stream has drained.
+static int check_status(cudaStream_t s) {
+  int* status = nullptr;
+  TK_TRY(device_status_word(&status));
+  int h = 0;
+  TK_CUDA_TRY(cudaStreamSynchronize(s));
+  TK_CUDA_TRY(cudaMemcpy(&h, status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h != 0) {
+    TK_CUDA_TRY(cudaMemset(status, 0, sizeof(int)));
+    return set_error(TK_ERR_DEVICE,
+                     "a Newton-Schulz kernel gave up on a bounded wait (code %d); results of "
+                     "this call are not valid",
+                     h);
+  }
+  return TK_OK;
+}
+
+// Runs NS over `count` same-shape matrices in waves that fit the scratch budget.
+static int run_batches(int64_t rows, int64_t cols, const std::vector<const void*>& src,
+                       const std::vector<void*>& dst, const std::vector<float*>* mom,
+                       int src_dtype, int dst_dtype, int update, float upd_scale, float mu,
+                       float om, int nesterov, int steps, int fmt, cudaStream_t s) {
+  const int64_t count = (int64_t)src.size();
+  const ns::GroupLayout one = ns::group_layout(rows, cols, 1);
+  const int64_t per_wave =
+      std::max<int64_t>(1, std::min<int64_t>(count, (int64_t)(ns_scratch_budget() / one.scratch_bytes)));
+  int* status = nullptr;
+  TK_TRY(device_status_word(&status));
+  for (int64_t first = 0; first < count; first += per_wave) {
+    const int64_t nb = std::min(per_wave, count - first);
+    const ns::GroupLayout L = ns::group_layout(rows, cols, nb);
+    Scratch scratch;
+    TK_TRY(scratch.alloc(L.scratch_bytes, s));
+    ns::GroupIO io;
+    io.src = src.data() + first;
+    io.dst = dst.data() + first;
+    io.mom = mom ? mom->data() + first : nullptr;
+    io.src_dtype = src_dtype;
+    io.dst_dtype = dst_dtype;
+    io.update = update;
+    io.upd_scale = upd_scale;
+    io.mu = mu;
+    io.om = om;
+    io.nesterov = nesterov;
+    TK_TRY(ns::run_group(L, io, steps, fmt, scratch.get(), status, s));
+  }
+  return TK_OK;
+}
+
+static size_t dt_size(int dt) { return dt == TK_F32 ? 4 : 2; }
+
+static int ns_entry(void* base, int64_t heads, int64_t rows, int64_t cols, int32_t steps,
+                    int32_t dtype, int32_t precision, cudaStream_t s) {
+  if (heads < 0 || rows < 0 || cols < 0 || steps < 0)
+    return set_error(TK_ERR_INVALID, "negative size or step count");
+  if (dtype != TK_F32 && dtype != TK_BF16)
+    return set_error(TK_ERR_INVALID, "matrix dtype %d is not f32 or bf16", dtype);
+  const int fmt = fmt_of(precision);
+  if (fmt < 0) return set_error(TK_ERR_INVALID, "unknown Newton-Schulz precision %d", precision);
+  // tensor_engine.rs:13-15: empty matrices are left alone
+  if (heads == 0 || rows == 0 || cols == 0) return TK_OK;
+  if (base == nullptr) return set_error(TK_ERR_INVALID, "matrix pointer is NULL");
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  Residency where;
+  TK_TRY(classify_pointer(base, &where, dev));
+  const size_t esz = dt_size(dtype);
+  const size_t bytes = (size_t)heads * rows * cols * esz;
+  Scratch stage;
+  char* dbase = static_cast<char*>(base);
+  if (where == Residency::kHost) {
+    TK_TRY(stage.alloc(bytes, s));
+    dbase = static_cast<char*>(stage.get());
+    TK_CUDA_TRY(cudaMemcpyAsync(dbase, base, bytes, cudaMemcpyHostToDevice, s));
+  }
+  std::vector<const void*> src(heads);
+  std::vector<void*> dst(heads);
+  for (int64_t h = 0; h < heads; ++h) {
+    dst[h] = dbase + (size_t)h * rows * cols * esz;
+    src[h] = dst[h];
+  }
+  TK_TRY(run_batches(rows, cols, src, dst, nullptr, dtype, dtype, 0, 0.f, 0.f, 0.f, 0, steps, fmt, s));
+  if (where == Residency::kHost)
+    TK_CUDA_TRY(cudaMemcpyAsync(base, dbase, bytes, cudaMemcpyDeviceToHost, s));
+  return check_status(s);
+}
+
+}  // namespace tk
+
+using namespace tk;
+
+extern "C" {
+
+int tk_newton_schulz_2d(void* matrix, int64_t rows, int64_t cols, int32_t steps, int32_t dtype,
+                        int32_t precision, void* stream) {
+  return ns_entry(matrix, 1, rows, cols, steps, dtype, precision,
+                  static_cast<cudaStream_t>(stream));
+}
+
+int tk_newton_schulz_3d(void* tensor, int64_t num_heads, int64_t head_dim_out,
+                        int64_t head_dim_in, int32_t steps, int32_t dtype, int32_t precision,
+                        void* stream) {
+  return ns_entry(tensor, num_heads, head_dim_out, head_dim_in, steps, dtype, precision,
+                  static_cast<cudaStream_t>(stream));
+}
+
+int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
+                 void* stream) {
+  if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
+  if (n_leaves > 0 && leaves == nullptr) return set_error(TK_ERR_INVALID, "leaves is NULL");
+  const int fmt = fmt_of(hp->precision);
+  if (fmt < 0) return set_error(TK_ERR_INVALID, "unknown Newton-Schulz precision %d", hp->precision);
+  if (hp->ns_steps < 0) return set_error(TK_ERR_INVALID, "negative Newton-Schulz step count");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+
+  struct Range {
+    uintptr_t lo, hi;
+    bool w;
+  };
+  std::vector<Range> ranges;
+  // group by (rows, cols, p dtype, g dtype): every head of every leaf of a
+  // group is one matrix of one batch
+  struct Batch {
+    std::vector<const void*> g;
+    std::vector<void*> p;
+    std::vector<float*> mom;
+  };
+  std::map<std::tuple<int64_t, int64_t, int, int>, Batch> groups;
+  for (size_t i = 0; i < n_leaves; ++i) {
+    const tk_muon_leaf& L = leaves[i];
+    if (L.heads < 0 || L.rows < 0 || L.cols < 0)
+      return set_error(TK_ERR_INVALID, "leaf %zu: negative shape", i);
+    if ((L.p_dtype != TK_F32 && L.p_dtype != TK_BF16) || (L.g_dtype != TK_F32 && L.g_dtype != TK_BF16))
+      return set_error(TK_ERR_INVALID, "leaf %zu: p and g must be f32 or bf16", i);
+    const int64_t heads = L.heads == 0 ? 1 : L.heads;
+    if (L.rows == 0 || L.cols == 0) continue;
+    if (L.p == nullptr || L.g == nullptr || L.momentum == nullptr)
+      return set_error(TK_ERR_INVALID, "leaf %zu: null p, g or momentum", i);
+    const size_t n = (size_t)heads * L.rows * L.cols;
+    ranges.push_back({(uintptr_t)L.p, (uintptr_t)L.p + n * dt_size(L.p_dtype), true});
+    ranges.push_back({(uintptr_t)L.g, (uintptr_t)L.g + n * dt_size(L.g_dtype), false});
+    ranges.push_back({(uintptr_t)L.momentum, (uintptr_t)L.momentum + n * 4, true});
+    for (const void* ptr : {(const void*)L.p, L.g, (const void*)L.momentum}) {
+      Residency r;
+      TK_TRY(classify_pointer(ptr, &r, dev));
+      if (r != Residency::kDevice)
+        return set_error(TK_ERR_INVALID, "leaf %zu: tk_muon_step takes device buffers", i);
+    }
+    Batch& b = groups[std::make_tuple(L.rows, L.cols, L.p_dtype, L.g_dtype)];
+    const size_t mat = (size_t)L.rows * L.cols;
+    for (int64_t h = 0; h < heads; ++h) {
+      b.g.push_back(static_cast<const char*>(L.g) + h * mat * dt_size(L.g_dtype));
+      b.p.push_back(static_cast<char*>(L.p) + h * mat * dt_size(L.p_dtype));
+      b.mom.push_back(L.momentum + h * mat);
+    }
+  }
+  std::sort(ranges.begin(), ranges.end(), [](const Range& a, const Range& b) { return a.lo < b.lo; });
+  uintptr_t max_any = 0, max_w = 0;
+  for (const Range& r : ranges) {
+    if ((r.w && max_any > r.lo) || max_w > r.lo)
+      return set_error(TK_ERR_INVALID, "Muon leaf buffers overlap at %p", (void*)r.lo);
+    max_any = std::max(max_any, r.hi);
+    if (r.w) max_w = std::max(max_w, r.hi);
+  }
+  // muon_nd.py: buf *= momentum; buf += (1.0 - momentum) * g  (NumPy float32 with
+  // Python-float scalars rounded once), scale = max(1, rows/cols) ** 0.5,
+  // p += (-lr * scale) * U
+  const float mu = (float)hp->momentum;
+  const float om = (float)(1.0 - hp->momentum);
+  for (auto& kv : groups) {
+    const int64_t rows = std::get<0>(kv.first), cols = std::get<1>(kv.first);
+    const int pdt = std::get<2>(kv.first), gdt = std::get<3>(kv.first);
+    const double scale = std::sqrt(std::max(1.0, (double)rows / (double)cols));
+    const float upd = (float)(-hp->lr * scale);
+    TK_TRY(run_batches(rows, cols, kv.second.g, kv.second.p, &kv.second.mom, gdt, pdt, 1, upd, mu,
+                       om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s));
+  }
+  return TK_OK;
+}
+
+int tk_device_status(int* status_out) {
+  if (status_out == nullptr) return set_error(TK_ERR_INVALID, "status_out is NULL");
+  int* status = nullptr;
+  TK_TRY(device_status_word(&status));
+  TK_CUDA_TRY(cudaDeviceSynchronize());
+  TK_CUDA_TRY(cudaMemcpy(status_out, status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (*status_out != 0) TK_CUDA_TRY(cudaMemset(status, 0, sizeof(int)));
+  return TK_OK;
+}
+
+int tk_testing_gemm_tn(const void* P, const void* Q, void* D, int batch, int M, int N, int K,
+                       int64_t ldp, int64_t ldq, int64_t ldd, float alpha, int fmt, void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = nullptr;
+  TK_TRY(device_status_word(&status));
+  TK_TRY(ns::plain_gemm(static_cast<const uint16_t*>(P), static_cast<const uint16_t*>(Q),
+                        static_cast<uint16_t*>(D), batch, M, N, K, ldp, ldq, ldd, alpha, fmt,
+                        status, s));
+  return check_status(s);
+}
+
+}  // extern "C"
