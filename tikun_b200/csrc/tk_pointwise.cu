@@ -22,8 +22,32 @@
 namespace tk {
 namespace {
 
+// Tuning knobs (compile time): quads each thread keeps in flight per loop
+// trip, the minimum resident CTAs per SM the register budget must allow, and
+// the cache policy of the streaming accesses (0: default, 1: evict-first).
+#ifndef TK_PW_UNROLL
+#define TK_PW_UNROLL 2
+#endif
+#ifndef TK_PW_MINBLOCKS
+#define TK_PW_MINBLOCKS 1
+#endif
+#ifndef TK_PW_STREAMING
+#define TK_PW_STREAMING 0
+#endif
 constexpr int kThreads = 256;
-constexpr int kUnroll = 2;
+constexpr int kUnroll = TK_PW_UNROLL;
+
+template <typename T>
+__device__ __forceinline__ T ld_stream(const T* p) {
+  if constexpr (TK_PW_STREAMING) return __ldcs(p);
+  else return *p;
+}
+
+template <typename T>
+__device__ __forceinline__ void st_stream(T* p, const T& v) {
+  if constexpr (TK_PW_STREAMING) __stcs(p, v);
+  else *p = v;
+}
 
 // ------------------------------------------------------------------ dtypes
 __device__ __forceinline__ float bf16_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
@@ -38,10 +62,10 @@ __device__ __forceinline__ uint32_t f32_to_bf16(float f) {
 template <int DT>
 __device__ __forceinline__ void load_quad(const void* base, uint64_t e, float (&x)[4]) {
   if constexpr (DT == TK_F32) {
-    const float4 q = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + e);
+    const float4 q = ld_stream(reinterpret_cast<const float4*>(static_cast<const float*>(base) + e));
     x[0] = q.x; x[1] = q.y; x[2] = q.z; x[3] = q.w;
   } else {
-    const uint2 q = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + e);
+    const uint2 q = ld_stream(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + e));
     x[0] = bf16_to_f32(q.x & 0xffffu); x[1] = bf16_to_f32(q.x >> 16);
     x[2] = bf16_to_f32(q.y & 0xffffu); x[3] = bf16_to_f32(q.y >> 16);
   }
@@ -50,12 +74,12 @@ __device__ __forceinline__ void load_quad(const void* base, uint64_t e, float (&
 template <int DT>
 __device__ __forceinline__ void store_quad(void* base, uint64_t e, const float (&x)[4]) {
   if constexpr (DT == TK_F32) {
-    *reinterpret_cast<float4*>(static_cast<float*>(base) + e) = make_float4(x[0], x[1], x[2], x[3]);
+    st_stream(reinterpret_cast<float4*>(static_cast<float*>(base) + e), make_float4(x[0], x[1], x[2], x[3]));
   } else {
     uint2 q;
     q.x = f32_to_bf16(x[0]) | (f32_to_bf16(x[1]) << 16);
     q.y = f32_to_bf16(x[2]) | (f32_to_bf16(x[3]) << 16);
-    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(base) + e) = q;
+    st_stream(reinterpret_cast<uint2*>(static_cast<uint16_t*>(base) + e), q);
   }
 }
 
@@ -203,7 +227,7 @@ clip_scale_kernel(const double* __restrict__ partials, int n, float max_norm,
 // ------------------------------------------------------------------ Tier 2
 // SCALE: 0 = no clipping, 1 = fold partials in every CTA, 2 = read scale_dev.
 template <int KIND, int PDT, int GDT, int SCALE>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, TK_PW_MINBLOCKS)
 pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
                  const double* __restrict__ partials, int n_partials, float max_norm,
                  const float* __restrict__ scale_dev, float* __restrict__ scale_out) {
