@@ -146,6 +146,21 @@ TK_API int tk_step_buffers_async(const tk_leaf* leaves, size_t n_leaves, int32_t
                           const tk_hparams* hp, uint64_t step, float max_norm,
                           float* clip_scale_dev, void* stream);
 
+/* tk_step_buffers for callers that cannot allocate device memory (an
+ * application that owns a fixed memory budget, or a host runtime whose
+ * allocator must not be re-entered from an optimizer hook).  No counterpart
+ * in the reference.  The norm's partial sums and the clip scale live in a
+ * fixed 64 KB device array per GPU (8192 f64 slots plus the scale) instead of
+ * pool memory; no cudaMalloc, cudaFree or other allocating routine is called.
+ * Device leaves only, at most 224 leaves and 8192 norm blocks per call, else
+ * TK_ERR_INVALID.  All calls on a device share the array: calls that overlap
+ * on the GPU race.  The first call on each device looks up the array's address
+ * (do it before any stream capture).  With clip_scale_out non-NULL the call
+ * waits for the stream and returns the scale. */
+TK_API int tk_step_buffers_noalloc(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                                   const tk_hparams* hp, uint64_t step, float max_norm,
+                                   float* clip_scale_out, void* stream);
+
 /* The pieces of the step, for callers that shard it (ZeRO-1 over ranks):
  *   tk_grad_sumsq       sum over the leaves of g*g in f64 -> *sumsq_dev
  *   tk_clip_scale       *scale_dev = clip scale of *sumsq_dev (lib.rs:117-122)

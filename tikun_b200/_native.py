@@ -125,6 +125,8 @@ _SIGNATURES = {
     "tk_apply_pointwise": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,
                            _P, _P],
     "tk_set_update_events": [_P, _P],
+    "tk_step_buffers_noalloc": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams),
+                                _U64, _F, ctypes.POINTER(_F), _P],
     "tk_newton_schulz_2d": [_P, _I64, _I64, _I32, _I32, _I32, _P],
     "tk_newton_schulz_3d": [_P, _I64, _I64, _I64, _I32, _I32, _I32, _P],
     "tk_muon_step": [ctypes.POINTER(TkMuonLeaf), _SZ, ctypes.POINTER(TkMuonHParams), _P],
