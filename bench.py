@@ -1,7 +1,8 @@
 """Benchmark of the tikun optimizer step on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tikun|reference]
-                    [--workload gpt2-small-clip|flat-100m]
+                    [--workload gpt2-small-clip|flat-100m|muon-gpt2-d768|
+                                muon-1.3b-inbackward|muon-llama3-8b]
 
 Default workload (the one the headline metric is quoted on at one GPU):
 clipped AdamW (global-norm clip 1.0) over the GPT-2-small PyTree, 148 fp32
@@ -17,6 +18,14 @@ updates its 1/N of the flat parameter space, f64 norm all-reduce, NCCL
 all-gather of the updated fp32 parameters) and the time is the max over ranks.
 ``e2e`` is the same step through the C ABI with the leaves in pinned host
 memory (the reference engine's calling convention), copies included.
+
+The Muon workloads (bf16 parameters and gradients, f32 momentum and AdamW
+moments; Muon with momentum 0.95, Nesterov, 5 Newton-Schulz steps, lr 0.02 on
+every hidden matrix; AdamW as above on embeddings and norms) report params/s
+and the Newton-Schulz tensor throughput (dense-equivalent FLOPs
+5(4m^2n + 2m^3) per matrix) against the measured bf16 peak.  At N GPUs the
+matrices are spread by FLOP-balanced bin-packing and the AdamW leaves by
+ZeRO-1; one all-gather per buffer reassembles the parameters.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's
 restatement of tikun-cpu; the Rust engine cannot be built here) on this host's
@@ -75,54 +84,65 @@ def load_peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples every 200 ms for the GPU with the given UUID."""
+    """Polls the GPU's SM clock and clock-event (throttle) reasons through NVML
+    every 2 ms while the timed region runs (nvidia-smi's 200 ms loop is too
+    coarse for a region of a few milliseconds)."""
 
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, uuid: str):
+    def __init__(self, uuid: str, period_s: float = 0.002):
         self.uuid = uuid
-        self.rows = []
-        self.proc = None
-        self.thread = None
+        self.period = period_s
+        self.samples = []
+        self.error = None
+        self._stop = threading.Event()
+        self._thread = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            u = self.uuid if self.uuid.startswith("GPU-") else "GPU-" + self.uuid
+            self._h = pynvml.nvmlDeviceGetHandleByUUID(u)
+            self._nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        except Exception as e:  # no NVML: report unsampled
+            self.error = f"{type(e).__name__}: {e}"
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and self.uuid and self.uuid in parts[0]:
-                self.rows.append(parts)
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((sm, reasons))
+            except Exception as e:
+                self.error = f"{type(e).__name__}: {e}"
+                return
+            time.sleep(self.period)
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.thread.join(timeout=5)
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self):
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "error": self.error}
+        nv = self._nv
+        reasons = sorted({name for _, r in self.samples for name, attr in self.REASONS
+                          if r & getattr(nv, attr)})
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+                "source": "nvml"}
 
 
 # ------------------------------------------------------------------ workload
@@ -183,43 +203,80 @@ def run_reference(args, wl, rank):
     }), flush=True)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="tikun", choices=["tikun", "reference"])
-    ap.add_argument("--workload", default="gpt2-small-clip", choices=sorted(WORKLOADS))
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-e2e", action="store_true")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
-    wl = WORKLOADS[args.workload]
+def muon_workloads():
+    """Muon configurations: (rows, cols) of the hidden matrices and AdamW leaf sizes."""
+    def gpt2(d=768, layers=12, vocab=50257):
+        mats = [(d, d)] * 4 + [(d, 4 * d), (4 * d, d)]
+        return mats * layers, [vocab * d] + [d] * (2 * (2 * layers + 1))
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    def gpt13(d=2048, layers=24, ffn=8192, vocab=50304):
+        mats = [(d, d)] * 4 + [(d, ffn), (ffn, d)]
+        return mats * layers, [vocab * d] + [d] * (2 * layers + 1), layers
 
-    if args.impl == "reference":
-        run_reference(args, wl, rank)
-        return
+    def llama8b(d=4096, layers=32, kv=1024, ffn=14336, vocab=128256):
+        mats = [(d, d), (d, kv), (d, kv), (d, d), (d, ffn), (d, ffn), (ffn, d)]
+        return mats * layers, [vocab * d, vocab * d] + [d] * (2 * layers + 1)
 
-    import torch
-    import torch.distributed as dist
+    m2, a2 = gpt2()
+    m3, a3, l3 = gpt13()
+    m4, a4 = llama8b()
+    return {
+        "muon-gpt2-d768": dict(mats=m2, adamw=a2, layers=12, inbackward=False,
+                               desc="Muon on 12 x {4 x 768^2, 768x3072, 3072x768} bf16 + AdamW "
+                                    "on wte 50257x768 and 25 LayerNorms"),
+        "muon-1.3b-inbackward": dict(mats=m3, adamw=a3, layers=l3, inbackward=True,
+                                     desc="Muon+AdamW, d=2048, 24 layers, ffn 8192, vocab 50304, "
+                                          "bf16; in-backward: per-layer steps fire in reverse "
+                                          "layer order on a side stream as each layer's "
+                                          "synthetic grads are produced"),
+        "muon-llama3-8b": dict(mats=m4, adamw=a4, layers=32, inbackward=False,
+                               desc="Muon+AdamW on Llama-3-8B shapes (d 4096, 32 layers, "
+                                    "GQA 4096x1024, ffn 14336, vocab 128256), bf16 params, "
+                                    "f32 momentum and moments"),
+    }
 
+
+MUON = muon_workloads()
+MUON_HP = dict(lr=0.02, momentum=0.95)
+
+
+def timed_loop(step_fn, steps, warmup, stream, world, dist, dev, torch, uuid, before_step=None):
+    """Warm-up, then `steps` timed steps between CUDA events on the launching
+    stream, bracketed by barrier + synchronize; returns (max-over-ranks ms,
+    launches, clock summary)."""
+    for _ in range(warmup):
+        step_fn()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches = 0
+    with ClockSampler(uuid) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        start.record(stream)
+        for k in range(steps):
+            if before_step is not None:
+                before_step(k)
+            launches += step_fn()
+        stop.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    t = torch.tensor([start.elapsed_time(stop)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), launches, clk.summary()
+
+
+def run_pointwise(args, wl, world, rank, dev, torch, dist):
     from tikun_b200 import _native
     from tikun_b200.arena import Arena, LayoutPlan, shard_bounds, shard_segments
 
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-    stream = torch.cuda.current_stream()
     L = _native.lib()
-
-    # --- state: one arena per array (p, g, m, v) -----------------------------
+    stream = torch.cuda.current_stream()
+    s_handle = stream.cuda_stream
     plan = LayoutPlan(wl["sizes"], pad_to=16 * max(world, 1))
     hp_np, hg_np = make_host_state(wl)
     P, G, M, V = (Arena(plan, device=dev) for _ in range(4))
@@ -229,82 +286,57 @@ def main():
     n_params = sum(wl["sizes"])
     lo, hi = shard_bounds(plan.total, world, rank)
     segs = shard_segments(plan, lo, hi)
-    es = 4
     pp, gp, mp, vp = P.ptrs(), G.ptrs(), M.ptrs(), V.ptrs()
     leaves, n_leaves = _native.make_leaves(
-        [pp[i] + a * es for i, a, c in segs], [gp[i] + a * es for i, a, c in segs],
-        [mp[i] + a * es for i, a, c in segs], [vp[i] + a * es for i, a, c in segs],
+        [pp[i] + a * 4 for i, a, c in segs], [gp[i] + a * 4 for i, a, c in segs],
+        [mp[i] + a * 4 for i, a, c in segs], [vp[i] + a * 4 for i, a, c in segs],
         [c for i, a, c in segs])
     my_params = sum(c for _, _, c in segs)
     hp = _native.TkHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"])
     scale_dev = torch.ones(1, dtype=torch.float32, device=dev)
     sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
-    s_handle = stream.cuda_stream
-    state = {"step": 0}
+    state = {"step": 0, "ev": None}
+    clip = wl["max_norm"] > 0
 
     def one_step():
         state["step"] += 1
+        ev = state["ev"]
+        _native.check(L.tk_set_update_events(*(ev if ev else (None, None))))
         if world == 1:
             _native.check(L.tk_step_buffers_async(leaves, n_leaves, _native.TK_ADAMW,
                                                   ctypes.byref(hp), state["step"],
                                                   wl["max_norm"], scale_dev.data_ptr(), s_handle))
-            return 2 if wl["max_norm"] > 0 else 1
+            return 2 if clip else 1
         launches = 0
-        if wl["max_norm"] > 0:
+        if clip:
             _native.check(L.tk_grad_sumsq(leaves, n_leaves, sumsq.data_ptr(), s_handle))
             dist.all_reduce(sumsq)
             _native.check(L.tk_clip_scale(sumsq.data_ptr(), wl["max_norm"], scale_dev.data_ptr(),
                                           s_handle))
             launches += 3
-        _native.check(L.tk_set_update_events(*state["ev"]) if "ev" in state else 0)
         _native.check(L.tk_apply_pointwise(leaves, n_leaves, _native.TK_ADAMW, ctypes.byref(hp),
-                                           state["step"],
-                                           scale_dev.data_ptr() if wl["max_norm"] > 0 else None,
+                                           state["step"], scale_dev.data_ptr() if clip else None,
                                            s_handle))
         dist.all_gather_into_tensor(P.flat, P.flat[lo:hi])
         return launches + 1
 
-    # --- timed region ----------------------------------------------------------
-    for _ in range(args.warmup):
-        one_step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(args.steps)]
     for a, b in ev_pairs:  # torch creates the CUDA events on first record
         a.record(stream)
         b.record(stream)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def before(k):
+        state["ev"] = (ev_pairs[k][0].cuda_event, ev_pairs[k][1].cuda_event)
+
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
-    launches = 0
-    with ClockSampler(uuid) as clk:
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        start.record(stream)
-        for k in range(args.steps):
-            a, b = ev_pairs[k]
-            state["ev"] = (ctypes.c_void_p(a.cuda_event), ctypes.c_void_p(b.cuda_event))
-            if world == 1:
-                _native.check(L.tk_set_update_events(a.cuda_event, b.cuda_event))
-            launches += one_step()
-        stop.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+    ms_total, launches, clocks = timed_loop(one_step, args.steps, args.warmup, stream, world, dist,
+                                            dev, torch, uuid, before)
+    state["ev"] = None
     _native.check(L.tk_set_update_events(None, None))
-    state.pop("ev", None)
-    ms_total = start.elapsed_time(stop)
     upd_ms = sum(a.elapsed_time(b) for a, b in ev_pairs) / args.steps
-    t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total = float(t.item())
     ms_step = ms_total / args.steps
     value = n_params / (ms_step / 1e3)
-
-    # --- roofline of the update kernel: 28 B/param (read p, g, m, v; write p, m, v)
     peak, peak_kind = load_peaks()
     upd_bytes = 28 * my_params
     achieved = upd_bytes / (upd_ms / 1e3) / 1e9
@@ -316,7 +348,6 @@ def main():
         if tr:
             traffic = tr["bytes_per_param"] * my_params
 
-    # --- e2e: host (pinned) leaves through the C ABI, copies inside the region
     e2e = None
     if not args.no_e2e and world == 1:
         hp_pin = [torch.from_numpy(x).pin_memory() for x in hp_np]
@@ -343,10 +374,10 @@ def main():
         e_ms = e0.elapsed_time(e1) / e2e_steps
         e2e = {"value": n_params / (e_ms / 1e3), "unit": "params/s", "ms_per_step": e_ms,
                "h2d_bytes_per_step": 16 * n_params, "d2h_bytes_per_step": 12 * n_params + 4,
-               "steps": e2e_steps, "host_memory": "pinned"}
+               "steps": e2e_steps, "host_memory": "pinned",
+               "api": "tk_step_buffers with host leaves (copies inside the call)"}
         del hp_pin, hg_pin, hm_pin, hv_pin
 
-    # --- CPU baseline (rank 0, one GPU): the oracle on a bounded sample
     cpu = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
         nthreads = os.cpu_count() or 1
@@ -354,29 +385,227 @@ def main():
         cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
                "sample": f"full workload, 2 timed steps after 1 warm-up, {nthreads} threads over "
                          f"leaves ({cms:.0f} ms/step)"}
+    return {
+        "value": value, "ms_per_step": ms_step, "dtype": "f32", "scaling": "strong",
+        "data": "synthetic (seeded N(0,0.02) params, N(0,%g) grads held fixed across steps)"
+                % wl["g_std"],
+        "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
+                   "leaves": len(wl["sizes"]),
+                   "parallelism": "single GPU" if world == 1 else f"zero1-dp{world}",
+                   "l2": "inputs (p,g,m,v) larger than L2; no flush"},
+        "roofline": {"bound": "hbm", "kernel": "pointwise_kernel (AdamW update)",
+                     "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "algorithmic_bytes_per_launch": upd_bytes, "update_ms": upd_ms,
+                     "step_GBps": (32 if clip else 28) * n_params / (ms_step / 1e3) / 1e9},
+        "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu,
+    }
 
+
+def run_muon(args, wl, world, rank, dev, torch, dist):
+    from tikun_b200 import _native
+    from tikun_b200.arena import LayoutPlan, shard_bounds, shard_segments
+    from tikun_b200.sharding import lpt_assign, ns_dense_flops, ns_issued_flops, owner_major_layout
+
+    L = _native.lib()
+    stream = torch.cuda.current_stream()
+    s_handle = stream.cuda_stream
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    mats = wl["mats"]
+    sizes = [r * c for r, c in mats]
+    costs = [ns_dense_flops(r, c) for r, c in mats]
+    owner = lpt_assign(costs, world) if world > 1 else [0] * len(mats)
+    offs, extent = owner_major_layout(sizes, owner, world)
+    bf = torch.bfloat16
+    # Muon parameters: owner-major arena (bf16), so one all-gather reassembles them
+    p_mu = torch.empty(extent * world, dtype=bf, device=dev)
+    p_mu.normal_(0, 0.02, generator=gen)
+    mine = [i for i in range(len(mats)) if owner[i] == rank]
+    g_mu, mom = {}, {}
+    for i in mine:
+        g_mu[i] = torch.empty(sizes[i], dtype=bf, device=dev).normal_(0, 1e-3, generator=gen)
+        mom[i] = torch.zeros(sizes[i], dtype=torch.float32, device=dev)
+    # AdamW leaves: one arena, ZeRO-1 slice per rank
+    plan = LayoutPlan(wl["adamw"], pad_to=64 * max(world, 1))
+    p_aw = torch.empty(plan.total, dtype=bf, device=dev).normal_(0, 0.02, generator=gen)
+    g_aw = torch.empty(plan.total, dtype=bf, device=dev).normal_(0, 1e-3, generator=gen)
+    m_aw = torch.zeros(plan.total, dtype=torch.float32, device=dev)
+    v_aw = torch.zeros(plan.total, dtype=torch.float32, device=dev)
+    lo, hi = shard_bounds(plan.total, world, rank)
+    segs = shard_segments(plan, lo, hi)
+
+    def aw_leaves(seg_list):
+        return _native.make_leaves(
+            [p_aw.data_ptr() + (plan.slots[i][0] + a) * 2 for i, a, c in seg_list],
+            [g_aw.data_ptr() + (plan.slots[i][0] + a) * 2 for i, a, c in seg_list],
+            [m_aw.data_ptr() + (plan.slots[i][0] + a) * 4 for i, a, c in seg_list],
+            [v_aw.data_ptr() + (plan.slots[i][0] + a) * 4 for i, a, c in seg_list],
+            [c for i, a, c in seg_list], [_native.TK_BF16] * len(seg_list),
+            [_native.TK_BF16] * len(seg_list))
+
+    hp = _native.TkHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"])
+    mhp = _native.TkMuonHParams(MUON_HP["lr"], MUON_HP["momentum"], 1, 5, _native.TK_NS_F16)
+
+    def mu_leaves(idx):
+        arr = (_native.TkMuonLeaf * max(len(idx), 1))()
+        for k, i in enumerate(idx):
+            r, c = mats[i]
+            arr[k] = _native.TkMuonLeaf(p_mu.data_ptr() + offs[i] * 2, g_mu[i].data_ptr(),
+                                        mom[i].data_ptr(), 1, r, c, _native.TK_BF16,
+                                        _native.TK_BF16)
+        return arr, len(idx)
+
+    state = {"step": 0, "ns_ms": []}
+    ns_ev = []
+    if not wl["inbackward"] or world > 1:
+        all_mu = mu_leaves(mine)
+        all_aw = aw_leaves(segs)
+
+        def one_step():
+            state["step"] += 1
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            _native.check(L.tk_muon_step(all_mu[0], all_mu[1], ctypes.byref(mhp), s_handle))
+            e1.record(stream)
+            ns_ev.append((e0, e1))
+            _native.check(L.tk_apply_pointwise(all_aw[0], all_aw[1], _native.TK_ADAMW,
+                                               ctypes.byref(hp), state["step"], None, s_handle))
+            if world > 1:
+                dist.all_gather_into_tensor(p_mu, p_mu[rank * extent:(rank + 1) * extent])
+                dist.all_gather_into_tensor(p_aw, p_aw[lo:hi])
+            return -1  # counted below from the tile plan
+    else:
+        # in-backward (one GPU): layer l's grads are produced on the main stream
+        # (a generator kernel standing in for backward), then its Muon and
+        # AdamW steps run on a side stream, in reverse layer order
+        side = torch.cuda.Stream(device=dev)
+        per_layer = len(mats) // wl["layers"]
+        layer_mu = [mu_leaves(list(range(l * per_layer, (l + 1) * per_layer)))
+                    for l in range(wl["layers"])]
+        # norms of layer l: the two leaves after the embedding for that layer
+        layer_aw = [aw_leaves([s for s in segs if s[0] in (1 + 2 * l, 2 + 2 * l)])
+                    for l in range(wl["layers"])]
+        rest_aw = aw_leaves([s for s in segs if s[0] == 0 or s[0] == len(wl["adamw"]) - 1])
+        layer_ev = [torch.cuda.Event() for _ in range(wl["layers"])]
+
+        def one_step():
+            state["step"] += 1
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(side)
+            for l in reversed(range(wl["layers"])):
+                for i in range(l * per_layer, (l + 1) * per_layer):
+                    g_mu[i].normal_(0, 1e-3, generator=gen)
+                layer_ev[l].record(stream)
+                side.wait_event(layer_ev[l])
+                _native.check(L.tk_muon_step(layer_mu[l][0], layer_mu[l][1], ctypes.byref(mhp),
+                                             side.cuda_stream))
+                _native.check(L.tk_apply_pointwise(layer_aw[l][0], layer_aw[l][1],
+                                                   _native.TK_ADAMW, ctypes.byref(hp),
+                                                   state["step"], None, side.cuda_stream))
+            _native.check(L.tk_apply_pointwise(rest_aw[0], rest_aw[1], _native.TK_ADAMW,
+                                               ctypes.byref(hp), state["step"], None,
+                                               side.cuda_stream))
+            e1.record(side)
+            ns_ev.append((e0, e1))
+            stream.wait_stream(side)
+            return -1
+
+    uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    ms_total, _, clocks = timed_loop(one_step, args.steps, args.warmup, stream, world, dist, dev,
+                                     torch, uuid)
+    assert _native.device_status() == 0, "a Newton-Schulz kernel reported a bounded-wait timeout"
+    ms_step = ms_total / args.steps
+    n_params = sum(sizes) + sum(wl["adamw"])
+    value = n_params / (ms_step / 1e3)
+    ns_ms = sum(a.elapsed_time(b) for a, b in ns_ev[-args.steps:]) / args.steps
+    my_dense = sum(costs[i] for i in mine)
+    my_issued = sum(ns_issued_flops(*mats[i]) for i in mine)
+    d = json.load(open(os.path.join(REPO, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(REPO, "MEASURED_PEAKS.json")) else {}
+    long_step = ms_step > 100
+    peak = d.get("bf16_tflops_sustained" if long_step else "bf16_tflops", 1590.0)
+    peak_kind = ("measured " + ("sustained" if long_step else "burst")) if d else "fallback"
+    achieved = my_dense / (ns_ms / 1e3) / 1e12
+    # launches per step: per shape group and wave, 2 prologue + 3 GEMMs x 5
+    # iterations; plus the AdamW update launch(es)
+    groups = {}
+    for i in mine:
+        groups[mats[i]] = groups.get(mats[i], 0) + 1
+    launches = 0
+    for (r, c), cnt in groups.items():
+        m, n = min(r, c), max(r, c)
+        per_mat = 2 * (3 * m * n + 2 * m * m) + 2048
+        per_wave = max(1, min(cnt, (8 << 30) // per_mat))
+        waves = -(-cnt // per_wave)
+        launches += waves * (2 + 15)
+    launches = (launches + (wl["layers"] + 1 if wl["inbackward"] and world == 1 else 1)) * args.steps
+    return {
+        "value": value, "ms_per_step": ms_step, "dtype": "bf16 params, f16 tensor-core operands",
+        "scaling": "strong",
+        "data": "synthetic (seeded N(0,0.02) bf16 params, N(0,1e-3) bf16 grads)",
+        "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
+                   "muon_matrices": len(mats), "adamw_leaves": len(wl["adamw"]),
+                   "parallelism": "single GPU" if world == 1 else
+                   f"muon-lpt{world}+zero1-dp{world}",
+                   "l2": "inputs larger than L2; no flush"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_tn_kernel (Newton-Schulz GEMMs)",
+                     "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                     "flops": "dense-equivalent 5(4m^2n+2m^3) per matrix",
+                     "ns_ms_per_step": ns_ms,
+                     "issued_tflops": my_issued / (ns_ms / 1e3) / 1e12,
+                     "issued_frac": my_issued / (ns_ms / 1e3) / 1e12 / peak,
+                     "ns_dense_tflop_per_step_this_rank": my_dense / 1e12},
+        "gpu_launches": launches, "clocks": clocks, "e2e": None, "cpu_baseline": None,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="tikun", choices=["tikun", "reference"])
+    ap.add_argument("--workload", default="gpt2-small-clip", choices=sorted(WORKLOADS) + sorted(MUON))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if args.workload not in WORKLOADS:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the CPU reference arm covers the pointwise workloads; "
+                                  "Muon workloads are timed on the GPU only"}), flush=True)
+            return
+        run_reference(args, WORKLOADS[args.workload], rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    if args.workload in WORKLOADS:
+        res = run_pointwise(args, WORKLOADS[args.workload], world, rank, dev, torch, dist)
+    else:
+        res = run_muon(args, MUON[args.workload], world, rank, dev, torch, dist)
     if rank == 0:
-        line = {
-            "metric": METRIC, "value": value, "unit": "params/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,0.02) params, N(0,1e-2) grads held fixed across steps)",
-            "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
-                       "leaves": len(wl["sizes"]),
-                       "parallelism": "single GPU" if world == 1 else f"zero1-dp{world}",
-                       "l2": "inputs (1.99 GB of p,g,m,v) larger than L2; no flush"},
-            "roofline": {"bound": "hbm", "kernel": "pointwise_kernel (AdamW update)",
-                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
-                         "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": upd_bytes,
-                         "update_ms": upd_ms,
-                         "step_GBps_32B_per_param": 32 * n_params / (ms_step / 1e3) / 1e9
-                         if wl["max_norm"] > 0 else 28 * n_params / (ms_step / 1e3) / 1e9},
-            "gpu_launches": launches,
-            "clocks": clk.summary(),
-            "e2e": e2e,
-            "cpu_baseline": cpu,
-        }
+        line = {"metric": METRIC, "value": res["value"], "unit": "params/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                "higher_is_better": True, "scaling": res["scaling"], "vs_baseline": None,
+                "dtype": res["dtype"], "data": res["data"], "config": res["config"],
+                "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
+                "clocks": res["clocks"], "e2e": res["e2e"], "cpu_baseline": res["cpu_baseline"]}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

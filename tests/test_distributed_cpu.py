@@ -1,0 +1,164 @@
+"""Host-side logic of the multi-GPU step, on CPU.
+
+* ZeRO-1 slices of the flat arena cover every leaf element exactly once.
+* LPT bin-packing of Muon matrices by Newton-Schulz FLOPs is deterministic
+  and balanced; the owner-major layout gives disjoint, aligned, per-rank ranges.
+* A 2-rank gloo run of the step's choreography: each rank transforms only the
+  elements it owns (a stand-in for the device update, done on CPU tensors), the
+  f64 partial sums are all-reduced, and one all-gather per buffer reassembles
+  identical full buffers on every rank.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tikun_b200.arena import LayoutPlan, shard_bounds, shard_segments
+from tikun_b200.sharding import (lpt_assign, ns_dense_flops, ns_issued_flops,
+                                 owner_major_layout)
+
+
+def llama8b_mats():
+    d, kv, ffn = 4096, 1024, 14336
+    return [(d, d), (d, kv), (d, kv), (d, d), (d, ffn), (d, ffn), (ffn, d)] * 32
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_zero1_slices_cover_each_element_once(world):
+    sizes = [50257 * 64, 17, 768, 1, 4097, 3 * 64 * 64]
+    plan = LayoutPlan(sizes, pad_to=16 * world)
+    seen = [np.zeros(n, np.int32) for n in sizes]
+    for r in range(world):
+        lo, hi = shard_bounds(plan.total, world, r)
+        assert lo % 16 == 0 and hi % 16 == 0
+        for i, a, c in shard_segments(plan, lo, hi):
+            seen[i][a:a + c] += 1
+    assert all((s == 1).all() for s in seen)
+
+
+def test_shard_bounds_rejects_unaligned_arena():
+    with pytest.raises(ValueError):
+        shard_bounds(100, 3, 0)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_lpt_balances_llama8b_newton_schulz(world):
+    mats = llama8b_mats()
+    costs = [ns_dense_flops(r, c) for r, c in mats]
+    owner = lpt_assign(costs, world)
+    assert owner == lpt_assign(costs, world)  # deterministic
+    load = [0] * world
+    for i, r in enumerate(owner):
+        load[r] += costs[i]
+    # the 4096x14336 matrices (5.5 TFLOP each) dominate; LPT keeps every rank
+    # within one such matrix of the mean
+    assert max(load) - min(load) <= max(costs)
+    assert max(load) / (sum(load) / world) < 1.05
+
+
+def test_ns_flop_accounting():
+    assert ns_dense_flops(768, 768) == 5 * (4 * 768 ** 3 + 2 * 768 ** 3)
+    assert ns_dense_flops(3072, 768) == ns_dense_flops(768, 3072)
+    total = sum(ns_dense_flops(r, c) for r, c in llama8b_mats())
+    assert abs(total / 1e12 - 665.9) < 0.05
+    # symmetric tiles save work: issued < dense-equivalent for square matrices
+    assert ns_issued_flops(4096, 4096) < ns_dense_flops(4096, 4096)
+
+
+def test_owner_major_layout_is_disjoint_and_aligned():
+    mats = llama8b_mats()[:14]
+    sizes = [r * c for r, c in mats]
+    owner = lpt_assign([ns_dense_flops(r, c) for r, c in mats], 4)
+    offs, extent = owner_major_layout(sizes, owner, 4)
+    spans = sorted((offs[i], offs[i] + sizes[i], owner[i]) for i in range(len(sizes)))
+    for (a0, a1, ra), (b0, b1, rb) in zip(spans, spans[1:]):
+        assert a1 <= b0
+    for i, o in enumerate(offs):
+        assert o % 64 == 0
+        assert owner[i] * extent <= o and o + sizes[i] <= (owner[i] + 1) * extent
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        # ZeRO-1 pointwise part
+        sizes = [1000, 17, 4097, 64]
+        plan = LayoutPlan(sizes, pad_to=16 * world)
+        g = torch.Generator().manual_seed(0)
+        p = torch.randn(plan.total, generator=g, dtype=torch.float64)
+        grad = torch.randn(plan.total, generator=g, dtype=torch.float64)
+        lo, hi = shard_bounds(plan.total, world, rank)
+        local = torch.zeros(1, dtype=torch.float64)
+        for i, a, c in shard_segments(plan, lo, hi):
+            off = plan.slots[i][0] + a
+            local += (grad[off:off + c] ** 2).sum()
+        dist.all_reduce(local)  # f64 sum of squares over ranks
+        mask = torch.zeros(plan.total, dtype=torch.bool)
+        for i, a, c in shard_segments(plan, lo, hi):
+            off = plan.slots[i][0] + a
+            mask[off:off + c] = True
+        new_p = p.clone()
+        new_p[mask] = p[mask] - 0.1 * grad[mask]
+        parts = [torch.empty(hi - lo, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(parts, new_p[lo:hi].contiguous())
+        gathered = torch.cat(parts)
+        # Muon part: owner-major buffer, one gather of equal extents
+        mats = [(64, 96), (96, 64), (32, 32), (128, 64), (16, 48)]
+        msz = [r * c for r, c in mats]
+        owner = lpt_assign([ns_dense_flops(r, c) for r, c in mats], world)
+        offs, extent = owner_major_layout(msz, owner, world)
+        buf = torch.zeros(extent * world, dtype=torch.float64)
+        for i in range(len(mats)):
+            if owner[i] == rank:
+                buf[offs[i]:offs[i] + msz[i]] = float(i + 1)
+        mparts = [torch.empty(extent, dtype=torch.float64) for _ in range(world)]
+        dist.all_gather(mparts, buf[rank * extent:(rank + 1) * extent].contiguous())
+        mfull = torch.cat(mparts)
+        result_q.put((rank, local.item(), gathered.numpy(), mfull.numpy(), offs, msz))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_choreography():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    res.sort(key=lambda x: x[0])
+    sizes = [1000, 17, 4097, 64]
+    plan = LayoutPlan(sizes, pad_to=16 * world)
+    g = torch.Generator().manual_seed(0)
+    p = torch.randn(plan.total, generator=g, dtype=torch.float64)
+    grad = torch.randn(plan.total, generator=g, dtype=torch.float64)
+    want_ss = sum(float((grad[o:o + n] ** 2).sum()) for o, n in plan.slots)
+    want = p.clone()
+    for o, n in plan.slots:
+        want[o:o + n] = p[o:o + n] - 0.1 * grad[o:o + n]
+    for rank, ss, gathered, mfull, offs, msz in res:
+        assert abs(ss - want_ss) <= 1e-12 * want_ss
+        for o, n in plan.slots:
+            np.testing.assert_array_equal(gathered[o:o + n], want[o:o + n].numpy())
+        for i, (o, n) in enumerate(zip(offs, msz)):
+            assert (mfull[o:o + n] == i + 1).all()
+    np.testing.assert_array_equal(res[0][2], res[1][2])

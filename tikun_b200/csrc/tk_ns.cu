@@ -70,27 +70,43 @@ struct GemmArgs {
   int64_t out_ld, out_bs;
   uint16_t* out2;  // GEMM3: X (transposed store)
   int64_t out2_ld, out2_bs;
-  // final iteration: per-matrix destination (NS output or parameter)
-  void* const* fin_ptrs;
-  int fin_dtype;       // TK_F32 / TK_BF16
-  int fin_update;      // 0: store O; 1: p = p + fin_scale * O
-  int fin_transposed;  // 1: O[c][r] (row length fin_ld); 0: O[r][c]
-  int64_t fin_ld;
-  float fin_scale;
   int* err;
+  // final iteration: per-matrix destination (NS output or parameter).  A tall
+  // matrix's output is X_final^T = D itself (O[r][c], row length N); a wide
+  // one's is X_final (O[c][r], row length M).
+  int fin_dtype;   // TK_F32 / TK_BF16
+  int fin_update;  // 0: store O; 1: p = p + scale * O
+  float fin_scale_wide, fin_scale_tall;
+  uint64_t fin_tall[kMaxBatch / 64];
+  void* fin_ptrs[kMaxBatch];
 };
 
+__device__ __forceinline__ bool bit_of(const uint64_t* mask, int b) {
+  return (mask[b >> 6] >> (b & 63)) & 1ull;
+}
+
 // ------------------------------------------------------------------ helpers
+// bf16 <-> f32 by bit manipulation: a raw 16-bit load followed by a shift keeps
+// independent loads free to overlap (no conversion intrinsic in between).
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);  // quiet NaN
+  u += 0x7fffu + ((u >> 16) & 1u);                                           // nearest even
+  return (uint16_t)(u >> 16);
+}
+
 template <int FMT>
 __device__ __forceinline__ uint16_t to_half_bits(float x) {
   if constexpr (FMT == 0) return __half_as_ushort(__float2half_rn(x));
-  else return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  else return f32_to_bf16_bits(x);
 }
 
 template <int FMT>
 __device__ __forceinline__ float from_half_bits(uint16_t h) {
   if constexpr (FMT == 0) return __half2float(__ushort_as_half(h));
-  else return __bfloat162float(__ushort_as_bfloat16(h));
+  else return bf16_bits_to_f32(h);
 }
 
 __device__ __forceinline__ void decode_tile(const GemmArgs& a, int t, int& b, int& tm, int& tn) {
@@ -222,20 +238,36 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
         if (c0 + j < a.N) d2[(int64_t)(c0 + j) * a.out2_ld + r] = hb[j];
     } else {
       void* dst = a.fin_ptrs[b];
+      const bool tall = bit_of(a.fin_tall, b);
+      const float scale = tall ? a.fin_scale_tall : a.fin_scale_wide;
+      // all 32 parameter loads are issued before any store, so their
+      // latencies overlap instead of serialising behind possible aliasing
+      int64_t idx[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (!(c0 + j < a.N)) continue;
-        const int64_t idx = a.fin_transposed ? (int64_t)(c0 + j) * a.fin_ld + r
-                                             : (int64_t)r * a.fin_ld + c0 + j;
-        if (a.fin_dtype == TK_F32) {
-          float* p = static_cast<float*>(dst) + idx;
-          *p = a.fin_update ? __fadd_rn(*p, __fmul_rn(a.fin_scale, o[j])) : o[j];
-        } else {
-          __nv_bfloat16* p = static_cast<__nv_bfloat16*>(dst) + idx;
-          const float cur = a.fin_update ? __bfloat162float(*p) : 0.f;
-          *p = __float2bfloat16_rn(a.fin_update ? __fadd_rn(cur, __fmul_rn(a.fin_scale, o[j]))
-                                                : o[j]);
+      for (int j = 0; j < 32; ++j)
+        idx[j] = tall ? (int64_t)r * a.N + c0 + j : (int64_t)(c0 + j) * a.M + r;
+      if (a.fin_dtype == TK_F32) {
+        float* p = static_cast<float*>(dst);
+        float cur[32];
+        if (a.fin_update) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) cur[j] = (c0 + j < a.N) ? p[idx[j]] : 0.f;
         }
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < a.N) p[idx[j]] = a.fin_update ? __fadd_rn(cur[j], __fmul_rn(scale, o[j])) : o[j];
+      } else {
+        uint16_t* p = static_cast<uint16_t*>(dst);
+        uint32_t raw[32];
+        if (a.fin_update) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) raw[j] = (c0 + j < a.N) ? p[idx[j]] : 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < a.N)
+            p[idx[j]] = f32_to_bf16_bits(
+                a.fin_update ? __fadd_rn(bf16_bits_to_f32(raw[j]), __fmul_rn(scale, o[j])) : o[j]);
       }
     }
   }
@@ -245,7 +277,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
 template <int EPI, int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const GemmArgs args) {
+               const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -397,27 +429,74 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ------------------------------------------------------------------ prologue
+template <int SDT>
+__device__ __forceinline__ float load_src1(const void* src, int64_t i) {
+  if constexpr (SDT == TK_F32) return static_cast<const float*>(src)[i];
+  else return bf16_bits_to_f32(static_cast<const uint16_t*>(src)[i]);
+}
+
+template <int SDT>
+__device__ __forceinline__ void load_src4(const void* src, int64_t i, float (&g)[4]) {
+  if constexpr (SDT == TK_F32) {
+    const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + i);
+    g[0] = v.x; g[1] = v.y; g[2] = v.z; g[3] = v.w;
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(src) + i);
+    g[0] = bf16_bits_to_f32(v.x & 0xffffu); g[1] = bf16_bits_to_f32(v.x >> 16);
+    g[2] = bf16_bits_to_f32(v.y & 0xffffu); g[3] = bf16_bits_to_f32(v.y >> 16);
+  }
+}
+
+// python/tikun/muon_nd.py:112-115 in f32: buf = mu*buf + om*g; u = mu*buf + om*g
+__device__ __forceinline__ float muon_u(const PrepArgs& a, float& buf, float g) {
+  buf = __fadd_rn(__fmul_rn(a.mu, buf), __fmul_rn(a.om, g));
+  return a.nesterov ? __fadd_rn(__fmul_rn(a.mu, buf), __fmul_rn(a.om, g)) : buf;
+}
+
 // Pass 1: per matrix, optional Muon momentum update, f64 sum of squares of the
-// matrix handed to Newton-Schulz.  grid (nblk, batch).
+// matrix handed to Newton-Schulz.  grid (nblk, batch); each block takes an
+// equal range of 4-element groups (128-bit momentum accesses).
 template <int SDT, bool MUON>
 __global__ void __launch_bounds__(256)
-prep_stats_kernel(const PrepArgs a, double* __restrict__ partials) {
+prep_stats_kernel(const __grid_constant__ PrepArgs a, double* __restrict__ partials) {
   const int b = blockIdx.y;
-  const int64_t total = a.rows * a.cols;
-  const int64_t chunk = (total + gridDim.x - 1) / gridDim.x;
-  const int64_t lo = blockIdx.x * chunk, hi = min(total, lo + chunk);
+  const int64_t total = a.m * a.n;
   const void* src = a.src[b];
   float* mom = MUON ? a.mom[b] : nullptr;
+  const bool vec = ((uintptr_t)src % (SDT == TK_F32 ? 16 : 8)) == 0 &&
+                   (!MUON || ((uintptr_t)mom % 16) == 0);
+  const int64_t groups = vec ? total / 4 : 0;
+  const int64_t g0 = groups * blockIdx.x / gridDim.x, g1 = groups * (blockIdx.x + 1) / gridDim.x;
   double s = 0.0;
-  for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-    const float g = SDT == TK_F32 ? static_cast<const float*>(src)[i]
-                                  : __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i]);
+  for (int64_t q = g0 + threadIdx.x; q < g1; q += blockDim.x) {
+    float g[4];
+    load_src4<SDT>(src, q * 4, g);
+    float u[4];
+    if constexpr (MUON) {
+      float4 m4 = *reinterpret_cast<float4*>(mom + q * 4);
+      float bb[4] = {m4.x, m4.y, m4.z, m4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) u[j] = muon_u(a, bb[j], g[j]);
+      *reinterpret_cast<float4*>(mom + q * 4) = make_float4(bb[0], bb[1], bb[2], bb[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) u[j] = g[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s = fma((double)u[j], (double)u[j], s);
+  }
+  // elements past the last whole group (or all of them when unaligned),
+  // split over the blocks the same way
+  const int64_t rest0 = groups * 4, rest = total - rest0;
+  const int64_t e0 = rest0 + rest * blockIdx.x / gridDim.x;
+  const int64_t e1 = rest0 + rest * (blockIdx.x + 1) / gridDim.x;
+  for (int64_t i = e0 + threadIdx.x; i < e1; i += blockDim.x) {
+    const float g = load_src1<SDT>(src, i);
     float u = g;
     if constexpr (MUON) {
-      // python/tikun/muon_nd.py:112-115 in f32: buf = mu*buf + om*g; u = mu*buf + om*g
-      const float buf = __fadd_rn(__fmul_rn(a.mu, mom[i]), __fmul_rn(a.om, g));
-      mom[i] = buf;
-      u = a.nesterov ? __fadd_rn(__fmul_rn(a.mu, buf), __fmul_rn(a.om, g)) : buf;
+      float bb = mom[i];
+      u = muon_u(a, bb, g);
+      mom[i] = bb;
     }
     s = fma((double)u, (double)u, s);
   }
@@ -433,82 +512,94 @@ prep_stats_kernel(const PrepArgs a, double* __restrict__ partials) {
   }
 }
 
-// Pass 2: normalise (tensor_engine.rs:37-44: x * 1/max(||U||, 1e-7) in f32),
+// Per matrix: 1 / max(||U||_F, 1e-7) in f32 (tensor_engine.rs:37-41) from the
+// f64 partial sums, in a fixed order.  grid (batch), block 32.
+__global__ void __launch_bounds__(32)
+prep_scale_kernel(const double* __restrict__ partials, int nblk, float* __restrict__ scales) {
+  double s = 0.0;
+  for (int i = threadIdx.x; i < nblk; i += 32) s += partials[(int64_t)blockIdx.x * nblk + i];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_down_sync(0xffffffffu, s, off);
+  if (threadIdx.x == 0) {
+    const float nrm = __double2float_rn(sqrt(s));
+    scales[blockIdx.x] = __fdiv_rn(1.0f, fmaxf(nrm, 1e-7f));
+  }
+}
+
+// Pass 2: normalise (x * 1/max(||U||, 1e-7) in f32, tensor_engine.rs:42-44),
 // pre-scale by 2^k, round to the operand type and write X (m x n) and X^T
-// (n x m) through a 32x32 shared-memory transpose.  grid (ceil(C/32),
-// ceil(R/32), batch), block (32, 8).  With steps == 0 it writes the output
-// (or applies the update) instead.
+// (n x m) through a 32x32 shared-memory transpose.  The input G is R x C
+// (m x n for a wide matrix, n x m for a tall one); grid (ceil(m/32) *
+// ceil(n/32), 1, batch) covers G's 32x32 tiles, block (32, 8).  With
+// steps == 0 it writes the output (or applies the update) instead.
 template <int SDT, bool MUON, int FMT>
 __global__ void __launch_bounds__(256)
-prep_write_kernel(const PrepArgs a, const double* __restrict__ partials, int nblk) {
-  __shared__ float s_scale;
+prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ scales) {
   __shared__ uint16_t tile[32][33];
   const int b = blockIdx.z;
-  const int tid = threadIdx.y * 32 + threadIdx.x;
-  {
-    double s = 0.0;
-    for (int i = tid; i < nblk; i += 256) s += partials[(int64_t)b * nblk + i];
-    __shared__ double red[8];
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) s += __shfl_down_sync(0xffffffffu, s, off);
-    if ((tid & 31) == 0) red[tid >> 5] = s;
-    __syncthreads();
-    if (tid == 0) {
-      double t = 0.0;
-      for (int w = 0; w < 8; ++w) t += red[w];
-      const float nrm = __double2float_rn(sqrt(t));
-      s_scale = __fdiv_rn(1.0f, fmaxf(nrm, 1e-7f));
-    }
-    __syncthreads();
-  }
-  const float inv = s_scale;
+  const float inv = __ldg(scales + b);
+  const bool tall = (a.tall[b >> 6] >> (b & 63)) & 1ull;  // G = X^T
+  const int64_t rows = tall ? a.n : a.m, cols = tall ? a.m : a.n;
+  const int64_t tiles_c = (cols + 31) / 32;
+  const int64_t tr = blockIdx.x / tiles_c, tc = blockIdx.x - tr * tiles_c;
   const void* src = a.src[b];
   const float* mom = MUON ? a.mom[b] : nullptr;
-  const int c = blockIdx.x * 32 + threadIdx.x;
-  const bool tall = a.rows > a.cols;  // X = G^T
+  const int64_t c = tc * 32 + threadIdx.x;
+  float x[4];
+  bool in[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int r = blockIdx.y * 32 + threadIdx.y + 8 * k;
-    float x = 0.f;
-    if (r < a.rows && c < a.cols) {
-      const int64_t i = (int64_t)r * a.cols + c;
-      const float g = SDT == TK_F32 ? static_cast<const float*>(src)[i]
-                                    : __bfloat162float(static_cast<const __nv_bfloat16*>(src)[i]);
+  for (int k = 0; k < 4; ++k) {  // loads first, so they overlap
+    const int64_t r = tr * 32 + threadIdx.y + 8 * k;
+    in[k] = r < rows && c < cols;
+    x[k] = 0.f;
+    if (in[k]) {
+      const int64_t i = r * cols + c;
+      const float g = load_src1<SDT>(src, i);
       float u = g;
       if constexpr (MUON) {
         const float buf = mom[i];
         u = a.nesterov ? __fadd_rn(__fmul_rn(a.mu, buf), __fmul_rn(a.om, g)) : buf;
       }
-      x = __fmul_rn(u, inv);
-      if (a.steps == 0) {
-        void* dst = a.dst[b];
-        if (a.dst_dtype == TK_F32) {
-          float* p = static_cast<float*>(dst) + i;
-          *p = a.update ? __fadd_rn(*p, __fmul_rn(a.upd_scale, x)) : x;
-        } else {
-          __nv_bfloat16* p = static_cast<__nv_bfloat16*>(dst) + i;
-          *p = __float2bfloat16_rn(a.update ? __fadd_rn(__bfloat162float(*p), __fmul_rn(a.upd_scale, x)) : x);
-        }
-        continue;
-      }
-      // same-layout target: X (wide) or X^T (tall); row length of G is cols
-      uint16_t* same = tall ? a.xt + (int64_t)b * a.xt_bs : a.x + (int64_t)b * a.x_bs;
-      const int64_t same_ld = tall ? a.xt_ld : a.x_ld;
-      const uint16_t h = to_half_bits<FMT>(__fmul_rn(x, a.prescale));
-      same[(int64_t)r * same_ld + c] = h;
-      tile[threadIdx.y + 8 * k][threadIdx.x] = h;
+      x[k] = __fmul_rn(u, inv);
     }
   }
-  if (a.steps == 0) return;
+  if (a.steps == 0) {
+    void* dst = a.dst[b];
+    const float sc = tall ? a.upd_scale_tall : a.upd_scale_wide;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (!in[k]) continue;
+      const int64_t i = (tr * 32 + threadIdx.y + 8 * k) * cols + c;
+      if (a.dst_dtype == TK_F32) {
+        float* p = static_cast<float*>(dst) + i;
+        *p = a.update ? __fadd_rn(*p, __fmul_rn(sc, x[k])) : x[k];
+      } else {
+        uint16_t* p = static_cast<uint16_t*>(dst) + i;
+        *p = f32_to_bf16_bits(a.update ? __fadd_rn(bf16_bits_to_f32(*p), __fmul_rn(sc, x[k])) : x[k]);
+      }
+    }
+    return;
+  }
+  // same-layout target: X (wide) or X^T (tall)
+  uint16_t* same = tall ? a.xt + (int64_t)b * a.xt_bs : a.x + (int64_t)b * a.x_bs;
+  const int64_t same_ld = tall ? a.xt_ld : a.x_ld;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    if (!in[k]) continue;
+    const int64_t r = tr * 32 + threadIdx.y + 8 * k;
+    const uint16_t h = to_half_bits<FMT>(__fmul_rn(x[k], a.prescale));
+    same[r * same_ld + c] = h;
+    tile[threadIdx.y + 8 * k][threadIdx.x] = h;
+  }
   __syncthreads();
   // transposed target: element (r, c) of G goes to row c, column r
   uint16_t* other = tall ? a.x + (int64_t)b * a.x_bs : a.xt + (int64_t)b * a.xt_bs;
   const int64_t other_ld = tall ? a.x_ld : a.xt_ld;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int cc = blockIdx.x * 32 + threadIdx.y + 8 * k;  // row of the target
-    const int rr = blockIdx.y * 32 + threadIdx.x;           // column of the target
-    if (cc < a.cols && rr < a.rows) other[(int64_t)cc * other_ld + rr] = tile[threadIdx.x][threadIdx.y + 8 * k];
+    const int64_t cc = tc * 32 + threadIdx.y + 8 * k;  // row of the target
+    const int64_t rr = tr * 32 + threadIdx.x;           // column of the target
+    if (cc < cols && rr < rows) other[cc * other_ld + rr] = tile[threadIdx.x][threadIdx.y + 8 * k];
   }
 }
 
@@ -599,23 +690,20 @@ static int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
-GroupLayout group_layout(int64_t rows, int64_t cols, int64_t batch) {
+GroupLayout group_layout(int64_t m, int64_t n, int64_t batch) {
   GroupLayout L;
-  L.R = rows;
-  L.C = cols;
-  L.tall = rows > cols;
-  L.m = std::min(rows, cols);
-  L.n = std::max(rows, cols);
+  L.m = m;
+  L.n = n;
   L.batch = batch;
   L.ldx = round_up(L.n, 64);
   L.ldm = round_up(L.m, 64);
   L.x_bytes = align256((size_t)(batch * L.m * L.ldx * 2));
   L.xt_bytes = align256((size_t)(batch * L.n * L.ldm * 2));
   L.a_bytes = align256((size_t)(batch * L.m * L.ldm * 2));
-  L.nblk = (int)std::max<int64_t>(1, std::min<int64_t>(64, (rows * cols + 65535) / 65536));
+  L.nblk = (int)std::max<int64_t>(1, std::min<int64_t>(256, (m * n + 16383) / 16384));
   L.scratch_bytes = L.x_bytes + 2 * L.xt_bytes + 2 * L.a_bytes +
-                    align256(sizeof(double) * batch * L.nblk) +
-                    align256(sizeof(void*) * batch * 3) + 256;
+                    align256(sizeof(double) * batch * L.nblk) + align256(sizeof(float) * batch) +
+                    256;
   return L;
 }
 
@@ -631,6 +719,7 @@ static int prescale_exp(int fmt, int64_t m, int64_t n) {
 int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void* scratch,
               int* err_dev, cudaStream_t s) {
   if (L.batch == 0 || L.m == 0) return TK_OK;
+  if (L.batch > kMaxBatch) return set_error(TK_ERR_INVALID, "batch of %lld > %d", (long long)L.batch, kMaxBatch);
   char* cur = static_cast<char*>(scratch);
   uint16_t* X = reinterpret_cast<uint16_t*>(cur);
   cur += L.x_bytes;
@@ -643,25 +732,20 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   cur += L.a_bytes;
   double* partials = reinterpret_cast<double*>(cur);
   cur += align256(sizeof(double) * L.batch * L.nblk);
-  void** ptrs = reinterpret_cast<void**>(cur);  // src[batch], dst[batch], mom[batch]
-
-  std::vector<void*> host_ptrs(3 * L.batch);
-  for (int64_t i = 0; i < L.batch; ++i) {
-    host_ptrs[i] = const_cast<void*>(io.src[i]);
-    host_ptrs[L.batch + i] = io.dst[i];
-    host_ptrs[2 * L.batch + i] = io.mom ? io.mom[i] : nullptr;
-  }
-  TK_CUDA_TRY(cudaMemcpyAsync(ptrs, host_ptrs.data(), sizeof(void*) * host_ptrs.size(),
-                              cudaMemcpyHostToDevice, s));
+  float* scales = reinterpret_cast<float*>(cur);
 
   const int k = prescale_exp(fmt, L.m, L.n);
-  PrepArgs pa;
+  // kernel parameters carry the per-matrix pointers and orientation bits
+  static thread_local PrepArgs pa;
   std::memset(&pa, 0, sizeof(pa));
-  pa.src = reinterpret_cast<const void* const*>(ptrs);
-  pa.dst = ptrs + L.batch;
-  pa.mom = reinterpret_cast<float* const*>(ptrs + 2 * L.batch);
-  pa.rows = L.R;
-  pa.cols = L.C;
+  for (int64_t i = 0; i < L.batch; ++i) {
+    pa.src[i] = io.src[i];
+    pa.dst[i] = io.dst[i];
+    pa.mom[i] = io.mom ? io.mom[i] : nullptr;
+    if (io.tall[i]) pa.tall[i >> 6] |= 1ull << (i & 63);
+  }
+  pa.m = L.m;
+  pa.n = L.n;
   pa.mu = io.mu;
   pa.om = io.om;
   pa.nesterov = io.nesterov;
@@ -675,7 +759,8 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   pa.steps = steps;
   pa.dst_dtype = io.dst_dtype;
   pa.update = io.update;
-  pa.upd_scale = io.upd_scale;
+  pa.upd_scale_wide = io.upd_scale_wide;
+  pa.upd_scale_tall = io.upd_scale_tall;
 
   const bool muon = io.mom != nullptr;
   {
@@ -688,9 +773,11 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       else prep_stats_kernel<TK_BF16, false><<<g1, 256, 0, s>>>(pa, partials);
     }
     TK_CUDA_TRY(cudaGetLastError());
-    dim3 g2((unsigned)((L.C + 31) / 32), (unsigned)((L.R + 31) / 32), (unsigned)L.batch);
+    prep_scale_kernel<<<(unsigned)L.batch, 32, 0, s>>>(partials, L.nblk, scales);
+    TK_CUDA_TRY(cudaGetLastError());
+    dim3 g2((unsigned)(((L.m + 31) / 32) * ((L.n + 31) / 32)), 1, (unsigned)L.batch);
     dim3 b2(32, 8);
-#define TK_PREP_WRITE(SDT, MU, F) prep_write_kernel<SDT, MU, F><<<g2, b2, 0, s>>>(pa, partials, L.nblk)
+#define TK_PREP_WRITE(SDT, MU, F) prep_write_kernel<SDT, MU, F><<<g2, b2, 0, s>>>(pa, scales)
     if (io.src_dtype == TK_F32) {
       if (muon) { if (fmt == 0) TK_PREP_WRITE(TK_F32, true, 0); else TK_PREP_WRITE(TK_F32, true, 1); }
       else { if (fmt == 0) TK_PREP_WRITE(TK_F32, false, 0); else TK_PREP_WRITE(TK_F32, false, 1); }
@@ -716,8 +803,8 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   const int tm_x = (int)((L.n + BM - 1) / BM);
   const float inv_pre = std::ldexp(1.0f, -k), inv_pre2 = std::ldexp(1.0f, -2 * k);
   int cur_xt = 0;
+  static thread_local GemmArgs g, h;
   for (int it = 0; it < steps; ++it) {
-    GemmArgs g;
     std::memset(&g, 0, sizeof(g));
     g.batch = (int)L.batch;
     g.err = err_dev;
@@ -743,7 +830,6 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     g.out = Bm;
     TK_TRY(launch_gemm_epi(EPI_POLY, fmt, mA128, mA256, g, s));
     // GEMM3: X_new^T = post (a X^T + X^T B)
-    GemmArgs h;
     std::memset(&h, 0, sizeof(h));
     h.batch = (int)L.batch;
     h.err = err_dev;
@@ -770,13 +856,14 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       TK_TRY(launch_gemm_epi(EPI_XUPD, fmt, mXT128[cur_xt], mB256, h, s));
       cur_xt ^= 1;
     } else {
-      h.fin_ptrs = ptrs + L.batch;
       h.fin_dtype = io.dst_dtype;
       h.fin_update = io.update;
-      h.fin_scale = io.upd_scale;
-      // D[r][c] = X_final^T[r][c]; a wide input's output is X_final: O[c][r]
-      h.fin_transposed = L.tall ? 0 : 1;
-      h.fin_ld = L.C;
+      h.fin_scale_wide = io.upd_scale_wide;
+      h.fin_scale_tall = io.upd_scale_tall;
+      for (int64_t i = 0; i < L.batch; ++i) {
+        h.fin_ptrs[i] = io.dst[i];
+        h.fin_tall[i >> 6] = pa.tall[i >> 6];
+      }
       TK_TRY(launch_gemm_epi(EPI_FINAL, fmt, mXT128[cur_xt], mB256, h, s));
     }
   }
@@ -792,7 +879,7 @@ int plain_gemm(const uint16_t* P, const uint16_t* Q, uint16_t* D, int batch, int
   CUtensorMap ma, mb;
   TK_TRY(make_map(&ma, P, fmt, K, M, ldp, batch, 128));
   TK_TRY(make_map(&mb, Q, fmt, K, N, ldq, batch, 256));
-  GemmArgs g;
+  static thread_local GemmArgs g;
   std::memset(&g, 0, sizeof(g));
   g.M = M;
   g.N = N;

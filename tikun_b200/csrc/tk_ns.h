@@ -10,37 +10,43 @@
 namespace tk {
 namespace ns {
 
-// Scratch layout of one batch of same-shape matrices (R x C each; m = min,
-// n = max; X is m x n, X^T is n x m, A and B are m x m, all half precision
-// with rows padded to a multiple of 64 elements).
+// Matrices per batch (one launch sequence).  Their pointers travel in the
+// kernels' parameter space, so a batch needs no device-side table.
+constexpr int kMaxBatch = 256;
+
+// Scratch layout of one batch of matrices that are all m x n or n x m
+// (m <= n): X is m x n, X^T is n x m, A and B are m x m, all half precision
+// with rows padded to a multiple of 64 elements.
 struct GroupLayout {
-  int64_t R, C, m, n, batch;
-  bool tall;
+  int64_t m, n, batch;
   int64_t ldx, ldm;
   size_t x_bytes, xt_bytes, a_bytes;
   int nblk;
   size_t scratch_bytes;
 };
 
-GroupLayout group_layout(int64_t rows, int64_t cols, int64_t batch);
+GroupLayout group_layout(int64_t m, int64_t n, int64_t batch);
 
-// Inputs and outputs of one batch (host arrays of device pointers).
+// Inputs and outputs of one batch (host arrays of device pointers, length
+// batch <= kMaxBatch).  A "tall" matrix is stored n x m (rows > cols).
 struct GroupIO {
   const void* const* src;  // NS input, or the Muon gradient
   void* const* dst;        // NS output (may equal src), or the Muon parameter
   float* const* mom;       // Muon momentum (f32), or nullptr for plain NS
+  const uint8_t* tall;
   int src_dtype, dst_dtype;
-  int update;              // 0: dst = O;  1: dst = dst + upd_scale * O
-  float upd_scale;
+  int update;              // 0: dst = O;  1: dst = dst + scale * O
+  float upd_scale_wide, upd_scale_tall;
   float mu, om;            // momentum and (1 - momentum) in f32
   int nesterov;
 };
 
 struct PrepArgs {
-  const void* const* src;
-  void* const* dst;
-  float* const* mom;
-  int64_t rows, cols;
+  const void* src[kMaxBatch];
+  void* dst[kMaxBatch];
+  float* mom[kMaxBatch];
+  uint64_t tall[kMaxBatch / 64];
+  int64_t m, n;
   float mu, om;
   int nesterov;
   uint16_t* x;
@@ -51,7 +57,7 @@ struct PrepArgs {
   int steps;
   int dst_dtype;
   int update;
-  float upd_scale;
+  float upd_scale_wide, upd_scale_tall;
 };
 
 // Enqueues the whole iteration for one batch on stream s.  scratch holds

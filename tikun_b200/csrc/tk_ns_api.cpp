@@ -45,30 +45,35 @@ static int check_status(cudaStream_t s) {
   return TK_OK;
 }
 
-// Runs NS over `count` same-shape matrices in waves that fit the scratch budget.
-static int run_batches(int64_t rows, int64_t cols, const std::vector<const void*>& src,
+// Runs NS over matrices that are all m x n or n x m, in waves that fit the
+// scratch budget and the per-launch pointer capacity.
+static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src,
                        const std::vector<void*>& dst, const std::vector<float*>* mom,
-                       int src_dtype, int dst_dtype, int update, float upd_scale, float mu,
-                       float om, int nesterov, int steps, int fmt, cudaStream_t s) {
+                       const std::vector<uint8_t>& tall, int src_dtype, int dst_dtype, int update,
+                       float scale_wide, float scale_tall, float mu, float om, int nesterov,
+                       int steps, int fmt, cudaStream_t s) {
   const int64_t count = (int64_t)src.size();
-  const ns::GroupLayout one = ns::group_layout(rows, cols, 1);
-  const int64_t per_wave =
-      std::max<int64_t>(1, std::min<int64_t>(count, (int64_t)(ns_scratch_budget() / one.scratch_bytes)));
+  const ns::GroupLayout one = ns::group_layout(m, n, 1);
+  const int64_t per_wave = std::max<int64_t>(
+      1, std::min<int64_t>({count, (int64_t)(ns_scratch_budget() / one.scratch_bytes),
+                            (int64_t)ns::kMaxBatch}));
   int* status = nullptr;
   TK_TRY(device_status_word(&status));
   for (int64_t first = 0; first < count; first += per_wave) {
     const int64_t nb = std::min(per_wave, count - first);
-    const ns::GroupLayout L = ns::group_layout(rows, cols, nb);
+    const ns::GroupLayout L = ns::group_layout(m, n, nb);
     Scratch scratch;
     TK_TRY(scratch.alloc(L.scratch_bytes, s));
     ns::GroupIO io;
     io.src = src.data() + first;
     io.dst = dst.data() + first;
     io.mom = mom ? mom->data() + first : nullptr;
+    io.tall = tall.data() + first;
     io.src_dtype = src_dtype;
     io.dst_dtype = dst_dtype;
     io.update = update;
-    io.upd_scale = upd_scale;
+    io.upd_scale_wide = scale_wide;
+    io.upd_scale_tall = scale_tall;
     io.mu = mu;
     io.om = om;
     io.nesterov = nesterov;
@@ -105,11 +110,13 @@ static int ns_entry(void* base, int64_t heads, int64_t rows, int64_t cols, int32
   }
   std::vector<const void*> src(heads);
   std::vector<void*> dst(heads);
+  std::vector<uint8_t> tall(heads, rows > cols ? 1 : 0);
   for (int64_t h = 0; h < heads; ++h) {
     dst[h] = dbase + (size_t)h * rows * cols * esz;
     src[h] = dst[h];
   }
-  TK_TRY(run_batches(rows, cols, src, dst, nullptr, dtype, dtype, 0, 0.f, 0.f, 0.f, 0, steps, fmt, s));
+  TK_TRY(run_batches(std::min(rows, cols), std::max(rows, cols), src, dst, nullptr, tall, dtype,
+                     dtype, 0, 0.f, 0.f, 0.f, 0.f, 0, steps, fmt, s));
   if (where == Residency::kHost)
     TK_CUDA_TRY(cudaMemcpyAsync(base, dbase, bytes, cudaMemcpyDeviceToHost, s));
   return check_status(s);
@@ -156,6 +163,7 @@ int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hpar
     std::vector<const void*> g;
     std::vector<void*> p;
     std::vector<float*> mom;
+    std::vector<uint8_t> tall;
   };
   std::map<std::tuple<int64_t, int64_t, int, int>, Batch> groups;
   for (size_t i = 0; i < n_leaves; ++i) {
@@ -178,12 +186,15 @@ int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hpar
       if (r != Residency::kDevice)
         return set_error(TK_ERR_INVALID, "leaf %zu: tk_muon_step takes device buffers", i);
     }
-    Batch& b = groups[std::make_tuple(L.rows, L.cols, L.p_dtype, L.g_dtype)];
+    // an m x n and an n x m matrix share one batch (m = min, n = max)
+    Batch& b = groups[std::make_tuple(std::min(L.rows, L.cols), std::max(L.rows, L.cols),
+                                      L.p_dtype, L.g_dtype)];
     const size_t mat = (size_t)L.rows * L.cols;
     for (int64_t h = 0; h < heads; ++h) {
       b.g.push_back(static_cast<const char*>(L.g) + h * mat * dt_size(L.g_dtype));
       b.p.push_back(static_cast<char*>(L.p) + h * mat * dt_size(L.p_dtype));
       b.mom.push_back(L.momentum + h * mat);
+      b.tall.push_back(L.rows > L.cols ? 1 : 0);
     }
   }
   std::sort(ranges.begin(), ranges.end(), [](const Range& a, const Range& b) { return a.lo < b.lo; });
@@ -200,12 +211,13 @@ int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hpar
   const float mu = (float)hp->momentum;
   const float om = (float)(1.0 - hp->momentum);
   for (auto& kv : groups) {
-    const int64_t rows = std::get<0>(kv.first), cols = std::get<1>(kv.first);
+    const int64_t m = std::get<0>(kv.first), n = std::get<1>(kv.first);
     const int pdt = std::get<2>(kv.first), gdt = std::get<3>(kv.first);
-    const double scale = std::sqrt(std::max(1.0, (double)rows / (double)cols));
-    const float upd = (float)(-hp->lr * scale);
-    TK_TRY(run_batches(rows, cols, kv.second.g, kv.second.p, &kv.second.mom, gdt, pdt, 1, upd, mu,
-                       om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s));
+    // rows/cols is m/n (<= 1) for a wide matrix and n/m for a tall one
+    const float upd_wide = (float)(-hp->lr * std::sqrt(std::max(1.0, (double)m / (double)n)));
+    const float upd_tall = (float)(-hp->lr * std::sqrt(std::max(1.0, (double)n / (double)m)));
+    TK_TRY(run_batches(m, n, kv.second.g, kv.second.p, &kv.second.mom, kv.second.tall, gdt, pdt,
+                       1, upd_wide, upd_tall, mu, om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s));
   }
   return TK_OK;
 }
