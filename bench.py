@@ -314,9 +314,14 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
             _native.check(L.tk_clip_scale(sumsq.data_ptr(), wl["max_norm"], scale_dev.data_ptr(),
                                           s_handle))
             launches += 3
+        k = state.get("k")
+        if k is not None:
+            ev_pairs[k][0].record(stream)
         _native.check(L.tk_apply_pointwise(leaves, n_leaves, _native.TK_ADAMW, ctypes.byref(hp),
                                            state["step"], scale_dev.data_ptr() if clip else None,
                                            s_handle))
+        if k is not None:
+            ev_pairs[k][1].record(stream)
         dist.all_gather_into_tensor(P.flat, P.flat[lo:hi])
         return launches + 1
 
@@ -327,12 +332,16 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         b.record(stream)
 
     def before(k):
-        state["ev"] = (ev_pairs[k][0].cuda_event, ev_pairs[k][1].cuda_event)
+        if world == 1:  # the library records them around its update launches
+            state["ev"] = (ev_pairs[k][0].cuda_event, ev_pairs[k][1].cuda_event)
+        else:
+            state["k"] = k
 
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
     ms_total, launches, clocks = timed_loop(one_step, args.steps, args.warmup, stream, world, dist,
                                             dev, torch, uuid, before)
     state["ev"] = None
+    state["k"] = None
     _native.check(L.tk_set_update_events(None, None))
     upd_ms = sum(a.elapsed_time(b) for a, b in ev_pairs) / args.steps
     ms_step = ms_total / args.steps
@@ -375,7 +384,8 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         e2e = {"value": n_params / (e_ms / 1e3), "unit": "params/s", "ms_per_step": e_ms,
                "h2d_bytes_per_step": 16 * n_params, "d2h_bytes_per_step": 12 * n_params + 4,
                "steps": e2e_steps, "host_memory": "pinned",
-               "api": "tk_step_buffers with host leaves (copies inside the call)"}
+               "api": "tk_step_buffers with pinned host leaves: g copied to HBM for the clip, "
+                      "p/m/v streamed over the host link by the update kernel"}
         del hp_pin, hg_pin, hm_pin, hv_pin
 
     cpu = None

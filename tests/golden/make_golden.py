@@ -141,6 +141,43 @@ def frontend_reference(tikun) -> dict:
         opt.step()
     for k, v in mparams.items():
         out[f"muon_nd/final/{k}"] = v.detach().numpy().copy()
+
+    # In-backward AdamW (universal.py:97-137): each leaf steps from its
+    # post-accumulate-grad hook, clip per leaf, step numbering read before
+    # step() increments it.  The loss sum(w1^2) + sum(w2 * c2) has gradients
+    # 2*w1 and c2, which every device computes exactly.
+    g1 = torch.Generator().manual_seed(17)
+    w1 = (torch.randn(37, generator=g1) * 0.5).requires_grad_(True)
+    w2 = (torch.randn(5, 7, generator=g1) * 0.5).requires_grad_(True)
+    c2 = torch.randn(5, 7, generator=g1)
+    out["inbwd/init/w1"] = w1.detach().numpy().copy()
+    out["inbwd/init/w2"] = w2.detach().numpy().copy()
+    out["inbwd/c2"] = c2.numpy().copy()
+    opt = tikun.AdamW([w1, w2], lr=1e-2, max_norm=1.0, in_backward=True)
+    for _ in range(4):
+        loss = (w1 * w1).sum() + (w2 * c2).sum()
+        loss.backward()
+        opt.step()
+    out["inbwd/final/w1"] = w1.detach().numpy().copy()
+    out["inbwd/final/w2"] = w2.detach().numpy().copy()
+
+    # tikun.Muon (muon.py:34-102): EMA momentum without Nesterov, torch f32 NS,
+    # scale sqrt(max(1, r/c)); AdamW (betas 0.9/0.95, decay 0.1) on the rest.
+    g2 = torch.Generator().manual_seed(23)
+    mw = (torch.randn(64, 96, generator=g2) * 0.02).requires_grad_(True)
+    mt = (torch.randn(80, 48, generator=g2) * 0.02).requires_grad_(True)
+    mb = torch.zeros(96).requires_grad_(True)
+    for k, v in (("w", mw), ("t", mt), ("b", mb)):
+        out[f"muon/init/{k}"] = v.detach().numpy().copy()
+    opt = tikun.Muon(muon_params=[mw, mt], adamw_params=[mb], lr=0.02, momentum=0.95,
+                     adamw_lr=1e-3)
+    for s in range(3):
+        for k, v in (("w", mw), ("t", mt), ("b", mb)):
+            v.grad = torch.randn(v.shape, generator=g2) * 1e-3
+            out[f"muon/grad{s}/{k}"] = v.grad.numpy().copy()
+        opt.step()
+    for k, v in (("w", mw), ("t", mt), ("b", mb)):
+        out[f"muon/final/{k}"] = v.detach().numpy().copy()
     return out
 
 

@@ -229,3 +229,40 @@ def test_muon_nd_frontend_matches_reference_frontend(golden_dir):
         d_ref = z[f"muon_nd/final/{k}"] - init
         d_got = to_np(params[k]) - init
         assert relf(d_got, d_ref) <= 5e-3, k
+
+
+def test_muon_frontend_matches_reference_frontend(golden_dir):
+    """tikun_b200.Muon against the reference's Muon (python/tikun/muon.py:34-102,
+    torch f32 Newton-Schulz): the AdamW leaf bit-identical, the Muon matrices'
+    updates within the Newton-Schulz bar."""
+    import tikun_b200
+
+    z = np.load(os.path.join(golden_dir, "frontend_reference.npz"))
+    ps = {k: torch.tensor(z[f"muon/init/{k}"], device="cuda", requires_grad=True)
+          for k in ("w", "t", "b")}
+    opt = tikun_b200.Muon(muon_params=[ps["w"], ps["t"]], adamw_params=[ps["b"]], lr=0.02,
+                          momentum=0.95, adamw_lr=1e-3)
+    for s in range(3):
+        for k in ps:
+            ps[k].grad = torch.tensor(z[f"muon/grad{s}/{k}"], device="cuda")
+        opt.step()
+    torch.cuda.synchronize()
+    assert_bitexact(to_np(ps["b"]), z["muon/final/b"], "adamw leaf")
+    for k in ("w", "t"):
+        d_ref = z[f"muon/final/{k}"] - z[f"muon/init/{k}"]
+        d_got = to_np(ps[k]) - z[f"muon/init/{k}"]
+        assert relf(d_got, d_ref) <= 5e-3, k
+
+
+def test_bounded_wait_gives_up_and_leaves_the_device_usable():
+    """Failure detection without a fault: a kernel whose mbarrier wait can
+    never complete gives up after 50 ms, the call reports TK_ERR_DEVICE, and
+    the next Newton-Schulz call on the same context works."""
+    st = _native.lib().tk_testing_bounded_wait(50, None)
+    assert st == _native.TK_ERR_DEVICE
+    assert b"bounded wait" in _native.lib().tk_last_error()
+    assert _native.device_status() == 0  # cleared when reported
+    x = (np.random.default_rng(2).standard_normal((64, 96)) * 0.1).astype(np.float32)
+    t = torch.from_numpy(x.copy()).cuda()
+    _native.newton_schulz_2d_ffi(t.data_ptr(), 64, 96, 5)
+    assert relf(to_np(t), oracle.polar_step_np(x, 5)) <= 5e-3

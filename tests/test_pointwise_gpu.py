@@ -146,18 +146,27 @@ def test_host_buffers_are_staged():
         assert_bitexact(a, b, "host")
 
 
-def test_pinned_host_buffers():
-    n = 1 << 16
-    p = (torch.randn(n) * 0.02).pin_memory()
-    g = (torch.randn(n) * 0.1).pin_memory()
-    m, v = torch.zeros(n).pin_memory(), torch.zeros(n).pin_memory()
-    rp, rg, rm, rv = p.numpy().copy(), g.numpy().copy(), m.numpy().copy(), v.numpy().copy()
-    s = _native.step_fast_buffers([p.data_ptr()], [g.data_ptr()], [m.data_ptr()],
-                                  [v.data_ptr()], [n], 1.0, "adamw", 1, 1e-3, 0.9, 0.999, 1e-8, 0.01)
-    r = oracle.step_two_tier([rp], [rg], [rm], [rv], oracle.ADAMW, 1e-3, 0.9, 0.999, 1e-8,
-                             0.01, 1, 1.0)
-    assert s == r
-    assert_bitexact(p.numpy(), rp, "pinned p")
+@pytest.mark.parametrize("kind,max_norm", [("adamw", 1.0), ("adamw", 0.0), ("lion", 0.5)])
+def test_pinned_host_buffers(kind, max_norm):
+    """Pinned host leaves: the update kernel works on them in place over the
+    host link (g is copied to the device first when clipping)."""
+    sizes = [1 << 16, 17, 3000]
+    p = [(torch.randn(n) * 0.02).pin_memory() for n in sizes]
+    m = [torch.zeros(n).pin_memory() for n in sizes]
+    v = [torch.zeros(n).pin_memory() for n in sizes]
+    rp = [t.numpy().copy() for t in p]
+    rm = [t.numpy().copy() for t in m]
+    rv = [t.numpy().copy() for t in v]
+    for step in (1, 2, 3):
+        g = [(torch.randn(n) * 0.1).pin_memory() for n in sizes]
+        s = _native.step_fast_buffers([t.data_ptr() for t in p], [t.data_ptr() for t in g],
+                                      [t.data_ptr() for t in m], [t.data_ptr() for t in v], sizes,
+                                      max_norm, kind, step, 1e-3, 0.9, 0.99, 1e-8, 0.01)
+        r = oracle.step_two_tier(rp, [t.numpy().copy() for t in g], rm, rv, oracle.opt_kind(kind),
+                                 1e-3, 0.9, 0.99, 1e-8, 0.01, step, max_norm)
+        assert s == r
+    for a, b in zip(p + m + v, rp + rm + rv):
+        assert_bitexact(a.numpy(), b, "pinned")
 
 
 def test_rejects_aliased_leaves():
@@ -260,3 +269,25 @@ def test_frontend_matches_reference_frontend(golden_dir, case):
     torch.cuda.synchronize()
     for k in keys:
         assert_bitexact(to_np(params[k]), z[f"{case}/final/{k}"], f"{case}/{k}")
+
+
+def test_inbackward_frontend_matches_reference(golden_dir):
+    """In-backward AdamW (python/tikun/universal.py:97-137) on CUDA tensors:
+    per-leaf steps from post-accumulate-grad hooks, per-leaf clip, and the
+    reference's step numbering (the first two backward passes both use step 1).
+    The loss has device-exact gradients, so the result must be bit-identical."""
+    import tikun_b200
+
+    z = np.load(os.path.join(golden_dir, "frontend_reference.npz"))
+    w1 = torch.tensor(z["inbwd/init/w1"], device="cuda", requires_grad=True)
+    w2 = torch.tensor(z["inbwd/init/w2"], device="cuda", requires_grad=True)
+    c2 = torch.tensor(z["inbwd/c2"], device="cuda")
+    opt = tikun_b200.AdamW([w1, w2], lr=1e-2, max_norm=1.0, in_backward=True)
+    for _ in range(4):
+        loss = (w1 * w1).sum() + (w2 * c2).sum()
+        loss.backward()
+        opt.step()
+    torch.cuda.synchronize()
+    assert w1.grad is None and w2.grad is None
+    assert_bitexact(to_np(w1), z["inbwd/final/w1"], "w1")
+    assert_bitexact(to_np(w2), z["inbwd/final/w2"], "w2")

@@ -131,6 +131,7 @@ _SIGNATURES = {
     "tk_newton_schulz_3d": [_P, _I64, _I64, _I64, _I32, _I32, _I32, _P],
     "tk_muon_step": [ctypes.POINTER(TkMuonLeaf), _SZ, ctypes.POINTER(TkMuonHParams), _P],
     "tk_device_status": [ctypes.POINTER(ctypes.c_int)],
+    "tk_testing_bounded_wait": [ctypes.c_int, _P],
     "tk_testing_gemm_tn": [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                            _I64, _I64, _I64, _F, ctypes.c_int, _P],
 }

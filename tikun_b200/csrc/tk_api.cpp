@@ -355,8 +355,211 @@ static int step_device(const tk_leaf* leaves, size_t n, int kind, const tk_hpara
   return TK_OK;
 }
 
-// Host leaves: copy everything the step touches into device scratch, run the
-// device step there and copy p, m, v back.  Synchronous.
+// ---- host leaves through the copy engines ----------------------------------
+// Per-device side streams and events for the pipelined host step.
+struct HostPipe {
+  std::mutex mu;  // one host-buffer step at a time per device (shared streams/events)
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  static constexpr int kSlots = 3;
+  cudaEvent_t start = nullptr, g_ready = nullptr, end = nullptr;
+  cudaEvent_t in_ready[kSlots] = {}, done[kSlots] = {}, out_done[kSlots] = {};
+};
+
+static int host_pipe(HostPipe** out) {
+  static HostPipe pipes[64];
+  static bool ready[64] = {};
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  if (!ready[dev]) {
+    HostPipe& P = pipes[dev];
+    TK_CUDA_TRY(cudaStreamCreateWithFlags(&P.h2d, cudaStreamNonBlocking));
+    TK_CUDA_TRY(cudaStreamCreateWithFlags(&P.d2h, cudaStreamNonBlocking));
+    for (cudaEvent_t* e : {&P.start, &P.g_ready, &P.end})
+      TK_CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    for (int k = 0; k < HostPipe::kSlots; ++k)
+      for (cudaEvent_t* e : {&P.in_ready[k], &P.done[k], &P.out_done[k]})
+        TK_CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    ready[dev] = true;
+  }
+  *out = &pipes[dev];
+  return TK_OK;
+}
+
+static bool all_pinned(const tk_leaf* leaves, size_t n, int kind) {
+  for (size_t i = 0; i < n; ++i) {
+    const tk_leaf& L = leaves[i];
+    if (L.n == 0) continue;
+    const void* ptrs[4] = {L.p, L.g, L.m, kind == TK_ADAMW ? (const void*)L.v : nullptr};
+    for (const void* p : ptrs) {
+      if (p == nullptr) continue;
+      cudaPointerAttributes a;
+      if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+      }
+      if (a.type != cudaMemoryTypeHost) return false;
+    }
+  }
+  return true;
+}
+
+// A piece of one leaf: elements [off, off + cnt).
+struct Piece {
+  size_t leaf;
+  uint64_t off, cnt;
+};
+
+// Pinned host leaves.  The elements are cut into chunks of at most
+// kChunkElems (whole small leaves share a chunk); chunk c moves through a ring
+// of three device slots: the H2D stream copies its p, m, v (and g, when not
+// clipping) into slot c % 3, the caller's stream updates it, the D2H stream
+// copies p, m, v back, so both copy directions and the update overlap.  With a
+// clip, all of g is copied first and Tier 1 runs on it before any update.
+static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const tk_hparams& hp,
+                               uint64_t step, float max_norm, float* clip_scale_out,
+                               cudaStream_t s) {
+  constexpr uint64_t kChunkElems = 8u << 20;
+  constexpr int kMaxPieces = kMaxLeavesPerLaunch;
+  HostPipe* P = nullptr;
+  TK_TRY(host_pipe(&P));
+  std::lock_guard<std::mutex> serial(P->mu);
+  const bool clip = max_norm > 0.0f;
+  const bool adam = kind == TK_ADAMW;
+
+  // chunks of pieces
+  std::vector<std::vector<Piece>> chunks;
+  std::vector<uint64_t> chunk_elems;
+  for (size_t i = 0; i < n; ++i) {
+    uint64_t off = 0;
+    while (off < leaves[i].n) {
+      if (chunks.empty() || chunk_elems.back() >= kChunkElems ||
+          (int)chunks.back().size() >= kMaxPieces) {
+        chunks.emplace_back();
+        chunk_elems.push_back(0);
+      }
+      const uint64_t take = std::min(leaves[i].n - off, kChunkElems - chunk_elems.back());
+      chunks.back().push_back({i, off, take});
+      chunk_elems.back() += (take + 63) / 64 * 64;
+      off += take;
+    }
+  }
+  if (chunks.empty()) {
+    if (clip_scale_out) *clip_scale_out = 1.0f;
+    return TK_OK;
+  }
+  // device memory: g for every leaf when clipping; three slots of
+  // (p, g unless clipping, m, v) for kChunkElems (+ padding) elements each
+  size_t gbytes = 0;
+  std::vector<size_t> goff(n, 0);
+  if (clip)
+    for (size_t i = 0; i < n; ++i) {
+      goff[i] = gbytes;
+      gbytes += (leaves[i].n * esize(leaves[i].g_dtype) + 255) / 256 * 256;
+    }
+  const uint64_t slot_elems = kChunkElems + 64 * (uint64_t)kMaxPieces;
+  const size_t arr_bytes = slot_elems * 4;
+  const int arrays = 2 + (adam ? 1 : 0) + (clip ? 0 : 1);  // p, m, [v], [g]
+  const size_t slot_bytes = arr_bytes * arrays;
+  Scratch sc;
+  TK_TRY(sc.alloc(256 + gbytes + slot_bytes * HostPipe::kSlots, s));
+  char* base = static_cast<char*>(sc.get());
+  float* scale_dev = reinterpret_cast<float*>(base);
+  char* gdev = base + 256;
+  char* slots = gdev + gbytes;
+
+  const PointwiseConsts c = make_consts(kind, hp, step);
+  // everything starts after the caller's earlier work on s
+  TK_CUDA_TRY(cudaEventRecord(P->start, s));
+  TK_CUDA_TRY(cudaStreamWaitEvent(P->h2d, P->start, 0));
+  TK_CUDA_TRY(cudaStreamWaitEvent(P->d2h, P->start, 0));
+
+  Scratch norm_scratch;
+  double* partials = nullptr;
+  int n_partials = 0;
+  if (clip) {
+    for (size_t i = 0; i < n; ++i)
+      if (leaves[i].n)
+        TK_CUDA_TRY(cudaMemcpyAsync(gdev + goff[i], leaves[i].g, leaves[i].n * esize(leaves[i].g_dtype),
+                                    cudaMemcpyHostToDevice, P->h2d));
+    TK_CUDA_TRY(cudaEventRecord(P->g_ready, P->h2d));
+    TK_CUDA_TRY(cudaStreamWaitEvent(s, P->g_ready, 0));
+    std::vector<tk_leaf> gl(leaves, leaves + n);
+    for (size_t i = 0; i < n; ++i) gl[i].g = gdev + goff[i];
+    Plan plan;
+    make_plan(gl.data(), n, TK_SGD, &plan);  // Tier 1 reads g only
+    TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s));
+  }
+
+  for (size_t ci = 0; ci < chunks.size(); ++ci) {
+    const int k = (int)(ci % HostPipe::kSlots);
+    char* slot = slots + k * slot_bytes;
+    char* pbase = slot;  // each array: slot_elems elements of up to 4 bytes
+    char* mbase = slot + arr_bytes;
+    char* vbase = slot + 2 * arr_bytes;
+    char* gbase = slot + (adam ? 3 : 2) * arr_bytes;
+    if (ci >= (size_t)HostPipe::kSlots) TK_CUDA_TRY(cudaStreamWaitEvent(P->h2d, P->out_done[k], 0));
+    std::vector<tk_leaf> dl;
+    uint64_t at = 0;
+    for (const Piece& pc : chunks[ci]) {
+      const tk_leaf& L = leaves[pc.leaf];
+      const size_t pe = esize(L.p_dtype), ge = esize(L.g_dtype);
+      tk_leaf d = L;
+      d.n = pc.cnt;
+      d.p = pbase + at * 4;
+      d.m = reinterpret_cast<float*>(mbase + at * 4);
+      d.v = adam ? reinterpret_cast<float*>(vbase + at * 4) : nullptr;
+      TK_CUDA_TRY(cudaMemcpyAsync(d.p, static_cast<const char*>(L.p) + pc.off * pe, pc.cnt * pe,
+                                  cudaMemcpyHostToDevice, P->h2d));
+      TK_CUDA_TRY(cudaMemcpyAsync(d.m, L.m + pc.off, pc.cnt * 4, cudaMemcpyHostToDevice, P->h2d));
+      if (adam)
+        TK_CUDA_TRY(cudaMemcpyAsync(d.v, L.v + pc.off, pc.cnt * 4, cudaMemcpyHostToDevice, P->h2d));
+      if (clip) {
+        d.g = gdev + goff[pc.leaf] + pc.off * ge;
+      } else {
+        d.g = gbase + at * 4;
+        TK_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(d.g), static_cast<const char*>(L.g) + pc.off * ge,
+                                    pc.cnt * ge, cudaMemcpyHostToDevice, P->h2d));
+      }
+      dl.push_back(d);
+      at += (pc.cnt + 63) / 64 * 64;
+    }
+    TK_CUDA_TRY(cudaEventRecord(P->in_ready[k], P->h2d));
+    TK_CUDA_TRY(cudaStreamWaitEvent(s, P->in_ready[k], 0));
+    Plan plan;
+    make_plan(dl.data(), dl.size(), kind, &plan);
+    for (size_t t = 0; t < plan.tables.size(); ++t)
+      TK_TRY(launch_pointwise(plan.tables[t], kind, plan.pdt[t], plan.gdt[t], c, partials,
+                              n_partials, max_norm, nullptr,
+                              (clip && ci == 0 && t == 0) ? scale_dev : nullptr, s));
+    TK_CUDA_TRY(cudaEventRecord(P->done[k], s));
+    TK_CUDA_TRY(cudaStreamWaitEvent(P->d2h, P->done[k], 0));
+    size_t j = 0;
+    for (const Piece& pc : chunks[ci]) {
+      const tk_leaf& L = leaves[pc.leaf];
+      const tk_leaf& d = dl[j++];
+      const size_t pe = esize(L.p_dtype);
+      TK_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(L.p) + pc.off * pe, d.p, pc.cnt * pe,
+                                  cudaMemcpyDeviceToHost, P->d2h));
+      TK_CUDA_TRY(cudaMemcpyAsync(L.m + pc.off, d.m, pc.cnt * 4, cudaMemcpyDeviceToHost, P->d2h));
+      if (adam)
+        TK_CUDA_TRY(cudaMemcpyAsync(L.v + pc.off, d.v, pc.cnt * 4, cudaMemcpyDeviceToHost, P->d2h));
+    }
+    TK_CUDA_TRY(cudaEventRecord(P->out_done[k], P->d2h));
+  }
+  // the caller's stream (and the scratch it frees) waits for the last copies
+  TK_CUDA_TRY(cudaEventRecord(P->end, P->d2h));
+  TK_CUDA_TRY(cudaStreamWaitEvent(s, P->end, 0));
+  float scale = 1.0f;
+  if (clip) TK_CUDA_TRY(cudaMemcpyAsync(&scale, scale_dev, 4, cudaMemcpyDeviceToHost, s));
+  TK_CUDA_TRY(cudaStreamSynchronize(s));
+  if (clip_scale_out) *clip_scale_out = scale;
+  return TK_OK;
+}
+
+// Pageable host leaves: copy everything the step touches into device scratch,
+// run the device step there and copy p, m, v back.  Synchronous.
 static int step_host(const tk_leaf* leaves, size_t n, int kind, const tk_hparams& hp,
                      uint64_t step, float max_norm, float* clip_scale_out, cudaStream_t s) {
   size_t bytes = 64;
@@ -418,6 +621,8 @@ static int step_entry(const tk_leaf* leaves, size_t n, int kind, const tk_hparam
   if (where == Residency::kHost) {
     if (!sync)
       return set_error(TK_ERR_INVALID, "the asynchronous step takes device buffers only");
+    if (all_pinned(leaves, n, kind))
+      return step_host_pipelined(leaves, n, kind, *hp, step, max_norm, clip_scale_out, s);
     return step_host(leaves, n, kind, *hp, step, max_norm, clip_scale_out, s);
   }
   if (!sync) {

@@ -870,7 +870,30 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   return TK_OK;
 }
 
-// ------------------------------------------------------------------ test hook
+// ------------------------------------------------------------------ test hooks
+// A wait that cannot complete: one thread waits on a fresh mbarrier that no
+// one arrives on, with the given bound.  It must give up, record code 9 in the
+// status word and return, leaving the context usable.
+__global__ void bounded_wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, err, 9, limit_ns);
+}
+
+int bounded_wait_probe(int* err_dev, int limit_ms, cudaStream_t s) {
+  if (limit_ms < 1 || limit_ms > 2000) return set_error(TK_ERR_INVALID, "limit %d ms outside 1..2000", limit_ms);
+  bounded_wait_probe_kernel<<<1, 32, 0, s>>>(err_dev, (unsigned long long)limit_ms * 1000000ull);
+  TK_CUDA_TRY(cudaGetLastError());
+  return TK_OK;
+}
+
+
 // Plain batched TN GEMM D = alpha * P Q^T on half-precision operands, for the
 // kernel's own tests.
 int plain_gemm(const uint16_t* P, const uint16_t* Q, uint16_t* D, int batch, int M, int N, int K,

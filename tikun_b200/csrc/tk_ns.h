@@ -71,5 +71,9 @@ int plain_gemm(const uint16_t* P, const uint16_t* Q, uint16_t* D, int batch, int
                int64_t ldp, int64_t ldq, int64_t ldd, float alpha, int fmt, int* err_dev,
                cudaStream_t s);
 
+// Test hook: a kernel whose only wait can never complete gives up after
+// limit_ms and records code 9 in *err_dev.
+int bounded_wait_probe(int* err_dev, int limit_ms, cudaStream_t s);
+
 }  // namespace ns
 }  // namespace tk

@@ -243,4 +243,12 @@ int tk_testing_gemm_tn(const void* P, const void* Q, void* D, int batch, int M, 
   return check_status(s);
 }
 
+int tk_testing_bounded_wait(int limit_ms, void* stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* status = nullptr;
+  TK_TRY(device_status_word(&status));
+  TK_TRY(ns::bounded_wait_probe(status, limit_ms, s));
+  return check_status(s);
+}
+
 }  // extern "C"

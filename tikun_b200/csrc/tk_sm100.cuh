@@ -60,12 +60,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // raises the CTA's abort flag and the kernel's error word) when the wait runs
 // past the limit, or when the abort flag is already up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag, int* err, int code) {
+                                          volatile int* abort_flag, int* err, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       if (err) atomicCAS(err, 0, code);
       return false;

@@ -16,6 +16,11 @@ TK_API int tk_testing_gemm_tn(const void* P, const void* Q, void* D, int batch, 
                               int K, int64_t ldp, int64_t ldq, int64_t ldd, float alpha, int fmt,
                               void* stream);
 
+/* Launches a kernel whose mbarrier wait can never complete; the bounded wait
+ * gives up after limit_ms (1..2000), the kernel returns and the call reports
+ * TK_ERR_DEVICE.  Exercises the failure path without faulting the GPU. */
+TK_API int tk_testing_bounded_wait(int limit_ms, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
