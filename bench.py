@@ -272,58 +272,51 @@ def timed_loop(step_fn, steps, warmup, stream, world, dist, dev, torch, uuid, be
 
 def run_pointwise(args, wl, world, rank, dev, torch, dist):
     from tikun_b200 import _native
-    from tikun_b200.arena import Arena, LayoutPlan, shard_bounds, shard_segments
+    from tikun_b200.arena import Arena, LayoutPlan
 
     L = _native.lib()
     stream = torch.cuda.current_stream()
     s_handle = stream.cuda_stream
-    plan = LayoutPlan(wl["sizes"], pad_to=16 * max(world, 1))
+    fused = world > 1 and args.zero == "fused"
+    chunks = 4 if world > 1 and not fused else 1
+    plan = LayoutPlan(wl["sizes"], pad_to=16 * max(world, 1) * chunks)
     hp_np, hg_np = make_host_state(wl)
-    P, G, M, V = (Arena(plan, device=dev) for _ in range(4))
+    P, G = (Arena(plan, device=dev) for _ in range(2))
     for i in range(len(plan)):
         P.leaf(i).copy_(torch.from_numpy(hp_np[i]))
         G.leaf(i).copy_(torch.from_numpy(hg_np[i]))
     n_params = sum(wl["sizes"])
-    lo, hi = shard_bounds(plan.total, world, rank)
-    segs = shard_segments(plan, lo, hi)
-    pp, gp, mp, vp = P.ptrs(), G.ptrs(), M.ptrs(), V.ptrs()
-    leaves, n_leaves = _native.make_leaves(
-        [pp[i] + a * 4 for i, a, c in segs], [gp[i] + a * 4 for i, a, c in segs],
-        [mp[i] + a * 4 for i, a, c in segs], [vp[i] + a * 4 for i, a, c in segs],
-        [c for i, a, c in segs])
-    my_params = sum(c for _, _, c in segs)
     hp = _native.TkHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"])
-    scale_dev = torch.ones(1, dtype=torch.float32, device=dev)
-    sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
-    state = {"step": 0, "ev": None}
+    state = {"step": 0, "ev": None, "k": None}
     clip = wl["max_norm"] > 0
+    if world == 1:
+        M, V = (Arena(plan, device=dev) for _ in range(2))
+        leaves, n_leaves = _native.make_leaves(P.ptrs(), G.ptrs(), M.ptrs(), V.ptrs(), wl["sizes"])
+        my_params = n_params
+        scale_dev = torch.ones(1, dtype=torch.float32, device=dev)
 
-    def one_step():
-        state["step"] += 1
-        ev = state["ev"]
-        _native.check(L.tk_set_update_events(*(ev if ev else (None, None))))
-        if world == 1:
+        def one_step():
+            state["step"] += 1
+            ev = state["ev"]
+            _native.check(L.tk_set_update_events(*(ev if ev else (None, None))))
             _native.check(L.tk_step_buffers_async(leaves, n_leaves, _native.TK_ADAMW,
                                                   ctypes.byref(hp), state["step"],
                                                   wl["max_norm"], scale_dev.data_ptr(), s_handle))
             return 2 if clip else 1
-        launches = 0
-        if clip:
-            _native.check(L.tk_grad_sumsq(leaves, n_leaves, sumsq.data_ptr(), s_handle))
-            dist.all_reduce(sumsq)
-            _native.check(L.tk_clip_scale(sumsq.data_ptr(), wl["max_norm"], scale_dev.data_ptr(),
-                                          s_handle))
-            launches += 3
-        k = state.get("k")
-        if k is not None:
-            ev_pairs[k][0].record(stream)
-        _native.check(L.tk_apply_pointwise(leaves, n_leaves, _native.TK_ADAMW, ctypes.byref(hp),
-                                           state["step"], scale_dev.data_ptr() if clip else None,
-                                           s_handle))
-        if k is not None:
-            ev_pairs[k][1].record(stream)
-        dist.all_gather_into_tensor(P.flat, P.flat[lo:hi])
-        return launches + 1
+    else:
+        # ZeRO-1: the update kernel stores into the peers' arenas (fused), or
+        # each super-chunk's all-gather overlaps the update of the next
+        from tikun_b200.distributed import ZeroHParams, ZeroPointwise
+
+        zp = ZeroPointwise(plan, P.flat, G.flat,
+                           ZeroHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"],
+                                       wl["max_norm"]), chunks=chunks, fused=fused)
+        my_params = sum(zp.all_leaves[0][i].n for i in range(zp.all_leaves[1]))
+
+        def one_step():
+            k = state["k"]
+            zp.step(update_events=ev_pairs[k] if k is not None else None)
+            return zp.launches_per_step
 
     ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(args.steps)]
@@ -343,6 +336,8 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
     state["ev"] = None
     state["k"] = None
     _native.check(L.tk_set_update_events(None, None))
+    if world > 1:
+        zp.close()
     upd_ms = sum(a.elapsed_time(b) for a, b in ev_pairs) / args.steps
     ms_step = ms_total / args.steps
     value = n_params / (ms_step / 1e3)
@@ -401,7 +396,9 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
                 % wl["g_std"],
         "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
                    "leaves": len(wl["sizes"]),
-                   "parallelism": "single GPU" if world == 1 else f"zero1-dp{world}",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"zero1-dp{world} (update kernel stores into peer arenas over NVLink)" if fused
+                   else f"zero1-dp{world} (chunk-major, all-gather overlapped with the update)",
                    "l2": "inputs (p,g,m,v) larger than L2; no flush"},
         "roofline": {"bound": "hbm", "kernel": "pointwise_kernel (AdamW update)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
@@ -579,6 +576,9 @@ def main():
     ap.add_argument("--workload", default="gpt2-small-clip", choices=sorted(WORKLOADS) + sorted(MUON))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--zero", default="fused", choices=["fused", "allgather"],
+                    help="multi-GPU AdamW exchange: peer stores from the update kernel, or "
+                         "chunk-major all-gathers overlapped with the update")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -231,6 +231,31 @@ TK_API int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves,
  * reported a problem). */
 TK_API int tk_device_status(int* status_out);
 
+/* tk_apply_pointwise for ZeRO-1 without a separate all-gather: the updated
+ * parameters of these leaves are also stored into n_peers (<= 7) other GPUs'
+ * copies of the same layout, at byte offset peer_deltas[i] from each local
+ * parameter address (peer memory mapped into this process, tk_ipc_import).
+ * The stores are made visible system-wide before the kernel ends; a caller
+ * orders the peers' later reads after it with any cross-GPU barrier (an
+ * all-reduce).  Device leaves only. */
+TK_API int tk_apply_pointwise_peers(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                                    const tk_hparams* hp, uint64_t step, const float* scale_dev,
+                                    const int64_t* peer_deltas, int n_peers, void* stream);
+
+/* CUDA IPC for the peer copies: tk_ipc_export writes the 64-byte handle of
+ * the device allocation holding ptr and ptr's offset in it; another process
+ * maps it with tk_ipc_import (returning the address of the same byte) and
+ * unmaps it with tk_ipc_close. */
+TK_API int tk_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+TK_API int tk_ipc_import(const void* handle, uint64_t offset, void** ptr_out);
+TK_API int tk_ipc_close(void* ptr);
+
+/* Leaves `sms` SMs of every device free of pointwise (Tier 1 / Tier 2) CTAs,
+ * so that kernels launched concurrently on other streams -- NCCL all-gathers
+ * overlapping a sharded update -- can run at the same time.  Process-wide;
+ * 0 (the default) lets the pointwise kernels use every SM. */
+TK_API int tk_set_reserved_sms(int sms);
+
 /* ---------------------------------------------------------------------- */
 /* measurement                                                             */
 /* ---------------------------------------------------------------------- */

@@ -162,3 +162,31 @@ def test_two_rank_gloo_choreography():
         for i, (o, n) in enumerate(zip(offs, msz)):
             assert (mfull[o:o + n] == i + 1).all()
     np.testing.assert_array_equal(res[0][2], res[1][2])
+
+
+@pytest.mark.parametrize("world,chunks", [(1, 1), (2, 4), (4, 4), (8, 3)])
+def test_chunk_major_pieces_cover_the_arena(world, chunks):
+    from tikun_b200.distributed import chunk_major_pieces, pieces_to_segments
+
+    sizes = [50257 * 8, 17, 768, 1, 4097, 3 * 64 * 64]
+    plan = LayoutPlan(sizes, pad_to=16 * world * chunks)
+    seen = [np.zeros(n, np.int32) for n in sizes]
+    cover = np.zeros(plan.total, np.int32)
+    for r in range(world):
+        pieces = chunk_major_pieces(plan.total, world, r, chunks)
+        assert len(pieces) == chunks
+        for c, (lo, hi) in enumerate(pieces):
+            sup = plan.total // chunks
+            assert c * sup <= lo < hi <= (c + 1) * sup and lo % 16 == 0
+            cover[lo:hi] += 1
+            for i, a, n in pieces_to_segments(plan, lo, hi):
+                seen[i][a:a + n] += 1
+    assert (cover == 1).all()
+    assert all((s == 1).all() for s in seen)
+
+
+def test_chunk_major_rejects_unaligned_arena():
+    from tikun_b200.distributed import chunk_major_pieces
+
+    with pytest.raises(ValueError):
+        chunk_major_pieces(1000, 2, 0, 4)

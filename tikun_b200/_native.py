@@ -125,6 +125,12 @@ _SIGNATURES = {
     "tk_apply_pointwise": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,
                            _P, _P],
     "tk_set_update_events": [_P, _P],
+    "tk_set_reserved_sms": [ctypes.c_int],
+    "tk_apply_pointwise_peers": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams),
+                                 _U64, _P, ctypes.POINTER(_I64), ctypes.c_int, _P],
+    "tk_ipc_export": [_P, _P, ctypes.POINTER(_U64)],
+    "tk_ipc_import": [_P, _U64, ctypes.POINTER(_P)],
+    "tk_ipc_close": [_P],
     "tk_step_buffers_noalloc": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams),
                                 _U64, _F, ctypes.POINTER(_F), _P],
     "tk_newton_schulz_2d": [_P, _I64, _I64, _I32, _I32, _I32, _P],

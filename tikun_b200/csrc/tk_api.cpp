@@ -1,9 +1,12 @@
 // C-ABI entry points of the pointwise step (include/tikun_cuda.h): the static
 // verifier, the layout plan, leaf validation and the Tier 1 / Tier 2
 // orchestration over the CUDA kernels in tk_pointwise.cu.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -46,6 +49,15 @@ int sm_count(int* out) {
     cached[dev] = n;
   }
   *out = cached[dev];
+  return TK_OK;
+}
+
+static std::atomic<int> g_reserved_sms{0};
+
+int pointwise_sms(int* out) {
+  int sms = 0;
+  TK_TRY(sm_count(&sms));
+  *out = std::max(1, sms - g_reserved_sms.load());
   return TK_OK;
 }
 
@@ -228,13 +240,21 @@ static int validate_leaves(const tk_leaf* leaves, size_t n, int kind, Residency*
 
 static bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
 
-// Splits the non-empty leaves with one (p, g) dtype pair into launch tables.
+static bool leaf_vec_ok(const tk_leaf& L, int kind) {
+  return aligned(L.p, 4 * esize(L.p_dtype)) && aligned(L.g, 4 * esize(L.g_dtype)) &&
+         aligned(L.m, 16) && (kind != TK_ADAMW || aligned(L.v, 16));
+}
+
+// Splits the non-empty leaves with one (p, g) dtype pair into launch tables;
+// `want_vec` selects leaves whose pointers are (1) or are not (0) aligned for
+// whole-group access, -1 takes both.
 static void build_tables(const tk_leaf* leaves, size_t n, int kind, int pdt, int gdt,
-                         std::vector<LeafTable>* out) {
+                         std::vector<LeafTable>* out, int want_vec = -1) {
   LeafTable* t = nullptr;
   for (size_t i = 0; i < n; ++i) {
     const tk_leaf& L = leaves[i];
     if (L.n == 0 || L.p_dtype != pdt || L.g_dtype != gdt) continue;
+    if (want_vec >= 0 && (int)leaf_vec_ok(L, kind) != want_vec) continue;
     if (t == nullptr || t->n_leaves == kMaxLeavesPerLaunch) {
       out->emplace_back();
       t = &out->back();
@@ -247,8 +267,7 @@ static void build_tables(const tk_leaf* leaves, size_t n, int kind, int pdt, int
     d.v = kind == TK_ADAMW ? L.v : nullptr;
     d.n = L.n;
     d.q_begin = t->total_quads;
-    d.vec_ok = aligned(L.p, 4 * esize(pdt)) && aligned(L.g, 4 * esize(gdt)) &&
-               aligned(L.m, 16) && (kind != TK_ADAMW || aligned(L.v, 16));
+    d.vec_ok = leaf_vec_ok(L, kind);
     t->total_quads += (L.n + 3) / 4;
   }
 }
@@ -290,19 +309,48 @@ static PointwiseConsts make_consts(int kind, const tk_hparams& hp, uint64_t step
 struct Plan {
   std::vector<LeafTable> tables;
   std::vector<int> pdt, gdt;
+  std::vector<char> bulk;  // table goes through the bulk-copy kernel
 };
+
+// With TIKUN_PW_BULK=1 in the environment, f32 leaves with aligned pointers
+// form tables for the bulk-copy pipeline kernel and every other leaf goes to
+// the register kernel.  Off by default: on B200 the bulk pipeline at its best
+// tile/ring shape only ties the register kernel (both near 0.87 of the copy
+// bandwidth, bound by the exact divide/square-root chain), and the register
+// kernel alone carries the peer stores.
+static bool bulk_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("TIKUN_PW_BULK");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
 
 static void make_plan(const tk_leaf* leaves, size_t n, int kind, Plan* plan) {
   const int dts[2] = {TK_F32, TK_BF16};
   for (int pd : dts)
     for (int gd : dts) {
-      size_t before = plan->tables.size();
-      build_tables(leaves, n, kind, pd, gd, &plan->tables);
-      for (size_t i = before; i < plan->tables.size(); ++i) {
-        plan->pdt.push_back(pd);
-        plan->gdt.push_back(gd);
+      const bool f32 = bulk_enabled() && pd == TK_F32 && gd == TK_F32;
+      for (int pass = 0; pass < (f32 ? 2 : 1); ++pass) {
+        size_t before = plan->tables.size();
+        build_tables(leaves, n, kind, pd, gd, &plan->tables, f32 ? (pass == 0 ? 1 : 0) : -1);
+        for (size_t i = before; i < plan->tables.size(); ++i) {
+          plan->pdt.push_back(pd);
+          plan->gdt.push_back(gd);
+          plan->bulk.push_back(f32 && pass == 0);
+        }
       }
     }
+}
+
+static int launch_table(const Plan& plan, size_t i, int kind, const PointwiseConsts& c,
+                        const double* partials, int n_partials, float max_norm,
+                        const float* scale_dev, float* scale_out, cudaStream_t s) {
+  if (plan.bulk[i])
+    return launch_pointwise_bulk(plan.tables[i], kind, c, partials, n_partials, max_norm,
+                                 scale_dev, scale_out, s);
+  return launch_pointwise(plan.tables[i], kind, plan.pdt[i], plan.gdt[i], c, partials, n_partials,
+                          max_norm, scale_dev, scale_out, s);
 }
 
 // Tier 1 partials for every table into one buffer; returns the block count.
@@ -346,10 +394,9 @@ static int step_device(const tk_leaf* leaves, size_t n, int kind, const tk_hpara
   int n_partials = 0;
   if (max_norm > 0.0f) TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s));
   if (g_update_start) TK_CUDA_TRY(cudaEventRecord(g_update_start, s));
-  for (size_t i = 0; i < plan.tables.size(); ++i) {
-    TK_TRY(launch_pointwise(plan.tables[i], kind, plan.pdt[i], plan.gdt[i], c, partials,
-                            n_partials, max_norm, nullptr, i == 0 ? scale_dev : nullptr, s));
-  }
+  for (size_t i = 0; i < plan.tables.size(); ++i)
+    TK_TRY(launch_table(plan, i, kind, c, partials, n_partials, max_norm, nullptr,
+                        i == 0 ? scale_dev : nullptr, s));
   if (g_update_stop) TK_CUDA_TRY(cudaEventRecord(g_update_stop, s));
   *scale_written = partials != nullptr && scale_dev != nullptr;
   return TK_OK;
@@ -530,9 +577,8 @@ static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const 
     Plan plan;
     make_plan(dl.data(), dl.size(), kind, &plan);
     for (size_t t = 0; t < plan.tables.size(); ++t)
-      TK_TRY(launch_pointwise(plan.tables[t], kind, plan.pdt[t], plan.gdt[t], c, partials,
-                              n_partials, max_norm, nullptr,
-                              (clip && ci == 0 && t == 0) ? scale_dev : nullptr, s));
+      TK_TRY(launch_table(plan, t, kind, c, partials, n_partials, max_norm, nullptr,
+                          (clip && ci == 0 && t == 0) ? scale_dev : nullptr, s));
     TK_CUDA_TRY(cudaEventRecord(P->done[k], s));
     TK_CUDA_TRY(cudaStreamWaitEvent(P->d2h, P->done[k], 0));
     size_t j = 0;
@@ -714,6 +760,13 @@ int tk_step_buffers_async(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
                     nullptr, clip_scale_dev, false, static_cast<cudaStream_t>(stream));
 }
 
+int tk_set_reserved_sms(int sms) {
+  g_last_error.clear();
+  if (sms < 0 || sms > 1024) return set_error(TK_ERR_INVALID, "reserved SM count %d out of range", sms);
+  g_reserved_sms.store(sms);
+  return TK_OK;
+}
+
 int tk_set_update_events(void* start_event, void* stop_event) {
   g_last_error.clear();
   if ((start_event == nullptr) != (stop_event == nullptr))
@@ -721,6 +774,106 @@ int tk_set_update_events(void* start_event, void* stop_event) {
   g_update_start = static_cast<cudaEvent_t>(start_event);
   g_update_stop = static_cast<cudaEvent_t>(stop_event);
   return TK_OK;
+}
+
+int tk_apply_pointwise_peers(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                             const tk_hparams* hp, uint64_t step, const float* scale_dev,
+                             const int64_t* peer_deltas, int n_peers, void* stream) {
+  g_last_error.clear();
+  if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
+    return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
+  Residency where;
+  TK_TRY(validate_leaves(leaves, n_leaves, kind, &where));
+  if (where == Residency::kHost)
+    return set_error(TK_ERR_INVALID, "tk_apply_pointwise_peers takes device buffers");
+  PeerSet peers;
+  std::memset(&peers, 0, sizeof(peers));
+  peers.n = n_peers;
+  for (int i = 0; i < n_peers; ++i) peers.delta[i] = peer_deltas[i];
+  // every leaf through the register kernel, which carries the peer stores
+  Plan plan;
+  const int dts[2] = {TK_F32, TK_BF16};
+  for (int pd : dts)
+    for (int gd : dts) {
+      size_t before = plan.tables.size();
+      build_tables(leaves, n_leaves, kind, pd, gd, &plan.tables);
+      for (size_t i = before; i < plan.tables.size(); ++i) {
+        plan.pdt.push_back(pd);
+        plan.gdt.push_back(gd);
+      }
+    }
+  const PointwiseConsts c = make_consts(kind, *hp, step);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (size_t i = 0; i < plan.tables.size(); ++i)
+    TK_TRY(launch_pointwise(plan.tables[i], kind, plan.pdt[i], plan.gdt[i], c, nullptr, 0, 0.f,
+                            scale_dev, nullptr, s, &peers));
+  return TK_OK;
+}
+
+typedef CUresult (*GetAddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static int alloc_base(const void* ptr, char** base) {
+  static GetAddressRangeFn fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000,
+                                                     cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess)
+      return set_error(TK_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+    fn = (GetAddressRangeFn)p;
+  }
+  CUdeviceptr b = 0;
+  size_t sz = 0;
+  if (fn(&b, &sz, (CUdeviceptr)(uintptr_t)ptr) != CUDA_SUCCESS)
+    return set_error(TK_ERR_INVALID, "%p is not inside a device allocation", ptr);
+  *base = reinterpret_cast<char*>((uintptr_t)b);
+  return TK_OK;
+}
+
+static std::mutex g_ipc_mu;
+static std::vector<std::pair<char*, char*>> g_ipc_open;  // (returned pointer, mapped base)
+
+int tk_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out) {
+  g_last_error.clear();
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return set_error(TK_ERR_INVALID, "null argument");
+  char* base = nullptr;
+  TK_TRY(alloc_base(ptr, &base));
+  cudaIpcMemHandle_t h;
+  TK_CUDA_TRY(cudaIpcGetMemHandle(&h, base));
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = (uint64_t)(static_cast<const char*>(ptr) - base);
+  return TK_OK;
+}
+
+int tk_ipc_import(const void* handle, uint64_t offset, void** ptr_out) {
+  g_last_error.clear();
+  if (handle == nullptr || ptr_out == nullptr) return set_error(TK_ERR_INVALID, "null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  TK_CUDA_TRY(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  char* p = static_cast<char*>(base) + offset;
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  g_ipc_open.emplace_back(p, static_cast<char*>(base));
+  *ptr_out = p;
+  return TK_OK;
+}
+
+int tk_ipc_close(void* ptr) {
+  g_last_error.clear();
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  for (size_t i = 0; i < g_ipc_open.size(); ++i)
+    if (g_ipc_open[i].first == ptr) {
+      char* base = g_ipc_open[i].second;
+      g_ipc_open.erase(g_ipc_open.begin() + (long)i);
+      TK_CUDA_TRY(cudaIpcCloseMemHandle(base));
+      return TK_OK;
+    }
+  return set_error(TK_ERR_INVALID, "%p was not returned by tk_ipc_import", ptr);
 }
 
 int tk_grad_sumsq(const tk_leaf* leaves, size_t n_leaves, double* sumsq_dev, void* stream) {
@@ -763,8 +916,7 @@ int tk_apply_pointwise(const tk_leaf* leaves, size_t n_leaves, int32_t kind, con
   const PointwiseConsts c = make_consts(kind, *hp, step);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   for (size_t i = 0; i < plan.tables.size(); ++i)
-    TK_TRY(launch_pointwise(plan.tables[i], kind, plan.pdt[i], plan.gdt[i], c, nullptr, 0, 0.f,
-                            scale_dev, nullptr, s));
+    TK_TRY(launch_table(plan, i, kind, c, nullptr, 0, 0.f, scale_dev, nullptr, s));
   return TK_OK;
 }
 

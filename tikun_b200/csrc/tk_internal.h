@@ -46,6 +46,10 @@ class Scratch {
 
 int sm_count(int* out);
 
+// SMs the pointwise kernels leave free (tk_set_reserved_sms); grids are sized
+// for the remaining ones.
+int pointwise_sms(int* out);
+
 // Where a pointer lives (cudaPointerGetAttributes); device memory of another
 // device is an error.
 enum class Residency { kNone, kDevice, kHost };
@@ -76,6 +80,15 @@ struct LeafTable {
   LeafDesc leaf[kMaxLeavesPerLaunch];
 };
 
+// Other GPUs' copies of the same parameter layout, mapped into this process:
+// a parameter at address a is also stored at a + delta[i] (bytes).
+constexpr int kMaxPeers = 7;
+struct PeerSet {
+  int32_t n;
+  int32_t reserved;
+  int64_t delta[kMaxPeers];
+};
+
 struct PointwiseConsts {
   float lr, b1, b2, eps, decay;
   float omb1, omb2;  // 1 - b1, 1 - b2 in f32
@@ -92,9 +105,14 @@ int launch_clip_scale(const double* sumsq, int n_partials, float max_norm, float
                       cudaStream_t s);
 // Tier 2.  If partials != nullptr every CTA folds partials[0..n_partials) into
 // the clip scale itself (same order in every CTA); else scale_dev (or 1.0).
+// Tier 2 for a table of f32 leaves whose four pointers are 16-byte aligned,
+// through the bulk-copy pipeline (tk_pointwise_bulk.cu).  Same results.
+int launch_pointwise_bulk(const LeafTable& t, int kind, const PointwiseConsts& c,
+                          const double* partials, int n_partials, float max_norm,
+                          const float* scale_dev, float* scale_out, cudaStream_t s);
 int launch_pointwise(const LeafTable& t, int kind, int p_dtype, int g_dtype,
                      const PointwiseConsts& c, const double* partials, int n_partials,
                      float max_norm, const float* scale_dev, float* scale_out,
-                     cudaStream_t s);
+                     cudaStream_t s, const PeerSet* peers = nullptr);
 
 }  // namespace tk

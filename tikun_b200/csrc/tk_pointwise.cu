@@ -15,12 +15,17 @@
 // results are bit-identical to tikun-cpu's.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <cstring>
 
 #include "tk_internal.h"
+#include "tk_pointwise_math.cuh"
 
 namespace tk {
 namespace {
+
+using namespace pw;
 
 // Tuning knobs (compile time): quads each thread keeps in flight per loop
 // trip, the minimum resident CTAs per SM the register budget must allow, and
@@ -36,6 +41,12 @@ namespace {
 #ifndef TK_PW_STREAMING
 #define TK_PW_STREAMING 0
 #endif
+// Grid sizing: 0 = one wave of resident CTAs, each with a long contiguous
+// slice; 1 = one short slice (kThreads * kUnroll groups) per CTA, many waves,
+// so the CTAs sweep memory together.
+#ifndef TK_PW_OVERSUB
+#define TK_PW_OVERSUB 0
+#endif
 constexpr int kThreads = 256;
 constexpr int kUnroll = TK_PW_UNROLL;
 
@@ -49,16 +60,6 @@ template <typename T>
 __device__ __forceinline__ void st_stream(T* p, const T& v) {
   if constexpr (TK_PW_STREAMING) __stcs(p, v);
   else *p = v;
-}
-
-// ------------------------------------------------------------------ dtypes
-__device__ __forceinline__ float bf16_to_f32(uint32_t h) { return __uint_as_float(h << 16); }
-
-__device__ __forceinline__ uint32_t f32_to_bf16(float f) {
-  uint32_t u = __float_as_uint(f);
-  if ((u & 0x7fffffffu) > 0x7f800000u) return ((u >> 16) | 0x40u) & 0xffffu;  // quiet NaN
-  u += 0x7fffu + ((u >> 16) & 1u);                                              // nearest even
-  return u >> 16;
 }
 
 template <int DT>
@@ -97,80 +98,6 @@ __device__ __forceinline__ void store1(void* base, uint64_t e, float x) {
   else static_cast<uint16_t*>(base)[e] = static_cast<uint16_t>(f32_to_bf16(x));
 }
 
-// ------------------------------------------------------------------ update rules
-// AdamW, crates/tikun-cpu/src/lib.rs:258-270 (g already scaled by the caller).
-__device__ __forceinline__ void adamw(float& p, float g, float& m, float& v,
-                                      const PointwiseConsts& k) {
-  m = __fadd_rn(__fmul_rn(k.b1, m), __fmul_rn(k.omb1, g));
-  v = __fadd_rn(__fmul_rn(k.b2, v), __fmul_rn(__fmul_rn(k.omb2, g), g));
-  const float m_hat = __fdiv_rn(m, k.bc1);
-  const float m_hat2 = __fdiv_rn(v, k.bc2);
-  const float step_update =
-      __fadd_rn(__fdiv_rn(m_hat, __fadd_rn(__fsqrt_rn(m_hat2), k.eps)), __fmul_rn(k.decay, p));
-  p = __fsub_rn(p, __fmul_rn(k.lr, step_update));
-}
-
-// Lion, lib.rs:347-358.
-__device__ __forceinline__ void lion(float& p, float g, float& m, const PointwiseConsts& k) {
-  const float c = __fadd_rn(__fmul_rn(k.b1, m), __fmul_rn(k.omb1, g));
-  const float sign_c = c > 0.0f ? 1.0f : (c < 0.0f ? -1.0f : 0.0f);
-  p = __fsub_rn(p, __fmul_rn(k.lr, __fadd_rn(sign_c, __fmul_rn(k.decay, p))));
-  m = __fadd_rn(__fmul_rn(k.b2, m), __fmul_rn(k.omb2, g));
-}
-
-// SGD with momentum, lib.rs:419-427 (momentum carried in b1).
-__device__ __forceinline__ void sgd(float& p, float g, float& m, const PointwiseConsts& k) {
-  m = __fadd_rn(__fmul_rn(k.b1, m), g);
-  const float update = __fadd_rn(m, __fmul_rn(k.decay, p));
-  p = __fsub_rn(p, __fmul_rn(k.lr, update));
-}
-
-template <int KIND>
-__device__ __forceinline__ void apply(float& p, float g, float& m, float& v,
-                                      const PointwiseConsts& k) {
-  if constexpr (KIND == TK_ADAMW) adamw(p, g, m, v, k);
-  else if constexpr (KIND == TK_LION) lion(p, g, m, k);
-  else sgd(p, g, m, k);
-}
-
-// ------------------------------------------------------------------ reductions
-// Deterministic block sum: fixed shuffle tree per warp, then warp 0 adds the
-// warp totals in warp order.  Result valid in thread 0.
-__device__ __forceinline__ double block_sum(double x) {
-  __shared__ double warp_tot[kThreads / 32];
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) x += __shfl_down_sync(0xffffffffu, x, off);
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (lane == 0) warp_tot[wid] = x;
-  __syncthreads();
-  double t = 0.0;
-  if (wid == 0) {
-    t = lane < (kThreads / 32) ? warp_tot[lane] : 0.0;
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) t += __shfl_down_sync(0xffffffffu, t, off);
-  }
-  __syncthreads();
-  return t;
-}
-
-// lib.rs:117-122: norm rounded to f32, scale only if it exceeds max_norm > 0.
-__device__ __forceinline__ float clip_from_sumsq(double total, float max_norm) {
-  const float norm = __double2float_rn(sqrt(total));
-  if (norm > max_norm && max_norm > 0.0f) return __fdiv_rn(max_norm, __fadd_rn(norm, 1e-6f));
-  return 1.0f;
-}
-
-__device__ __forceinline__ int find_leaf(const LeafTable& t, uint64_t q) {
-  int lo = 0, hi = t.n_leaves - 1;  // last leaf with q_begin <= q
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (t.leaf[mid].q_begin <= q) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
-__device__ __forceinline__ uint64_t leaf_quads(const LeafDesc& L) { return (L.n + 3) >> 2; }
-
 // ------------------------------------------------------------------ Tier 1
 template <int GDT>
 __global__ void __launch_bounds__(kThreads)
@@ -205,7 +132,7 @@ sumsq_partials_kernel(const __grid_constant__ LeafTable t, double* __restrict__ 
     }
   }
   // x*x of an f32 value is exact in f64, so fma == multiply-then-add here.
-  const double s = block_sum(acc);
+  const double s = block_sum<kThreads>(acc);
   if (threadIdx.x == 0) partials[blockIdx.x] = s;
 }
 
@@ -213,7 +140,7 @@ __global__ void __launch_bounds__(kThreads)
 sumsq_reduce_kernel(const double* __restrict__ partials, int n, double* __restrict__ total) {
   double acc = 0.0;
   for (int i = threadIdx.x; i < n; i += kThreads) acc += partials[i];
-  const double s = block_sum(acc);
+  const double s = block_sum<kThreads>(acc);
   if (threadIdx.x == 0) *total = s;
 }
 
@@ -222,7 +149,7 @@ clip_scale_kernel(const double* __restrict__ partials, int n, float max_norm,
                   float* __restrict__ scale_out) {
   double acc = 0.0;
   for (int i = threadIdx.x; i < n; i += kThreads) acc += partials[i];
-  const double s = block_sum(acc);
+  const double s = block_sum<kThreads>(acc);
   if (threadIdx.x == 0) *scale_out = clip_from_sumsq(s, max_norm);
 }
 
@@ -232,13 +159,14 @@ template <int KIND, int PDT, int GDT, int SCALE>
 __global__ void __launch_bounds__(kThreads, TK_PW_MINBLOCKS)
 pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
                  const double* __restrict__ partials, int n_partials, float max_norm,
-                 const float* __restrict__ scale_dev, float* __restrict__ scale_out) {
+                 const float* __restrict__ scale_dev, float* __restrict__ scale_out,
+                 const PeerSet peers) {
   float scale = 1.0f;
   if constexpr (SCALE == 1) {
     __shared__ float s_scale;
     double acc = 0.0;
     for (int i = threadIdx.x; i < n_partials; i += kThreads) acc += partials[i];
-    const double s = block_sum(acc);
+    const double s = block_sum<kThreads>(acc);
     if (threadIdx.x == 0) {
       const float sc = clip_from_sumsq(s, max_norm);
       s_scale = sc;
@@ -289,6 +217,8 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         }
         const uint64_t e = (lq + (uint64_t)u * kThreads) * 4;
         store_quad<PDT>(L.p, e, P[u]);
+        for (int r = 0; r < peers.n; ++r)  // the updated parameters, into each peer's copy
+          store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, P[u]);
         store_quad<TK_F32>(L.m, e, M[u]);
         if constexpr (KIND == TK_ADAMW) store_quad<TK_F32>(L.v, e, V[u]);
       }
@@ -304,6 +234,7 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         if constexpr (KIND == TK_ADAMW) v = L.v[e];
         apply<KIND>(p, g, m, v, k);
         store1<PDT>(L.p, e, p);
+        for (int r = 0; r < peers.n; ++r) store1<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, p);
         L.m[e] = m;
         if constexpr (KIND == TK_ADAMW) L.v[e] = v;
       }
@@ -311,32 +242,36 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
     q = seg_end;
     ++li;
   }
+  if (peers.n) __threadfence_system();  // peer stores visible before the kernel ends
 }
 
 template <int KIND, int PDT, int GDT, int SCALE>
 int occupancy_grid(uint64_t total_quads) {
-  static int cap = 0;
-  if (cap == 0) {
-    int sms = 0, per_sm = 0;
-    if (sm_count(&sms) != TK_OK) return 0;
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &per_sm, pointwise_kernel<KIND, PDT, GDT, SCALE>, kThreads, 0) != cudaSuccess ||
-        per_sm < 1)
-      per_sm = 1;
-    cap = sms * per_sm;
+            &occ, pointwise_kernel<KIND, PDT, GDT, SCALE>, kThreads, 0) != cudaSuccess ||
+        occ < 1)
+      occ = 1;
+    per_sm = occ;
   }
+  int sms = 0;
+  if (pointwise_sms(&sms) != TK_OK) return 0;
+  const int cap = sms * per_sm;
   const uint64_t want = (total_quads + kThreads * kUnroll - 1) / (kThreads * kUnroll);
+  if (TK_PW_OVERSUB) return (int)std::min<uint64_t>(want ? want : 1, 1u << 30);
   return (int)(want < (uint64_t)cap ? (want ? want : 1) : cap);
 }
 
 template <int KIND, int PDT, int GDT, int SCALE>
 int launch_t(const LeafTable& t, const PointwiseConsts& c, const double* partials,
              int n_partials, float max_norm, const float* scale_dev, float* scale_out,
-             cudaStream_t s) {
+             cudaStream_t s, const PeerSet& peers) {
   const int grid = occupancy_grid<KIND, PDT, GDT, SCALE>(t.total_quads);
   if (grid <= 0) return set_error(TK_ERR_CUDA, "could not size the pointwise grid");
   pointwise_kernel<KIND, PDT, GDT, SCALE><<<grid, kThreads, 0, s>>>(
-      t, c, partials, n_partials, max_norm, scale_dev, scale_out);
+      t, c, partials, n_partials, max_norm, scale_dev, scale_out, peers);
   TK_CUDA_TRY(cudaGetLastError());
   return TK_OK;
 }
@@ -344,35 +279,37 @@ int launch_t(const LeafTable& t, const PointwiseConsts& c, const double* partial
 template <int KIND, int PDT, int GDT>
 int launch_scale(const LeafTable& t, const PointwiseConsts& c, const double* partials,
                  int n_partials, float max_norm, const float* scale_dev, float* scale_out,
-                 cudaStream_t s) {
-  if (partials) return launch_t<KIND, PDT, GDT, 1>(t, c, partials, n_partials, max_norm, nullptr, scale_out, s);
-  if (scale_dev) return launch_t<KIND, PDT, GDT, 2>(t, c, nullptr, 0, 0.f, scale_dev, nullptr, s);
-  return launch_t<KIND, PDT, GDT, 0>(t, c, nullptr, 0, 0.f, nullptr, nullptr, s);
+                 cudaStream_t s, const PeerSet& pr) {
+  if (partials) return launch_t<KIND, PDT, GDT, 1>(t, c, partials, n_partials, max_norm, nullptr, scale_out, s, pr);
+  if (scale_dev) return launch_t<KIND, PDT, GDT, 2>(t, c, nullptr, 0, 0.f, scale_dev, nullptr, s, pr);
+  return launch_t<KIND, PDT, GDT, 0>(t, c, nullptr, 0, 0.f, nullptr, nullptr, s, pr);
 }
 
 template <int KIND>
 int launch_kind(const LeafTable& t, int pdt, int gdt, const PointwiseConsts& c,
                 const double* partials, int n_partials, float max_norm, const float* scale_dev,
-                float* scale_out, cudaStream_t s) {
-  if (pdt == TK_F32 && gdt == TK_F32) return launch_scale<KIND, TK_F32, TK_F32>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
-  if (pdt == TK_F32 && gdt == TK_BF16) return launch_scale<KIND, TK_F32, TK_BF16>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
-  if (pdt == TK_BF16 && gdt == TK_F32) return launch_scale<KIND, TK_BF16, TK_F32>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
-  if (pdt == TK_BF16 && gdt == TK_BF16) return launch_scale<KIND, TK_BF16, TK_BF16>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+                float* scale_out, cudaStream_t s, const PeerSet& pr) {
+  if (pdt == TK_F32 && gdt == TK_F32) return launch_scale<KIND, TK_F32, TK_F32>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
+  if (pdt == TK_F32 && gdt == TK_BF16) return launch_scale<KIND, TK_F32, TK_BF16>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
+  if (pdt == TK_BF16 && gdt == TK_F32) return launch_scale<KIND, TK_BF16, TK_F32>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
+  if (pdt == TK_BF16 && gdt == TK_BF16) return launch_scale<KIND, TK_BF16, TK_BF16>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
   return set_error(TK_ERR_INVALID, "unsupported dtype pair p=%d g=%d", pdt, gdt);
 }
 
 }  // namespace
 
 int sumsq_blocks_for(uint64_t total_quads) {
-  static int cap = 0;
-  if (cap == 0) {
-    int sms = 0, per_sm = 0;
-    if (sm_count(&sms) != TK_OK) return 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, sumsq_partials_kernel<TK_F32>,
-                                                      kThreads, 0) != cudaSuccess || per_sm < 1)
-      per_sm = 1;
-    cap = sms * per_sm;
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, sumsq_partials_kernel<TK_F32>,
+                                                      kThreads, 0) != cudaSuccess || occ < 1)
+      occ = 1;
+    per_sm = occ;
   }
+  int sms = 0;
+  if (pointwise_sms(&sms) != TK_OK) return 0;
+  const int cap = sms * per_sm;
   const uint64_t want = (total_quads + kThreads - 1) / kThreads;
   return (int)(want < (uint64_t)cap ? (want ? want : 1) : cap);
 }
@@ -401,11 +338,15 @@ int launch_clip_scale(const double* sumsq, int n_partials, float max_norm, float
 
 int launch_pointwise(const LeafTable& t, int kind, int p_dtype, int g_dtype,
                      const PointwiseConsts& c, const double* partials, int n_partials,
-                     float max_norm, const float* scale_dev, float* scale_out, cudaStream_t s) {
+                     float max_norm, const float* scale_dev, float* scale_out, cudaStream_t s,
+                     const PeerSet* peers) {
+  PeerSet none;
+  std::memset(&none, 0, sizeof(none));
+  const PeerSet& pr = peers ? *peers : none;
   switch (kind) {
-    case TK_ADAMW: return launch_kind<TK_ADAMW>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
-    case TK_LION: return launch_kind<TK_LION>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
-    case TK_SGD: return launch_kind<TK_SGD>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+    case TK_ADAMW: return launch_kind<TK_ADAMW>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
+    case TK_LION: return launch_kind<TK_LION>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
+    case TK_SGD: return launch_kind<TK_SGD>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
     default: return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   }
 }

@@ -1,0 +1,207 @@
+"""ZeRO-1 pointwise optimizer step across ranks (one process per GPU).
+
+Ownership is chunk-major: the flat parameter arena is cut into ``chunks``
+super-chunks and every super-chunk is split evenly across the ranks, so rank r
+owns one contiguous piece of each.  A step is
+
+1. Tier 1 on the rank's pieces (f64 partial sum of g^2), one all-reduce of that
+   double, the clip scale (crates/tikun-cpu/src/lib.rs:79-125);
+2. per super-chunk: Tier 2 on the rank's piece, then an in-place all-gather of
+   that super-chunk, issued right away so it overlaps the next piece's update.
+
+With ``fused=True`` there is no all-gather: every rank maps the other ranks'
+parameter arenas into its address space (CUDA IPC) and the update kernel
+stores each new parameter into the local arena and into every peer's copy
+over NVLink as it produces it (tk_apply_pointwise_peers), so the exchange
+overlaps the arithmetic.  One 8-byte all-reduce on the same stream after the
+update is the end-of-step barrier: no rank reads its arena before every peer
+has finished writing into it.
+
+Optimizer state (m, v) exists only for the rank's pieces.  Results are
+identical to the single-GPU step: the update is element-wise and the clip
+scale comes from the same global sum (up to f64 summation order).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import _native
+from .arena import LayoutPlan
+
+
+def chunk_major_pieces(total: int, world: int, rank: int, chunks: int,
+                       align: int = 16) -> list[tuple[int, int]]:
+    """[lo, hi) ranges of the flat arena owned by ``rank``: one per
+    super-chunk.  ``total`` must be a multiple of chunks * world * align."""
+    if total % (chunks * world * align) != 0:
+        raise ValueError(f"arena of {total} elements does not split into {chunks} chunks x "
+                         f"{world} ranks x {align}-element granules")
+    sup = total // chunks
+    per = sup // world
+    return [(c * sup + rank * per, c * sup + (rank + 1) * per) for c in range(chunks)]
+
+
+def pieces_to_segments(plan: LayoutPlan, lo: int, hi: int) -> list[tuple[int, int, int]]:
+    """(leaf, start within leaf, count) of the leaf elements inside [lo, hi)."""
+    out = []
+    for i, (off, n) in enumerate(plan.slots):
+        a, b = max(off, lo), min(off + n, hi)
+        if a < b:
+            out.append((i, a - off, b - a))
+    return out
+
+
+@dataclass
+class ZeroHParams:
+    lr: float = 1e-3
+    beta1: float = 0.9
+    beta2: float = 0.999
+    eps: float = 1e-8
+    weight_decay: float = 0.01
+    max_norm: float = 0.0
+    kind: str = "adamw"
+
+
+class ZeroPointwise:
+    """ZeRO-1 AdamW/Lion/SGD over f32 parameter and gradient arenas (flat
+    tensors laid out by ``plan``, replicated on every rank)."""
+
+    def __init__(self, plan: LayoutPlan, p_flat: torch.Tensor, g_flat: torch.Tensor,
+                 hp: ZeroHParams, group=None, chunks: int = 4, fused: bool = False):
+        self.plan, self.p, self.g, self.hp, self.group = plan, p_flat, g_flat, hp, group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.chunks = chunks
+        self.pieces = chunk_major_pieces(plan.total, self.world, self.rank, chunks)
+        self.kind = _native.opt_kind(hp.kind)
+        owned = sum(hi - lo for lo, hi in self.pieces)
+        dev = p_flat.device
+        self.m = torch.zeros(owned, dtype=torch.float32, device=dev)
+        self.v = torch.zeros(owned, dtype=torch.float32, device=dev)
+        self.sumsq = torch.zeros(1, dtype=torch.float64, device=dev)
+        self.scale = torch.ones(1, dtype=torch.float32, device=dev)
+        self.step_count = 0
+        # one leaf table per piece (C ABI leaves), plus one over all pieces for Tier 1
+        self.tables = []
+        base_p, base_g = p_flat.data_ptr(), g_flat.data_ptr()
+        base_m, base_v = self.m.data_ptr(), self.v.data_ptr()
+        state_off = 0
+        all_segs = []
+        for lo, hi in self.pieces:
+            segs = pieces_to_segments(plan, lo, hi)
+            flat = [plan.slots[i][0] + a for i, a, c in segs]
+            local = [state_off + (f - lo) for f in flat]
+            leaves = _native.make_leaves([base_p + 4 * f for f in flat], [base_g + 4 * f for f in flat],
+                                         [base_m + 4 * x for x in local], [base_v + 4 * x for x in local],
+                                         [c for _, _, c in segs])
+            self.tables.append(leaves)
+            all_segs.extend(zip(flat, local, [c for _, _, c in segs]))
+            state_off += hi - lo
+        self.all_leaves = _native.make_leaves([base_p + 4 * f for f, _, _ in all_segs],
+                                              [base_g + 4 * f for f, _, _ in all_segs],
+                                              [base_m + 4 * x for _, x, _ in all_segs],
+                                              [base_v + 4 * x for _, x, _ in all_segs],
+                                              [c for _, _, c in all_segs])
+        self.launches_per_step = 0
+        self.fused = fused and self.world > 1
+        self.peer_ptrs: list[int] = []
+        if self.fused:
+            self._map_peers()
+
+    def _map_peers(self) -> None:
+        """Exchange IPC handles of every rank's parameter arena and map the
+        peers' arenas; peer_deltas[i] = peer address - local address."""
+        if self.p.dtype != torch.float32 or not self.p.is_contiguous():
+            raise ValueError("fused ZeRO-1 needs a contiguous f32 parameter arena")
+        L = _native.lib()
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _native.check(L.tk_ipc_export(self.p.data_ptr(), handle, ctypes.byref(off)))
+        mine = (bytes(handle.raw), int(off.value), self.plan.total)
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine, group=self.group)
+        deltas = []
+        for r, (h, o, total) in enumerate(everyone):
+            if total != self.plan.total:
+                raise ValueError(f"rank {r} has an arena of {total} elements, "
+                                 f"this rank {self.plan.total}")
+            if r == self.rank:
+                continue
+            ptr = ctypes.c_void_p()
+            _native.check(L.tk_ipc_import(h, o, ctypes.byref(ptr)))
+            self.peer_ptrs.append(ptr.value)
+            deltas.append(ptr.value - self.p.data_ptr())
+        self.peer_deltas = (ctypes.c_int64 * max(len(deltas), 1))(*deltas)
+        self.barrier_buf = torch.zeros(1, dtype=torch.float64, device=self.p.device)
+
+    def close(self) -> None:
+        """Unmaps the peers' arenas (fused mode); call on every rank, before
+        the process group is destroyed."""
+        if self.peer_ptrs:
+            torch.cuda.synchronize(self.p.device)
+            if dist.is_initialized():
+                dist.barrier(group=self.group)
+            L = _native.lib()
+            for p in self.peer_ptrs:
+                _native.check(L.tk_ipc_close(ctypes.c_void_p(p)))
+            self.peer_ptrs = []
+
+    def step(self, update_events=None) -> None:
+        """One optimizer step on the current stream; returns once everything
+        (the all-gathers included) is enqueued on it."""
+        self.step_count += 1
+        L = _native.lib()
+        s = torch.cuda.current_stream(self.p.device).cuda_stream
+        hp = _native.TkHParams(self.hp.lr, self.hp.beta1, self.hp.beta2, self.hp.eps,
+                               self.hp.weight_decay)
+        launches = 0
+        clip = self.hp.max_norm > 0
+        if clip:
+            _native.check(L.tk_grad_sumsq(self.all_leaves[0], self.all_leaves[1],
+                                          self.sumsq.data_ptr(), s))
+            if self.world > 1:
+                dist.all_reduce(self.sumsq, group=self.group)
+            _native.check(L.tk_clip_scale(self.sumsq.data_ptr(), self.hp.max_norm,
+                                          self.scale.data_ptr(), s))
+            launches += 3
+        if self.fused:
+            if not clip:
+                # the norm all-reduce is not there to order this update after
+                # every peer's reads of its arena from the previous step
+                dist.all_reduce(self.barrier_buf, group=self.group)
+            if update_events is not None:
+                update_events[0].record()
+            leaves, n = self.all_leaves
+            _native.check(L.tk_apply_pointwise_peers(leaves, n, self.kind, ctypes.byref(hp),
+                                                     self.step_count,
+                                                     self.scale.data_ptr() if clip else None,
+                                                     self.peer_deltas, len(self.peer_ptrs), s))
+            if update_events is not None:
+                update_events[1].record()
+            # every peer has written into this arena once this completes
+            dist.all_reduce(self.barrier_buf, group=self.group)
+            self.launches_per_step = launches + 1
+            return
+        works = []
+        sup = self.plan.total // self.chunks
+        for c, (leaves, n) in enumerate(self.tables):
+            if update_events is not None and c == 0:
+                update_events[0].record()
+            _native.check(L.tk_apply_pointwise(leaves, n, self.kind, ctypes.byref(hp),
+                                               self.step_count,
+                                               self.scale.data_ptr() if clip else None, s))
+            launches += 1
+            if update_events is not None and c == len(self.tables) - 1:
+                update_events[1].record()
+            if self.world > 1:
+                lo, hi = self.pieces[c]
+                works.append(dist.all_gather_into_tensor(self.p[c * sup:(c + 1) * sup],
+                                                         self.p[lo:hi], group=self.group,
+                                                         async_op=True))
+        for w in works:
+            w.wait()
+        self.launches_per_step = launches
