@@ -273,13 +273,13 @@ def timed_loop(step_fn, steps, warmup, stream, world, dist, dev, torch, uuid, be
 def run_pointwise(args, wl, world, rank, dev, torch, dist):
     from tikun_b200 import _native
     from tikun_b200.arena import Arena, LayoutPlan
+    from tikun_b200.distributed import pieces_to_segments
 
     L = _native.lib()
     stream = torch.cuda.current_stream()
     s_handle = stream.cuda_stream
     fused = world > 1 and args.zero == "fused"
-    chunks = 4 if world > 1 and not fused else 1
-    plan = LayoutPlan(wl["sizes"], pad_to=16 * max(world, 1) * chunks)
+    plan = LayoutPlan(wl["sizes"], pad_to=16 * max(world, 1))
     hp_np, hg_np = make_host_state(wl)
     P, G = (Arena(plan, device=dev) for _ in range(2))
     for i in range(len(plan)):
@@ -287,7 +287,7 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         G.leaf(i).copy_(torch.from_numpy(hg_np[i]))
     n_params = sum(wl["sizes"])
     hp = _native.TkHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"])
-    state = {"step": 0, "ev": None, "k": None}
+    state = {"step": 0, "ev": None}
     clip = wl["max_norm"] > 0
     if world == 1:
         M, V = (Arena(plan, device=dev) for _ in range(2))
@@ -304,19 +304,21 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
                                                   wl["max_norm"], scale_dev.data_ptr(), s_handle))
             return 2 if clip else 1
     else:
-        # ZeRO-1: the update kernel stores into the peers' arenas (fused), or
-        # each super-chunk's all-gather overlaps the update of the next
-        from tikun_b200.distributed import ZeroHParams, ZeroPointwise
+        # ZeRO-1 through the C ABI (tk_shard_*): the update kernel stores into
+        # the peers' arenas (peers), or an all-gather follows it
+        from tikun_b200.distributed import ShardedStep, ZeroHParams
 
-        zp = ZeroPointwise(plan, P.flat, G.flat,
-                           ZeroHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"],
-                                       wl["max_norm"]), chunks=chunks, fused=fused)
-        my_params = sum(zp.all_leaves[0][i].n for i in range(zp.all_leaves[1]))
+        zp = ShardedStep(plan, P.flat, G.flat,
+                         ZeroHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"],
+                                     wl["max_norm"]),
+                         exchange="peers" if fused else "allgather")
+        my_params = sum(n for _, _, n in pieces_to_segments(plan, zp.lo, zp.hi))
 
         def one_step():
-            k = state["k"]
-            zp.step(update_events=ev_pairs[k] if k is not None else None)
-            return zp.launches_per_step
+            ev = state["ev"]
+            _native.check(L.tk_set_update_events(*(ev if ev else (None, None))))
+            zp.step()
+            return 4 if clip else 1  # norm partials, norm reduce, clip scale, update
 
     ev_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(args.steps)]
@@ -324,17 +326,13 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         a.record(stream)
         b.record(stream)
 
-    def before(k):
-        if world == 1:  # the library records them around its update launches
-            state["ev"] = (ev_pairs[k][0].cuda_event, ev_pairs[k][1].cuda_event)
-        else:
-            state["k"] = k
+    def before(k):  # the library records them around its update launches
+        state["ev"] = (ev_pairs[k][0].cuda_event, ev_pairs[k][1].cuda_event)
 
     uuid = str(torch.cuda.get_device_properties(dev).uuid)
     ms_total, launches, clocks = timed_loop(one_step, args.steps, args.warmup, stream, world, dist,
                                             dev, torch, uuid, before)
     state["ev"] = None
-    state["k"] = None
     _native.check(L.tk_set_update_events(None, None))
     if world > 1:
         zp.close()
@@ -353,34 +351,61 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
             traffic = tr["bytes_per_param"] * my_params
 
     e2e = None
-    if not args.no_e2e and world == 1:
-        hp_pin = [torch.from_numpy(x).pin_memory() for x in hp_np]
-        hg_pin = [torch.from_numpy(x).pin_memory() for x in hg_np]
-        hm_pin = [torch.zeros(n).pin_memory() for n in wl["sizes"]]
-        hv_pin = [torch.zeros(n).pin_memory() for n in wl["sizes"]]
+    if not args.no_e2e:
+        # pinned host leaves: the whole PyTree on one GPU (tk_step_buffers), or
+        # each rank's ZeRO-1 slice of it (tk_step_buffers_sharded, the Tier-1
+        # sum all-reduced over NCCL)
+        if world == 1:
+            segs = [(i, 0, n) for i, n in enumerate(wl["sizes"])]
+        else:
+            segs = pieces_to_segments(plan, zp.lo, zp.hi)
+        hp_pin = [torch.from_numpy(hp_np[i][a:a + n]).pin_memory() for i, a, n in segs]
+        hg_pin = [torch.from_numpy(hg_np[i][a:a + n]).pin_memory() for i, a, n in segs]
+        hm_pin = [torch.zeros(n).pin_memory() for _, _, n in segs]
+        hv_pin = [torch.zeros(n).pin_memory() for _, _, n in segs]
         hleaves, hn = _native.make_leaves([t.data_ptr() for t in hp_pin],
                                           [t.data_ptr() for t in hg_pin],
                                           [t.data_ptr() for t in hm_pin],
-                                          [t.data_ptr() for t in hv_pin], wl["sizes"])
+                                          [t.data_ptr() for t in hv_pin], [n for _, _, n in segs])
         out = ctypes.c_float()
+        comm = None
+        if world > 1:
+            from tikun_b200.distributed import nccl_comm_ptr
+            comm = nccl_comm_ptr(None, dev)
+
+        def host_step(k):
+            if comm is None:
+                _native.check(L.tk_step_buffers(hleaves, hn, _native.TK_ADAMW, ctypes.byref(hp),
+                                                k, wl["max_norm"], ctypes.byref(out), s_handle))
+            else:
+                _native.check(L.tk_step_buffers_sharded(hleaves, hn, _native.TK_ADAMW,
+                                                        ctypes.byref(hp), k, wl["max_norm"],
+                                                        ctypes.byref(out), comm, s_handle))
+
         e2e_steps = max(3, min(args.steps, 10))
-        for s in range(3):
-            _native.check(L.tk_step_buffers(hleaves, hn, _native.TK_ADAMW, ctypes.byref(hp), s + 1,
-                                            wl["max_norm"], ctypes.byref(out), s_handle))
+        for k in range(3):
+            host_step(k + 1)
         torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for s in range(e2e_steps):
-            _native.check(L.tk_step_buffers(hleaves, hn, _native.TK_ADAMW, ctypes.byref(hp), s + 4,
-                                            wl["max_norm"], ctypes.byref(out), s_handle))
+        for k in range(e2e_steps):
+            host_step(k + 4)
         e1.record(stream)
         torch.cuda.synchronize()
         e_ms = e0.elapsed_time(e1) / e2e_steps
+        if world > 1:
+            t = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
         e2e = {"value": n_params / (e_ms / 1e3), "unit": "params/s", "ms_per_step": e_ms,
-               "h2d_bytes_per_step": 16 * n_params, "d2h_bytes_per_step": 12 * n_params + 4,
+               "h2d_bytes_per_step": 16 * n_params, "d2h_bytes_per_step": 12 * n_params + 4 * world,
                "steps": e2e_steps, "host_memory": "pinned",
-               "api": "tk_step_buffers with pinned host leaves: g copied to HBM for the clip, "
-                      "p/m/v streamed over the host link by the update kernel"}
+               "api": ("tk_step_buffers" if world == 1 else
+                       f"tk_step_buffers_sharded on each of {world} ranks over its ZeRO-1 slice") +
+                      " with pinned host leaves: g copied to HBM for the clip, p/m/v streamed "
+                      "through the copy engines around the update kernel; bytes are whole-job"}
         del hp_pin, hg_pin, hm_pin, hv_pin
 
     cpu = None
@@ -390,15 +415,16 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
                "sample": f"full workload, 2 timed steps after 1 warm-up, {nthreads} threads over "
                          f"leaves ({cms:.0f} ms/step)"}
-    return {
+    res = {
         "value": value, "ms_per_step": ms_step, "dtype": "f32", "scaling": "strong",
         "data": "synthetic (seeded N(0,0.02) params, N(0,%g) grads held fixed across steps)"
                 % wl["g_std"],
         "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
                    "leaves": len(wl["sizes"]),
                    "parallelism": "single GPU" if world == 1 else
-                   f"zero1-dp{world} (update kernel stores into peer arenas over NVLink)" if fused
-                   else f"zero1-dp{world} (chunk-major, all-gather overlapped with the update)",
+                   f"zero1-dp{world} via tk_shard_step (update kernel stores into peer arenas "
+                   "over NVLink)" if fused else
+                   f"zero1-dp{world} via tk_shard_step (ncclAllGather after the update)",
                    "l2": "inputs (p,g,m,v) larger than L2; no flush"},
         "roofline": {"bound": "hbm", "kernel": "pointwise_kernel (AdamW update)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
@@ -407,6 +433,19 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
                      "step_GBps": (32 if clip else 28) * n_params / (ms_step / 1e3) / 1e9},
         "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu,
     }
+    if fused:
+        # the update kernel also writes 4 B per owned parameter to each peer
+        # over NVLink and receives the peers' slices into its own HBM: its
+        # target time is the slower of HBM and NVLink (measured 770 GB/s per
+        # direction per GPU)
+        nvl_bytes = 4 * my_params * (world - 1)
+        hbm_bytes = upd_bytes + 4 * (n_params - my_params)
+        target_ms = max(hbm_bytes / (peak * 1e9), nvl_bytes / 770e9) * 1e3
+        res["roofline"]["fused_exchange"] = {
+            "nvlink_bytes_per_launch": nvl_bytes, "nvlink_peak_GBps": 770,
+            "hbm_bytes_per_launch": hbm_bytes, "target_ms": target_ms,
+            "frac_of_target": target_ms / upd_ms}
+    return res
 
 
 def run_muon(args, wl, world, rank, dev, torch, dist):

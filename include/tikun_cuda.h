@@ -250,6 +250,63 @@ TK_API int tk_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out
 TK_API int tk_ipc_import(const void* handle, uint64_t offset, void** ptr_out);
 TK_API int tk_ipc_close(void* ptr);
 
+/* ---------------------------------------------------------------------- */
+/* ZeRO-1 over NCCL (one process per GPU)                                  */
+/* ---------------------------------------------------------------------- */
+
+/* The multi-GPU form of tk_step_buffers (the reference's step_fast_buffers,
+ * tikun-py/src/lib.rs:155-222, has no multi-GPU counterpart; this follows
+ * the sharding of its arena, crates/tikun-core/src/arena.rs:34-103).  Every
+ * rank holds the full f32 parameter and gradient arenas, leaf i at element
+ * offset leaf_offsets[i] with leaf_sizes[i] elements (ascending, disjoint;
+ * padding between leaves is never touched).  Rank r of W owns elements
+ * [r*n/W, (r+1)*n/W) -- n_elems must be a multiple of 16*W -- and keeps the
+ * optimizer state for those only.  tk_shard_step: Tier 1 on the owned
+ * elements, one f64 ncclAllReduce, the clip scale, Tier 2 on the owned
+ * elements, then the exchange of the updated parameters:
+ *   TK_SHARD_PEERS      the update kernel also stores them into every other
+ *                       rank's arena (CUDA IPC mappings; all ranks on one
+ *                       node, W <= 8) and an 8-byte all-reduce closes the
+ *                       step;
+ *   TK_SHARD_ALLGATHER  an in-place ncclAllGather follows the update.
+ * All calls are collective over nccl_comm (an ncclComm_t; from PyTorch,
+ * ProcessGroupNCCL._comm_ptr()), made on the communicator's device, in the
+ * same order on every rank.  clip_scale_out (host, may be NULL) receives the
+ * step's clip scale (1 without clipping) and makes the call synchronous.
+ * NCCL is resolved at run time from the libnccl.so.2 loaded in the process. */
+typedef struct tk_shard tk_shard;
+enum { TK_SHARD_ALLGATHER = 0, TK_SHARD_PEERS = 1 };
+
+/* tk_step_buffers for one rank's share of a PyTree split across the ranks of
+ * nccl_comm (any split: whole leaves or pieces of leaves, each element on one
+ * rank): the Tier-1 f64 sum is all-reduced over the communicator before the
+ * clip scale is formed, so every rank clips with the global norm.  Leaves may
+ * be device or host buffers as for tk_step_buffers (pinned host leaves stream
+ * through the copy engines).  Collective when max_norm > 0; a rank holding no
+ * elements still calls it.  No parameter exchange: ranks whose leaves live in
+ * one shared host arena need none. */
+TK_API int tk_step_buffers_sharded(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                                   const tk_hparams* hp, uint64_t step, float max_norm,
+                                   float* clip_scale_out, void* nccl_comm, void* stream);
+#define TK_NCCL_ID_BYTES 128
+
+TK_API int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_t n_elems,
+                         const uint64_t* leaf_offsets, const uint64_t* leaf_sizes,
+                         size_t n_leaves, int32_t kind, int32_t exchange, void* stream,
+                         tk_shard** out);
+TK_API int tk_shard_step(tk_shard* shard, const tk_hparams* hp, uint64_t step, float max_norm,
+                         float* clip_scale_out, void* stream);
+/* The owned element range and its optimizer state (v is NULL unless AdamW). */
+TK_API int tk_shard_info(const tk_shard* shard, uint64_t* lo, uint64_t* hi, float** m, float** v);
+/* Collective; waits for the stream, then unmaps the peers and frees the state. */
+TK_API int tk_shard_destroy(tk_shard* shard, void* stream);
+
+/* A communicator without PyTorch: rank 0 makes the id (TK_NCCL_ID_BYTES),
+ * every rank passes the same bytes to tk_nccl_comm_init. */
+TK_API int tk_nccl_unique_id(void* id_out);
+TK_API int tk_nccl_comm_init(const void* id, int world, int rank, void** comm_out);
+TK_API int tk_nccl_comm_destroy(void* comm);
+
 /* Leaves `sms` SMs of every device free of pointwise (Tier 1 / Tier 2) CTAs,
  * so that kernels launched concurrently on other streams -- NCCL all-gathers
  * overlapping a sharded update -- can run at the same time.  Process-wide;

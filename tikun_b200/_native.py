@@ -131,6 +131,18 @@ _SIGNATURES = {
     "tk_ipc_export": [_P, _P, ctypes.POINTER(_U64)],
     "tk_ipc_import": [_P, _U64, ctypes.POINTER(_P)],
     "tk_ipc_close": [_P],
+    "tk_step_buffers_sharded": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,
+                                ctypes.c_float, ctypes.POINTER(ctypes.c_float), _P, _P],
+    "tk_shard_init": [_P, _P, _P, _U64, ctypes.POINTER(_U64), ctypes.POINTER(_U64), _SZ, _I32,
+                      _I32, _P, ctypes.POINTER(_P)],
+    "tk_shard_step": [_P, ctypes.POINTER(TkHParams), _U64, ctypes.c_float,
+                      ctypes.POINTER(ctypes.c_float), _P],
+    "tk_shard_info": [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_P),
+                      ctypes.POINTER(_P)],
+    "tk_shard_destroy": [_P, _P],
+    "tk_nccl_unique_id": [_P],
+    "tk_nccl_comm_init": [_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)],
+    "tk_nccl_comm_destroy": [_P],
     "tk_step_buffers_noalloc": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams),
                                 _U64, _F, ctypes.POINTER(_F), _P],
     "tk_newton_schulz_2d": [_P, _I64, _I64, _I32, _I32, _I32, _P],

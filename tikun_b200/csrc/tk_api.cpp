@@ -32,6 +32,8 @@ int set_error(int code, const char* fmt, ...) {
   return code;
 }
 
+void clear_error() { g_last_error.clear(); }
+
 int cuda_error(cudaError_t e, const char* what) {
   return set_error(TK_ERR_CUDA, "CUDA error %s (%s) in %s", cudaGetErrorName(e),
                    cudaGetErrorString(e), what);
@@ -354,8 +356,11 @@ static int launch_table(const Plan& plan, size_t i, int kind, const PointwiseCon
 }
 
 // Tier 1 partials for every table into one buffer; returns the block count.
+// With a communicator (the leaves are this rank's share of a sharded PyTree)
+// the partials are summed into one f64, all-reduced over it, and that global
+// sum is returned as the single partial.
 static int launch_norm(const Plan& plan, Scratch* scratch, double** partials, int* n_partials,
-                       cudaStream_t s) {
+                       cudaStream_t s, void* comm = nullptr) {
   std::vector<int> blocks;
   int total = 0;
   for (const LeafTable& t : plan.tables) {
@@ -373,6 +378,14 @@ static int launch_norm(const Plan& plan, Scratch* scratch, double** partials, in
   }
   *partials = base;
   *n_partials = total;
+  if (comm != nullptr) {
+    double* sum = base + total;  // inside the 64 spare bytes
+    if (total > 0) TK_TRY(launch_sumsq_reduce(base, total, sum, s));
+    else TK_CUDA_TRY(cudaMemsetAsync(sum, 0, sizeof(double), s));
+    TK_TRY(nccl_allreduce_sum_f64(sum, 1, comm, s));
+    *partials = sum;
+    *n_partials = 1;
+  }
   return TK_OK;
 }
 
@@ -380,19 +393,33 @@ static int launch_norm(const Plan& plan, Scratch* scratch, double** partials, in
 static thread_local cudaEvent_t g_update_start = nullptr;
 static thread_local cudaEvent_t g_update_stop = nullptr;
 
+int record_update_event(bool start, cudaStream_t s) {
+  cudaEvent_t e = start ? g_update_start : g_update_stop;
+  if (e) TK_CUDA_TRY(cudaEventRecord(e, s));
+  return TK_OK;
+}
+
 // The device-resident step.  scale_dev (may be null) receives the clip scale.
 static int step_device(const tk_leaf* leaves, size_t n, int kind, const tk_hparams& hp,
                        uint64_t step, float max_norm, float* scale_dev, bool* scale_written,
-                       cudaStream_t s) {
+                       cudaStream_t s, void* comm = nullptr) {
   *scale_written = false;
   Plan plan;
   make_plan(leaves, n, kind, &plan);
-  if (plan.tables.empty()) return TK_OK;  // nothing to update; the scale is 1
+  const bool join = comm != nullptr && max_norm > 0.0f;  // the norm all-reduce is collective
+  if (plan.tables.empty() && !join) return TK_OK;  // nothing to update; the scale is 1
   const PointwiseConsts c = make_consts(kind, hp, step);
   Scratch norm_scratch;
   double* partials = nullptr;
   int n_partials = 0;
-  if (max_norm > 0.0f) TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s));
+  if (max_norm > 0.0f) TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s, comm));
+  if (plan.tables.empty()) {  // a rank holding no elements still reports the global scale
+    if (scale_dev != nullptr) {
+      TK_TRY(launch_clip_scale(partials, n_partials, max_norm, scale_dev, s));
+      *scale_written = true;
+    }
+    return TK_OK;
+  }
   if (g_update_start) TK_CUDA_TRY(cudaEventRecord(g_update_start, s));
   for (size_t i = 0; i < plan.tables.size(); ++i)
     TK_TRY(launch_table(plan, i, kind, c, partials, n_partials, max_norm, nullptr,
@@ -466,7 +493,7 @@ struct Piece {
 // clip, all of g is copied first and Tier 1 runs on it before any update.
 static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const tk_hparams& hp,
                                uint64_t step, float max_norm, float* clip_scale_out,
-                               cudaStream_t s) {
+                               cudaStream_t s, void* comm = nullptr) {
   constexpr uint64_t kChunkElems = 8u << 20;
   constexpr int kMaxPieces = kMaxLeavesPerLaunch;
   HostPipe* P = nullptr;
@@ -493,6 +520,20 @@ static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const 
     }
   }
   if (chunks.empty()) {
+    if (comm != nullptr && clip) {  // join the collective norm; nothing to update
+      Scratch sc, norm_scratch;
+      TK_TRY(sc.alloc(64, s));
+      float* scale_dev = static_cast<float*>(sc.get());
+      double* partials = nullptr;
+      int n_partials = 0;
+      TK_TRY(launch_norm(Plan(), &norm_scratch, &partials, &n_partials, s, comm));
+      TK_TRY(launch_clip_scale(partials, n_partials, max_norm, scale_dev, s));
+      float scale = 1.0f;
+      TK_CUDA_TRY(cudaMemcpyAsync(&scale, scale_dev, 4, cudaMemcpyDeviceToHost, s));
+      TK_CUDA_TRY(cudaStreamSynchronize(s));
+      if (clip_scale_out) *clip_scale_out = scale;
+      return TK_OK;
+    }
     if (clip_scale_out) *clip_scale_out = 1.0f;
     return TK_OK;
   }
@@ -536,7 +577,7 @@ static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const 
     for (size_t i = 0; i < n; ++i) gl[i].g = gdev + goff[i];
     Plan plan;
     make_plan(gl.data(), n, TK_SGD, &plan);  // Tier 1 reads g only
-    TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s));
+    TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s, comm));
   }
 
   for (size_t ci = 0; ci < chunks.size(); ++ci) {
@@ -607,7 +648,8 @@ static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const 
 // Pageable host leaves: copy everything the step touches into device scratch,
 // run the device step there and copy p, m, v back.  Synchronous.
 static int step_host(const tk_leaf* leaves, size_t n, int kind, const tk_hparams& hp,
-                     uint64_t step, float max_norm, float* clip_scale_out, cudaStream_t s) {
+                     uint64_t step, float max_norm, float* clip_scale_out, cudaStream_t s,
+                     void* comm = nullptr) {
   size_t bytes = 64;
   for (size_t i = 0; i < n; ++i) {
     const tk_leaf& L = leaves[i];
@@ -642,7 +684,7 @@ static int step_host(const tk_leaf* leaves, size_t n, int kind, const tk_hparams
       TK_CUDA_TRY(cudaMemcpyAsync(dev[i].v, L.v, L.n * 4, cudaMemcpyHostToDevice, s));
   }
   bool written = false;
-  TK_TRY(step_device(dev.data(), n, kind, hp, step, max_norm, scale_dev, &written, s));
+  TK_TRY(step_device(dev.data(), n, kind, hp, step, max_norm, scale_dev, &written, s, comm));
   for (size_t i = 0; i < n; ++i) {
     const tk_leaf& L = leaves[i];
     if (L.n == 0) continue;
@@ -660,7 +702,7 @@ static int step_host(const tk_leaf* leaves, size_t n, int kind, const tk_hparams
 
 static int step_entry(const tk_leaf* leaves, size_t n, int kind, const tk_hparams* hp,
                       uint64_t step, float max_norm, float* clip_scale_out, float* scale_dev,
-                      bool sync, cudaStream_t s) {
+                      bool sync, cudaStream_t s, void* comm = nullptr) {
   if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
   Residency where;
   TK_TRY(validate_leaves(leaves, n, kind, &where));
@@ -668,8 +710,8 @@ static int step_entry(const tk_leaf* leaves, size_t n, int kind, const tk_hparam
     if (!sync)
       return set_error(TK_ERR_INVALID, "the asynchronous step takes device buffers only");
     if (all_pinned(leaves, n, kind))
-      return step_host_pipelined(leaves, n, kind, *hp, step, max_norm, clip_scale_out, s);
-    return step_host(leaves, n, kind, *hp, step, max_norm, clip_scale_out, s);
+      return step_host_pipelined(leaves, n, kind, *hp, step, max_norm, clip_scale_out, s, comm);
+    return step_host(leaves, n, kind, *hp, step, max_norm, clip_scale_out, s, comm);
   }
   if (!sync) {
     bool written = false;
@@ -687,7 +729,7 @@ static int step_entry(const tk_leaf* leaves, size_t n, int kind, const tk_hparam
     dscale = static_cast<float*>(sc.get());
   }
   bool written = false;
-  TK_TRY(step_device(leaves, n, kind, *hp, step, max_norm, dscale, &written, s));
+  TK_TRY(step_device(leaves, n, kind, *hp, step, max_norm, dscale, &written, s, comm));
   float scale = 1.0f;
   if (written) TK_CUDA_TRY(cudaMemcpyAsync(&scale, dscale, 4, cudaMemcpyDeviceToHost, s));
   TK_CUDA_TRY(cudaStreamSynchronize(s));
@@ -748,6 +790,17 @@ int tk_step_buffers(const tk_leaf* leaves, size_t n_leaves, int32_t kind, const 
                     uint64_t step, float max_norm, float* clip_scale_out, void* stream) {
   const tk_pipeline pl = {kFastNodes, 3, max_norm > 0.0f ? max_norm : 0.0f};
   return tk_step_two_tier(&pl, leaves, n_leaves, kind, hp, step, clip_scale_out, stream);
+}
+
+int tk_step_buffers_sharded(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
+                            const tk_hparams* hp, uint64_t step, float max_norm,
+                            float* clip_scale_out, void* nccl_comm, void* stream) {
+  g_last_error.clear();
+  if (nccl_comm == nullptr) return set_error(TK_ERR_INVALID, "nccl_comm is NULL");
+  const tk_pipeline pl = {kFastNodes, 3, max_norm > 0.0f ? max_norm : 0.0f};
+  TK_TRY(verify_pipeline(&pl));
+  return step_entry(leaves, n_leaves, kind, hp, step, max_norm > 0.0f ? max_norm : 0.0f,
+                    clip_scale_out, nullptr, true, static_cast<cudaStream_t>(stream), nccl_comm);
 }
 
 int tk_step_buffers_async(const tk_leaf* leaves, size_t n_leaves, int32_t kind,

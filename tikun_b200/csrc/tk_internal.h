@@ -13,6 +13,7 @@ namespace tk {
 
 // ---------------------------------------------------------------- errors
 int set_error(int code, const char* fmt, ...);
+void clear_error();
 int cuda_error(cudaError_t e, const char* what);
 
 #define TK_CUDA_TRY(expr)                                     \
@@ -45,6 +46,14 @@ class Scratch {
 };
 
 int sm_count(int* out);
+
+// In-place ncclAllReduce(sum) of count doubles over an ncclComm_t (NCCL
+// resolved at run time; tk_shard.cpp).
+int nccl_allreduce_sum_f64(double* buf, size_t count, void* comm, cudaStream_t s);
+
+// Records the calling thread's update start/stop event (tk_set_update_events)
+// on s, if one is set.
+int record_update_event(bool start, cudaStream_t s);
 
 // SMs the pointwise kernels leave free (tk_set_reserved_sms); grids are sized
 // for the remaining ones.

@@ -205,3 +205,72 @@ class ZeroPointwise:
         for w in works:
             w.wait()
         self.launches_per_step = launches
+
+
+def nccl_comm_ptr(group=None, device=None) -> int:
+    """The ncclComm_t behind a PyTorch NCCL process group (created by a tiny
+    all-reduce if the group was initialised lazily)."""
+    group = group or dist.distributed_c10d._get_default_group()
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    backend = group._get_backend(device)
+    try:
+        ptr = backend._comm_ptr()
+    except RuntimeError:
+        ptr = 0
+    if not ptr:
+        dist.all_reduce(torch.zeros(1, device=device), group=group)
+        torch.cuda.synchronize(device)
+        ptr = backend._comm_ptr()
+    return int(ptr)
+
+
+class ShardedStep:
+    """ZeRO-1 clipped AdamW/Lion/SGD through the C ABI (tk_shard_*): the
+    native multi-GPU step over a flat f32 parameter/gradient arena laid out by
+    ``plan`` and replicated on every rank.  ``exchange`` is "peers" (the
+    update kernel stores into every rank's arena over NVLink) or "allgather"
+    (an in-place ncclAllGather after the update).  ``comm`` is an ncclComm_t
+    to use instead of the process group's (e.g. from tk_nccl_comm_init)."""
+
+    def __init__(self, plan: LayoutPlan, p_flat: torch.Tensor, g_flat: torch.Tensor,
+                 hp: ZeroHParams, group=None, exchange: str = "peers", comm: int | None = None):
+        for t in (p_flat, g_flat):
+            if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != plan.total:
+                raise ValueError("ShardedStep needs contiguous f32 arenas of plan.total elements")
+        self.plan, self.p, self.g, self.hp = plan, p_flat, g_flat, hp
+        self.step_count = 0
+        self.kind = _native.opt_kind(hp.kind)
+        mode = {"allgather": 0, "peers": 1}[exchange]
+        L = _native.lib()
+        offs = (ctypes.c_uint64 * len(plan))(*[o for o, _ in plan.slots])
+        lens = (ctypes.c_uint64 * len(plan))(*[n for _, n in plan.slots])
+        comm = comm or nccl_comm_ptr(group, p_flat.device)
+        handle = ctypes.c_void_p()
+        s = torch.cuda.current_stream(p_flat.device).cuda_stream
+        _native.check(L.tk_shard_init(comm, p_flat.data_ptr(), g_flat.data_ptr(), plan.total,
+                                      offs, lens, len(plan), self.kind, mode, s,
+                                      ctypes.byref(handle)))
+        self.handle = handle
+        lo, hi = ctypes.c_uint64(), ctypes.c_uint64()
+        _native.check(L.tk_shard_info(handle, ctypes.byref(lo), ctypes.byref(hi), None, None))
+        self.lo, self.hi = lo.value, hi.value
+        self.hparams = _native.TkHParams(hp.lr, hp.beta1, hp.beta2, hp.eps, hp.weight_decay)
+
+    def step(self, return_scale: bool = False) -> float | None:
+        """One step on the current stream; with ``return_scale`` waits for it
+        and returns the clip scale (step_fast_buffers' return value)."""
+        self.step_count += 1
+        L = _native.lib()
+        s = torch.cuda.current_stream(self.p.device).cuda_stream
+        out = ctypes.c_float(1.0)
+        _native.check(L.tk_shard_step(self.handle, ctypes.byref(self.hparams), self.step_count,
+                                      self.hp.max_norm, ctypes.byref(out) if return_scale else None,
+                                      s))
+        return out.value if return_scale else None
+
+    def close(self) -> None:
+        """Collective: every rank calls it before the process group goes."""
+        if self.handle:
+            s = torch.cuda.current_stream(self.p.device).cuda_stream
+            _native.check(_native.lib().tk_shard_destroy(self.handle, s))
+            self.handle = None
