@@ -278,7 +278,7 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
     L = _native.lib()
     stream = torch.cuda.current_stream()
     s_handle = stream.cuda_stream
-    fused = world > 1 and args.zero == "fused"
+    fused = world > 1 and args.zero != "allgather"
     plan = LayoutPlan(wl["sizes"], pad_to=16 * max(world, 1))
     hp_np, hg_np = make_host_state(wl)
     P, G = (Arena(plan, device=dev) for _ in range(2))
@@ -311,7 +311,7 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         zp = ShardedStep(plan, P.flat, G.flat,
                          ZeroHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"],
                                      wl["max_norm"]),
-                         exchange="peers" if fused else "allgather")
+                         exchange={"fused": "peers", "copy": "copy"}.get(args.zero, "allgather"))
         my_params = sum(n for _, _, n in pieces_to_segments(plan, zp.lo, zp.hi))
 
         def one_step():
@@ -422,9 +422,10 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
                    "leaves": len(wl["sizes"]),
                    "parallelism": "single GPU" if world == 1 else
-                   f"zero1-dp{world} via tk_shard_step (update kernel stores into peer arenas "
-                   "over NVLink)" if fused else
-                   f"zero1-dp{world} via tk_shard_step (ncclAllGather after the update)",
+                   f"zero1-dp{world} via tk_shard_step (" + {
+                       "fused": "update kernel stores into peer arenas over NVLink",
+                       "copy": "copy engines copy each updated chunk into peer arenas",
+                       "allgather": "ncclAllGather after the update"}[args.zero] + ")",
                    "l2": "inputs (p,g,m,v) larger than L2; no flush"},
         "roofline": {"bound": "hbm", "kernel": "pointwise_kernel (AdamW update)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
@@ -451,7 +452,7 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
 def run_muon(args, wl, world, rank, dev, torch, dist):
     from tikun_b200 import _native
     from tikun_b200.arena import LayoutPlan, shard_bounds, shard_segments
-    from tikun_b200.sharding import lpt_assign, ns_dense_flops, ns_issued_flops, owner_major_layout
+    from tikun_b200.sharding import ns_dense_flops, ns_issued_flops, owner_major_layout
 
     L = _native.lib()
     stream = torch.cuda.current_stream()
@@ -460,17 +461,18 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     mats = wl["mats"]
     sizes = [r * c for r, c in mats]
     costs = [ns_dense_flops(r, c) for r, c in mats]
-    owner = lpt_assign(costs, world) if world > 1 else [0] * len(mats)
-    offs, extent = owner_major_layout(sizes, owner, world)
     bf = torch.bfloat16
-    # Muon parameters: owner-major arena (bf16), so one all-gather reassembles them
-    p_mu = torch.empty(extent * world, dtype=bf, device=dev)
-    p_mu.normal_(0, 0.02, generator=gen)
-    mine = [i for i in range(len(mats)) if owner[i] == rank]
     g_mu, mom = {}, {}
-    for i in mine:
-        g_mu[i] = torch.empty(sizes[i], dtype=bf, device=dev).normal_(0, 1e-3, generator=gen)
-        mom[i] = torch.zeros(sizes[i], dtype=torch.float32, device=dev)
+    if world == 1:
+        # Muon parameters: one arena (bf16)
+        owner = [0] * len(mats)
+        offs, extent = owner_major_layout(sizes, owner, 1)
+        p_mu = torch.empty(extent, dtype=bf, device=dev)
+        p_mu.normal_(0, 0.02, generator=gen)
+        mine = list(range(len(mats)))
+        for i in mine:
+            g_mu[i] = torch.empty(sizes[i], dtype=bf, device=dev).normal_(0, 1e-3, generator=gen)
+            mom[i] = torch.zeros(sizes[i], dtype=torch.float32, device=dev)
     # AdamW leaves: one arena, ZeRO-1 slice per rank
     plan = LayoutPlan(wl["adamw"], pad_to=64 * max(world, 1))
     p_aw = torch.empty(plan.total, dtype=bf, device=dev).normal_(0, 0.02, generator=gen)
@@ -503,7 +505,39 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
 
     state = {"step": 0, "ns_ms": []}
     ns_ev = []
-    if not wl["inbackward"] or world > 1:
+    exchange = "allgather" if args.zero == "allgather" else "peers"
+    if world > 1:
+        # Muon matrices LPT-assigned to ranks (MuonShard); AdamW leaves ZeRO-1;
+        # with "peers" both update kernels store into every rank's arena over
+        # NVLink, otherwise all-gathers follow them
+        from tikun_b200.distributed import MuonShard, PeerArena
+
+        ms = MuonShard(mats, bf, dev, MUON_HP["lr"], MUON_HP["momentum"], exchange=exchange)
+        ms.params.normal_(0, 0.02, generator=gen)
+        mine = ms.mine
+        g_mu = {i: torch.empty(sizes[i], dtype=bf, device=dev).normal_(0, 1e-3, generator=gen)
+                for i in mine}
+        aw_peer = PeerArena(p_aw) if exchange == "peers" else None
+        all_aw = aw_leaves(segs)
+        barrier = torch.zeros(1, dtype=torch.float64, device=dev)
+
+        def one_step():
+            state["step"] += 1
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ms.step(g_mu, events=(e0, e1))
+            ns_ev.append((e0, e1))
+            if aw_peer is not None:
+                _native.check(L.tk_apply_pointwise_peers(all_aw[0], all_aw[1], _native.TK_ADAMW,
+                                                         ctypes.byref(hp), state["step"], None,
+                                                         aw_peer.deltas, aw_peer.n, s_handle))
+                dist.all_reduce(barrier)
+            else:
+                _native.check(L.tk_apply_pointwise(all_aw[0], all_aw[1], _native.TK_ADAMW,
+                                                   ctypes.byref(hp), state["step"], None,
+                                                   s_handle))
+                dist.all_gather_into_tensor(p_aw, p_aw[lo:hi])
+            return -1  # counted below from the tile plan
+    elif not wl["inbackward"]:
         all_mu = mu_leaves(mine)
         all_aw = aw_leaves(segs)
 
@@ -516,9 +550,6 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
             ns_ev.append((e0, e1))
             _native.check(L.tk_apply_pointwise(all_aw[0], all_aw[1], _native.TK_ADAMW,
                                                ctypes.byref(hp), state["step"], None, s_handle))
-            if world > 1:
-                dist.all_gather_into_tensor(p_mu, p_mu[rank * extent:(rank + 1) * extent])
-                dist.all_gather_into_tensor(p_aw, p_aw[lo:hi])
             return -1  # counted below from the tile plan
     else:
         # in-backward (one GPU): layer l's grads are produced on the main stream
@@ -560,6 +591,10 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     ms_total, _, clocks = timed_loop(one_step, args.steps, args.warmup, stream, world, dist, dev,
                                      torch, uuid)
     assert _native.device_status() == 0, "a Newton-Schulz kernel reported a bounded-wait timeout"
+    if world > 1:
+        ms.close()
+        if aw_peer is not None:
+            aw_peer.close()
     ms_step = ms_total / args.steps
     n_params = sum(sizes) + sum(wl["adamw"])
     value = n_params / (ms_step / 1e3)
@@ -592,7 +627,9 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
                    "muon_matrices": len(mats), "adamw_leaves": len(wl["adamw"]),
                    "parallelism": "single GPU" if world == 1 else
-                   f"muon-lpt{world}+zero1-dp{world}",
+                   f"muon-lpt{world}+zero1-dp{world}, " + (
+                       "update kernels store into peer arenas over NVLink" if exchange == "peers"
+                       else "all-gathers after the updates"),
                    "l2": "inputs larger than L2; no flush"},
         "roofline": {"bound": "tensor", "kernel": "gemm_tn_kernel (Newton-Schulz GEMMs)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
@@ -615,9 +652,10 @@ def main():
     ap.add_argument("--workload", default="gpt2-small-clip", choices=sorted(WORKLOADS) + sorted(MUON))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--zero", default="fused", choices=["fused", "allgather"],
-                    help="multi-GPU AdamW exchange: peer stores from the update kernel, or "
-                         "chunk-major all-gathers overlapped with the update")
+    ap.add_argument("--zero", default="fused", choices=["fused", "copy", "allgather"],
+                    help="multi-GPU AdamW exchange: peer stores from the update kernel, "
+                         "copy-engine peer copies of each updated chunk, or an all-gather "
+                         "after the update")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -231,6 +231,18 @@ TK_API int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves,
  * reported a problem). */
 TK_API int tk_device_status(int* status_out);
 
+/* tk_muon_step for a Muon group sharded by matrix across GPUs: the final
+ * Newton-Schulz GEMM's epilogue stores each updated parameter both locally
+ * and into n_peers (<= 7) other GPUs' copies at byte offset peer_deltas[i]
+ * from the local address (peer memory mapped with tk_ipc_import), so the
+ * parameter exchange overlaps the tensor-core work.  The stores are visible
+ * system-wide when the kernels end; order the peers' reads after them with a
+ * cross-GPU barrier (an all-reduce).  No reference counterpart: the
+ * reference's Muon (python/tikun/muon_nd.py:94-160) is single-process. */
+TK_API int tk_muon_step_peers(const tk_muon_leaf* leaves, size_t n_leaves,
+                              const tk_muon_hparams* hp, const int64_t* peer_deltas, int n_peers,
+                              void* stream);
+
 /* tk_apply_pointwise for ZeRO-1 without a separate all-gather: the updated
  * parameters of these leaves are also stored into n_peers (<= 7) other GPUs'
  * copies of the same layout, at byte offset peer_deltas[i] from each local
@@ -268,6 +280,10 @@ TK_API int tk_ipc_close(void* ptr);
  *                       rank's arena (CUDA IPC mappings; all ranks on one
  *                       node, W <= 8) and an 8-byte all-reduce closes the
  *                       step;
+ *   TK_SHARD_COPY       the update runs in chunks of ~4M elements and the copy
+ *                       engines copy each finished chunk into every other
+ *                       rank's arena (one stream per peer, CUDA IPC), then
+ *                       an 8-byte all-reduce closes the step;
  *   TK_SHARD_ALLGATHER  an in-place ncclAllGather follows the update.
  * All calls are collective over nccl_comm (an ncclComm_t; from PyTorch,
  * ProcessGroupNCCL._comm_ptr()), made on the communicator's device, in the
@@ -275,7 +291,7 @@ TK_API int tk_ipc_close(void* ptr);
  * step's clip scale (1 without clipping) and makes the call synchronous.
  * NCCL is resolved at run time from the libnccl.so.2 loaded in the process. */
 typedef struct tk_shard tk_shard;
-enum { TK_SHARD_ALLGATHER = 0, TK_SHARD_PEERS = 1 };
+enum { TK_SHARD_ALLGATHER = 0, TK_SHARD_PEERS = 1, TK_SHARD_COPY = 2 };
 
 /* tk_step_buffers for one rank's share of a PyTree split across the ranks of
  * nccl_comm (any split: whole leaves or pieces of leaves, each element on one

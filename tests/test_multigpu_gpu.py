@@ -6,7 +6,8 @@ leaf table through
   all-reduce, then either overlapped all-gathers or the fused update that
   stores into the peer's arena over NVLink), and
 * ShardedStep (the C ABI's tk_shard_*, on PyTorch's communicator or on one
-  made by tk_nccl_comm_init), with both exchanges, for AdamW, Lion and SGD,
+  made by tk_nccl_comm_init), with each exchange (peer stores, copy-engine
+  copies, all-gather), for AdamW, Lion and SGD,
 * tk_step_buffers_sharded with whole leaves dealt round-robin to the ranks,
   from pinned host buffers, and with every leaf on rank 0 (rank 1 only joins
   the norm all-reduce),
@@ -191,6 +192,8 @@ CASES = [
     dict(api="zero", exchange="peers", kind="adamw", max_norm=0.0),
     dict(api="shard", exchange="peers", kind="adamw", max_norm=1.0),
     dict(api="shard", exchange="allgather", kind="adamw", max_norm=1.0),
+    dict(api="shard", exchange="copy", kind="adamw", max_norm=1.0),
+    dict(api="shard", exchange="copy", kind="sgd", max_norm=0.0),
     dict(api="shard", exchange="peers", kind="lion", max_norm=0.0),
     dict(api="shard", exchange="allgather", kind="sgd", max_norm=1.0),
     dict(api="shard-own-comm", exchange="peers", kind="adamw", max_norm=1.0),
@@ -224,3 +227,83 @@ def test_zero1_two_gpus_matches_single_gpu(cfg):
             assert abs(got - want) <= 1e-6 * abs(want), (got, want)
     if cfg["max_norm"] > 0:
         assert res[0]["ref_scales"][0] < 1.0  # the clip engaged
+
+
+MUON_SHAPES = [(256, 512), (512, 256), (384, 384), (128, 1024), (640, 320), (256, 512),
+               (96, 200), (1024, 256)]
+
+
+def _muon_rank(rank, world, port, q, exchange, dtype_name):
+    import sys
+    from datetime import timedelta
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, repo)
+    import torch.distributed as dist
+
+    from tikun_b200 import _native
+    from tikun_b200.distributed import MuonShard
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=60))
+    try:
+        dtype = getattr(torch, dtype_name)
+        gen = torch.Generator(device="cpu").manual_seed(11)
+        p0 = [torch.randn(r, c, generator=gen) * 0.02 for r, c in MUON_SHAPES]
+        grads = [[(torch.randn(r, c, generator=gen) * 1e-3) for r, c in MUON_SHAPES]
+                 for _ in range(3)]
+        ms = MuonShard(MUON_SHAPES, dtype, dev, lr=0.02, exchange=exchange)
+        for i in range(len(MUON_SHAPES)):
+            ms.param(i).copy_(p0[i])
+        for s in range(3):
+            ms.step({i: grads[s][i].to(dev, dtype).contiguous() for i in ms.mine})
+        torch.cuda.synchronize()
+        out = {"shard": [ms.param(i).float().cpu().numpy() for i in range(len(MUON_SHAPES))],
+               "mine": ms.mine}
+        ms.close()
+        if rank == 0:
+            # every matrix on this GPU through tk_muon_step
+            ps = [p0[i].to(dev, dtype).contiguous() for i in range(len(MUON_SHAPES))]
+            moms = [torch.zeros(r * c, device=dev) for r, c in MUON_SHAPES]
+            dt = _native.TK_F32 if dtype == torch.float32 else _native.TK_BF16
+            for s in range(3):
+                gs = [grads[s][i].to(dev, dtype).contiguous() for i in range(len(MUON_SHAPES))]
+                _native.muon_step([(ps[i].data_ptr(), gs[i].data_ptr(), moms[i].data_ptr(), 1,
+                                    r, c, dt, dt) for i, (r, c) in enumerate(MUON_SHAPES)],
+                                  lr=0.02, momentum=0.95)
+            torch.cuda.synchronize()
+            out["single"] = [p.float().cpu().numpy() for p in ps]
+        q.put((rank, out))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("exchange,dtype_name", [("peers", "bfloat16"), ("peers", "float32"),
+                                                 ("allgather", "bfloat16")])
+def test_muon_shard_two_gpus_matches_single_gpu(exchange, dtype_name):
+    """MuonShard (LPT-assigned matrices, peer stores from the final
+    Newton-Schulz epilogue or an all-gather) equals tk_muon_step of every
+    matrix on one GPU bit for bit, on both ranks: each matrix's arithmetic is
+    independent of which batch or GPU it runs in."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_muon_rank, args=(r, 2, port, q, exchange, dtype_name))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert res[0]["mine"] and res[1]["mine"]  # both ranks own matrices
+    for r in (0, 1):
+        for i, (a, b) in enumerate(zip(res[r]["shard"], res[0]["single"])):
+            np.testing.assert_array_equal(a, b, err_msg=f"rank {r} matrix {i}")

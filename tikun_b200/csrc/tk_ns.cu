@@ -79,6 +79,10 @@ struct GemmArgs {
   float fin_scale_wide, fin_scale_tall;
   uint64_t fin_tall[kMaxBatch / 64];
   void* fin_ptrs[kMaxBatch];
+  // the final parameters also go to these byte offsets from each local
+  // address: the same parameter in other GPUs' arenas (peer memory)
+  int fin_npeers;
+  int64_t fin_peer_delta[kMaxPeers];
 };
 
 __device__ __forceinline__ bool bit_of(const uint64_t* mask, int b) {
@@ -240,6 +244,51 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
       void* dst = a.fin_ptrs[b];
       const bool tall = bit_of(a.fin_tall, b);
       const float scale = tall ? a.fin_scale_tall : a.fin_scale_wide;
+      // A tall matrix's 32 outputs of this thread are contiguous in the
+      // parameter (row r, columns c0 .. c0+31): 16-byte vector accesses,
+      // locally and into the peers' copies.
+      if (tall && full && (a.N & 7) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        if (a.fin_dtype == TK_F32) {
+          float4* row = reinterpret_cast<float4*>(static_cast<float*>(dst) + (int64_t)r * a.N + c0);
+          float4 v4[8];
+          float* v = reinterpret_cast<float*>(v4);
+          if (a.fin_update) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) v4[q] = row[q];
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = a.fin_update ? __fadd_rn(v[j], __fmul_rn(scale, o[j])) : o[j];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) row[q] = v4[q];
+          for (int k = 0; k < a.fin_npeers; ++k) {
+            float4* pr = reinterpret_cast<float4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) pr[q] = v4[q];
+          }
+        } else {
+          uint4* row = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + (int64_t)r * a.N + c0);
+          uint4 in4[4], out4[4];
+          const uint16_t* h = reinterpret_cast<const uint16_t*>(in4);
+          uint16_t* w = reinterpret_cast<uint16_t*>(out4);
+          if (a.fin_update) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) in4[q] = row[q];
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            w[j] = f32_to_bf16_bits(
+                a.fin_update ? __fadd_rn(bf16_bits_to_f32(h[j]), __fmul_rn(scale, o[j])) : o[j]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) row[q] = out4[q];
+          for (int k = 0; k < a.fin_npeers; ++k) {
+            uint4* pr = reinterpret_cast<uint4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) pr[q] = out4[q];
+          }
+        }
+        return;
+      }
       // all 32 parameter loads are issued before any store, so their
       // latencies overlap instead of serialising behind possible aliasing
       int64_t idx[32];
@@ -255,7 +304,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (c0 + j < a.N) p[idx[j]] = a.fin_update ? __fadd_rn(cur[j], __fmul_rn(scale, o[j])) : o[j];
+          if (c0 + j < a.N) {
+            const float val = a.fin_update ? __fadd_rn(cur[j], __fmul_rn(scale, o[j])) : o[j];
+            p[idx[j]] = val;
+            for (int q = 0; q < a.fin_npeers; ++q)
+              *reinterpret_cast<float*>(reinterpret_cast<char*>(p + idx[j]) + a.fin_peer_delta[q]) = val;
+          }
       } else {
         uint16_t* p = static_cast<uint16_t*>(dst);
         uint32_t raw[32];
@@ -265,9 +319,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
         }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (c0 + j < a.N)
-            p[idx[j]] = f32_to_bf16_bits(
+          if (c0 + j < a.N) {
+            const uint16_t val = f32_to_bf16_bits(
                 a.fin_update ? __fadd_rn(bf16_bits_to_f32(raw[j]), __fmul_rn(scale, o[j])) : o[j]);
+            p[idx[j]] = val;
+            for (int q = 0; q < a.fin_npeers; ++q)
+              *reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(p + idx[j]) + a.fin_peer_delta[q]) = val;
+          }
       }
     }
   }
@@ -419,6 +477,9 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+  }
+  if constexpr (EPI == EPI_FINAL) {
+    if (args.fin_npeers) __threadfence_system();  // peer stores visible before the kernel ends
   }
   tc_fence_before();
   __syncthreads();
@@ -863,6 +924,10 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       for (int64_t i = 0; i < L.batch; ++i) {
         h.fin_ptrs[i] = io.dst[i];
         h.fin_tall[i >> 6] = pa.tall[i >> 6];
+      }
+      if (io.peers != nullptr) {
+        h.fin_npeers = io.peers->n;
+        for (int q = 0; q < io.peers->n; ++q) h.fin_peer_delta[q] = io.peers->delta[q];
       }
       TK_TRY(launch_gemm_epi(EPI_FINAL, fmt, mXT128[cur_xt], mB256, h, s));
     }

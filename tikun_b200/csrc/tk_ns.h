@@ -7,6 +7,8 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "tk_internal.h"
+
 namespace tk {
 namespace ns {
 
@@ -39,6 +41,7 @@ struct GroupIO {
   float upd_scale_wide, upd_scale_tall;
   float mu, om;            // momentum and (1 - momentum) in f32
   int nesterov;
+  const PeerSet* peers = nullptr;  // the final parameters also go to these peers
 };
 
 struct PrepArgs {

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <tuple>
 #include <vector>
@@ -51,7 +52,7 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
                        const std::vector<void*>& dst, const std::vector<float*>* mom,
                        const std::vector<uint8_t>& tall, int src_dtype, int dst_dtype, int update,
                        float scale_wide, float scale_tall, float mu, float om, int nesterov,
-                       int steps, int fmt, cudaStream_t s) {
+                       int steps, int fmt, cudaStream_t s, const PeerSet* peers = nullptr) {
   const int64_t count = (int64_t)src.size();
   const ns::GroupLayout one = ns::group_layout(m, n, 1);
   const int64_t per_wave = std::max<int64_t>(
@@ -77,6 +78,7 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
     io.mu = mu;
     io.om = om;
     io.nesterov = nesterov;
+    io.peers = peers;
     TK_TRY(ns::run_group(L, io, steps, fmt, scratch.get(), status, s));
   }
   return TK_OK;
@@ -141,8 +143,8 @@ int tk_newton_schulz_3d(void* tensor, int64_t num_heads, int64_t head_dim_out,
                   static_cast<cudaStream_t>(stream));
 }
 
-int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
-                 void* stream) {
+static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
+                     const PeerSet* peers, void* stream) {
   if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
   if (n_leaves > 0 && leaves == nullptr) return set_error(TK_ERR_INVALID, "leaves is NULL");
   const int fmt = fmt_of(hp->precision);
@@ -217,9 +219,26 @@ int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hpar
     const float upd_wide = (float)(-hp->lr * std::sqrt(std::max(1.0, (double)m / (double)n)));
     const float upd_tall = (float)(-hp->lr * std::sqrt(std::max(1.0, (double)n / (double)m)));
     TK_TRY(run_batches(m, n, kv.second.g, kv.second.p, &kv.second.mom, kv.second.tall, gdt, pdt,
-                       1, upd_wide, upd_tall, mu, om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s));
+                       1, upd_wide, upd_tall, mu, om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s,
+                       peers));
   }
   return TK_OK;
+}
+
+int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
+                 void* stream) {
+  return muon_step(leaves, n_leaves, hp, nullptr, stream);
+}
+
+int tk_muon_step_peers(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
+                       const int64_t* peer_deltas, int n_peers, void* stream) {
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
+    return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
+  PeerSet peers;
+  std::memset(&peers, 0, sizeof(peers));
+  peers.n = n_peers;
+  for (int i = 0; i < n_peers; ++i) peers.delta[i] = peer_deltas[i];
+  return muon_step(leaves, n_leaves, hp, &peers, stream);
 }
 
 int tk_device_status(int* status_out) {

@@ -120,6 +120,13 @@ struct tk_shard {
   std::vector<tk_leaf> leaves;  // owned segments of the leaves
   std::vector<void*> peer_ptrs;
   std::vector<int64_t> deltas;
+  // TK_SHARD_COPY: the owned range in chunks, each updated then copied to
+  // every peer by the copy engines (one stream per peer)
+  std::vector<std::vector<tk_leaf>> chunk_leaves;
+  std::vector<std::pair<uint64_t, uint64_t>> chunk_range;
+  std::vector<cudaEvent_t> chunk_done;
+  std::vector<cudaStream_t> peer_streams;
+  std::vector<cudaEvent_t> peer_done;
 };
 
 extern "C" {
@@ -161,6 +168,9 @@ int tk_nccl_comm_destroy(void* comm) {
 }
 
 static void shard_free(tk_shard* sh) {
+  for (cudaEvent_t e : sh->chunk_done) cudaEventDestroy(e);
+  for (cudaEvent_t e : sh->peer_done) cudaEventDestroy(e);
+  for (cudaStream_t q : sh->peer_streams) cudaStreamDestroy(q);
   for (void* p : sh->peer_ptrs) tk_ipc_close(p);
   if (sh->m) cudaFree(sh->m);
   if (sh->v) cudaFree(sh->v);
@@ -180,7 +190,7 @@ int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_
     return set_error(TK_ERR_INVALID, "null leaf offsets or sizes");
   if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD)
     return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
-  if (exchange != TK_SHARD_ALLGATHER && exchange != TK_SHARD_PEERS)
+  if (exchange != TK_SHARD_ALLGATHER && exchange != TK_SHARD_PEERS && exchange != TK_SHARD_COPY)
     return set_error(TK_ERR_INVALID, "unknown exchange mode %d", exchange);
   const Nccl* N = nullptr;
   TK_TRY(nccl(&N));
@@ -193,7 +203,7 @@ int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_
   if (cdev != dev)
     return set_error(TK_ERR_INVALID, "the communicator is on device %d, the current device is %d",
                      cdev, dev);
-  if (exchange == TK_SHARD_PEERS && world > 1 + kMaxPeers)
+  if (exchange != TK_SHARD_ALLGATHER && world > 1 + kMaxPeers)
     return set_error(TK_ERR_UNSUPPORTED, "peer stores reach at most %d peers", kMaxPeers);
   if (n_elems == 0 || n_elems % (16ull * (uint64_t)world) != 0)
     return set_error(TK_ERR_INVALID,
@@ -257,7 +267,7 @@ int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_
   std::memset(&mine, 0, sizeof(mine));
   mine.n_elems = n_elems;
   mine.exchange = exchange;
-  if (exchange == TK_SHARD_PEERS && world > 1) {
+  if (exchange != TK_SHARD_ALLGATHER && world > 1) {
     int st = tk_ipc_export(p_arena, mine.handle, &mine.offset);
     if (st != TK_OK) return fail(st);
   }
@@ -292,7 +302,7 @@ int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_
                             "%llu and %d", r, (unsigned long long)all[(size_t)r].n_elems,
                             (long long)all[(size_t)r].exchange, (unsigned long long)n_elems,
                             exchange));
-  if (exchange == TK_SHARD_PEERS)
+  if (exchange != TK_SHARD_ALLGATHER)
     for (int r = 0; r < world; ++r) {
       if (r == rank) continue;
       void* ptr = nullptr;
@@ -301,6 +311,44 @@ int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_
       sh->peer_ptrs.push_back(ptr);
       sh->deltas.push_back((int64_t)((char*)ptr - (char*)p_arena));
     }
+  if (exchange == TK_SHARD_COPY && world > 1) {
+    // chunks of about kChunkElems, on 16-element boundaries
+    constexpr uint64_t kChunkElems = 4ull << 20;
+    const uint64_t k = std::max<uint64_t>(1, (per + kChunkElems - 1) / kChunkElems);
+    const uint64_t len = ((per + k - 1) / k + 15) / 16 * 16;
+    for (uint64_t a = sh->lo; a < sh->hi; a += len) {
+      const uint64_t b = std::min(a + len, sh->hi);
+      std::vector<tk_leaf> cl;
+      for (const tk_leaf& L : sh->leaves) {
+        const uint64_t l0 = (uint64_t)(static_cast<float*>(L.p) - p_arena), l1 = l0 + L.n;
+        const uint64_t x = std::max(l0, a), y = std::min(l1, b);
+        if (x >= y) continue;
+        tk_leaf c = L;
+        c.p = static_cast<float*>(L.p) + (x - l0);
+        c.g = static_cast<const float*>(L.g) + (x - l0);
+        c.m = L.m + (x - l0);
+        c.v = L.v ? L.v + (x - l0) : nullptr;
+        c.n = y - x;
+        cl.push_back(c);
+      }
+      sh->chunk_leaves.push_back(cl);
+      sh->chunk_range.emplace_back(a, b);
+      cudaEvent_t e;
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+        return fail(set_error(TK_ERR_CUDA, "could not create the chunk events"));
+      sh->chunk_done.push_back(e);
+    }
+    for (size_t j = 0; j < sh->peer_ptrs.size(); ++j) {
+      cudaStream_t q;
+      cudaEvent_t e;
+      if (cudaStreamCreateWithFlags(&q, cudaStreamNonBlocking) != cudaSuccess)
+        return fail(set_error(TK_ERR_CUDA, "could not create the copy streams"));
+      sh->peer_streams.push_back(q);
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+        return fail(set_error(TK_ERR_CUDA, "could not create the copy events"));
+      sh->peer_done.push_back(e);
+    }
+  }
   *out = sh;
   return TK_OK;
 }
@@ -321,19 +369,40 @@ int tk_shard_step(tk_shard* sh, const tk_hparams* hp, uint64_t step, float max_n
   const size_t nl = sh->leaves.size();
   const bool clip = max_norm > 0.f;
   const bool peers = sh->exchange == TK_SHARD_PEERS && sh->world > 1;
+  const bool copy = sh->exchange == TK_SHARD_COPY && sh->world > 1;
   if (clip) {
     if (nl > 0) TK_TRY(tk_grad_sumsq(L, nl, sh->sumsq, s));
     else TK_CUDA_TRY(cudaMemsetAsync(sh->sumsq, 0, sizeof(double), s));
     TK_NCCL_TRY(N, N->AllReduce(sh->sumsq, sh->sumsq, 1, ncclFloat64, ncclSum, sh->comm, s));
     TK_TRY(tk_clip_scale(sh->sumsq, max_norm, sh->scale, s));
-  } else if (peers) {
+  } else if (peers || copy) {
     // orders this step's stores into the peers' arenas after their reads of
     // the previous parameters (the norm all-reduce does it when clipping)
     TK_NCCL_TRY(N, N->AllReduce(sh->sumsq + 1, sh->sumsq + 1, 1, ncclFloat64, ncclSum, sh->comm, s));
   }
   const float* scale = clip ? sh->scale : nullptr;
   TK_TRY(record_update_event(true, s));
-  if (peers) {
+  if (copy) {
+    for (size_t c = 0; c < sh->chunk_leaves.size(); ++c) {
+      const std::vector<tk_leaf>& cl = sh->chunk_leaves[c];
+      if (!cl.empty()) TK_TRY(tk_apply_pointwise(cl.data(), cl.size(), sh->kind, hp, step, scale, s));
+      TK_CUDA_TRY(cudaEventRecord(sh->chunk_done[c], s));
+      const uint64_t a = sh->chunk_range[c].first, b = sh->chunk_range[c].second;
+      for (size_t j = 0; j < sh->peer_streams.size(); ++j) {
+        TK_CUDA_TRY(cudaStreamWaitEvent(sh->peer_streams[j], sh->chunk_done[c], 0));
+        TK_CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<char*>(sh->p + a) + sh->deltas[j], sh->p + a,
+                                    (b - a) * sizeof(float), cudaMemcpyDeviceToDevice,
+                                    sh->peer_streams[j]));
+      }
+    }
+    TK_TRY(record_update_event(false, s));
+    for (size_t j = 0; j < sh->peer_streams.size(); ++j) {
+      TK_CUDA_TRY(cudaEventRecord(sh->peer_done[j], sh->peer_streams[j]));
+      TK_CUDA_TRY(cudaStreamWaitEvent(s, sh->peer_done[j], 0));
+    }
+    // every peer's copies into this arena have landed once this completes
+    TK_NCCL_TRY(N, N->AllReduce(sh->sumsq + 1, sh->sumsq + 1, 1, ncclFloat64, ncclSum, sh->comm, s));
+  } else if (peers) {
     if (nl > 0)
       TK_TRY(tk_apply_pointwise_peers(L, nl, sh->kind, hp, step, scale, sh->deltas.data(),
                                       (int)sh->deltas.size(), s));

@@ -228,8 +228,9 @@ class ShardedStep:
     """ZeRO-1 clipped AdamW/Lion/SGD through the C ABI (tk_shard_*): the
     native multi-GPU step over a flat f32 parameter/gradient arena laid out by
     ``plan`` and replicated on every rank.  ``exchange`` is "peers" (the
-    update kernel stores into every rank's arena over NVLink) or "allgather"
-    (an in-place ncclAllGather after the update).  ``comm`` is an ncclComm_t
+    update kernel stores into every rank's arena over NVLink), "copy" (the
+    copy engines copy each updated chunk into every rank's arena) or
+    "allgather" (an in-place ncclAllGather after the update).  ``comm`` is an ncclComm_t
     to use instead of the process group's (e.g. from tk_nccl_comm_init)."""
 
     def __init__(self, plan: LayoutPlan, p_flat: torch.Tensor, g_flat: torch.Tensor,
@@ -240,7 +241,7 @@ class ShardedStep:
         self.plan, self.p, self.g, self.hp = plan, p_flat, g_flat, hp
         self.step_count = 0
         self.kind = _native.opt_kind(hp.kind)
-        mode = {"allgather": 0, "peers": 1}[exchange]
+        mode = {"allgather": 0, "peers": 1, "copy": 2}[exchange]
         L = _native.lib()
         offs = (ctypes.c_uint64 * len(plan))(*[o for o, _ in plan.slots])
         lens = (ctypes.c_uint64 * len(plan))(*[n for _, n in plan.slots])
@@ -274,3 +275,135 @@ class ShardedStep:
             s = torch.cuda.current_stream(self.p.device).cuda_stream
             _native.check(_native.lib().tk_shard_destroy(self.handle, s))
             self.handle = None
+
+
+class PeerArena:
+    """Every rank's copy of one device tensor (same size and dtype on every
+    rank) mapped into this process with CUDA IPC.  ``deltas[i]`` is the byte
+    offset from an address in the local tensor to the same element in the
+    i-th other rank's copy (the form the peer-store kernels take)."""
+
+    def __init__(self, t: torch.Tensor, group=None):
+        self.group = group
+        self.ptrs: list[int] = []
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        L = _native.lib()
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _native.check(L.tk_ipc_export(t.data_ptr(), handle, ctypes.byref(off)))
+        mine = (bytes(handle.raw), int(off.value), t.numel() * t.element_size())
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+        deltas = []
+        for r, (h, o, nbytes) in enumerate(everyone):
+            if nbytes != mine[2]:
+                raise ValueError(f"rank {r} shares {nbytes} bytes, this rank {mine[2]}")
+            if r == rank:
+                continue
+            ptr = ctypes.c_void_p()
+            _native.check(L.tk_ipc_import(h, o, ctypes.byref(ptr)))
+            self.ptrs.append(ptr.value)
+            deltas.append(ptr.value - t.data_ptr())
+        self.n = len(deltas)
+        self.deltas = (ctypes.c_int64 * max(self.n, 1))(*deltas)
+
+    def close(self) -> None:
+        """Collective: waits for this device and every rank, then unmaps."""
+        if self.ptrs:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            L = _native.lib()
+            for p in self.ptrs:
+                _native.check(L.tk_ipc_close(ctypes.c_void_p(p)))
+            self.ptrs = []
+
+
+class MuonShard:
+    """Muon over matrices split across ranks (one process per GPU).
+
+    Whole matrices are owned by one rank each, assigned by LPT bin-packing on
+    their Newton-Schulz FLOPs (``sharding.lpt_assign``); the parameters live
+    in an owner-major arena replicated on every rank
+    (``sharding.owner_major_layout``); momentum exists on the owner only.
+    ``step(grads)`` runs momentum, Nesterov, Newton-Schulz and the update for
+    the rank's matrices (tk_muon_step, python/tikun/muon_nd.py:94-160 per
+    matrix) and exchanges them: with ``exchange="peers"`` the final GEMM's
+    epilogue stores each updated matrix into every rank's arena over NVLink
+    (tk_muon_step_peers) and one 8-byte all-reduce closes the step; with
+    ``"allgather"`` an all-gather of the owner-major arena follows."""
+
+    def __init__(self, shapes, dtype: torch.dtype, device, lr: float, momentum: float = 0.95,
+                 nesterov: bool = True, ns_steps: int = 5, precision: int | None = None,
+                 group=None, exchange: str = "peers"):
+        from .sharding import lpt_assign, ns_dense_flops, owner_major_layout
+
+        if dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("Muon parameters are f32 or bf16")
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.shapes = [tuple(s) for s in shapes]
+        sizes = [r * c for r, c in self.shapes]
+        self.owner = lpt_assign([ns_dense_flops(r, c) for r, c in self.shapes], self.world)
+        self.offs, self.extent = owner_major_layout(sizes, self.owner, self.world)
+        self.dtype, self.device = dtype, torch.device(device)
+        self.params = torch.zeros(self.extent * self.world, dtype=dtype, device=self.device)
+        self.mine = [i for i in range(len(sizes)) if self.owner[i] == self.rank]
+        self.momentum = {i: torch.zeros(sizes[i], dtype=torch.float32, device=self.device)
+                         for i in self.mine}
+        self.hp = _native.TkMuonHParams(lr, momentum, 1 if nesterov else 0, ns_steps,
+                                        _native.DEFAULT_NS_PRECISION if precision is None
+                                        else precision)
+        self.exchange = exchange if self.world > 1 else "none"
+        if self.exchange not in ("peers", "allgather", "none"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.peers = PeerArena(self.params, group) if self.exchange == "peers" else None
+        self.barrier_buf = torch.zeros(1, dtype=torch.float64, device=self.device)
+
+    def param(self, i: int) -> torch.Tensor:
+        r, c = self.shapes[i]
+        return self.params[self.offs[i]:self.offs[i] + r * c].view(r, c)
+
+    def step(self, grads, events=None) -> None:
+        """``grads[i]`` (device tensors, any of f32/bf16, contiguous) for the
+        rank's own matrices ``self.mine``; others are not read.  Enqueued on
+        the current stream.  ``events`` (two CUDA events) are recorded just
+        around the Newton-Schulz launches."""
+        L = _native.lib()
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        gdt = {torch.float32: _native.TK_F32, torch.bfloat16: _native.TK_BF16}
+        pdt = gdt[self.dtype]
+        arr = (_native.TkMuonLeaf * max(len(self.mine), 1))()
+        for k, i in enumerate(self.mine):
+            r, c = self.shapes[i]
+            g = grads[i]
+            if g.numel() != r * c or not g.is_contiguous():
+                raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
+            arr[k] = _native.TkMuonLeaf(self.param(i).data_ptr(), g.data_ptr(),
+                                        self.momentum[i].data_ptr(), 1, r, c, pdt, gdt[g.dtype])
+        if self.exchange == "peers":
+            # the peers are done reading this step's destination ranges
+            dist.all_reduce(self.barrier_buf, group=self.group)
+            if events:
+                events[0].record()
+            _native.check(L.tk_muon_step_peers(arr, len(self.mine), ctypes.byref(self.hp),
+                                               self.peers.deltas, self.peers.n, s))
+            if events:
+                events[1].record()
+            dist.all_reduce(self.barrier_buf, group=self.group)
+        else:
+            if events:
+                events[0].record()
+            _native.check(L.tk_muon_step(arr, len(self.mine), ctypes.byref(self.hp), s))
+            if events:
+                events[1].record()
+            if self.exchange == "allgather":
+                lo = self.rank * self.extent
+                dist.all_gather_into_tensor(self.params, self.params[lo:lo + self.extent],
+                                            group=self.group)
+
+    def close(self) -> None:
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
