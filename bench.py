@@ -278,6 +278,8 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
     L = _native.lib()
     stream = torch.cuda.current_stream()
     s_handle = stream.cuda_stream
+    if args.zero == "auto":
+        args.zero = "fused"
     fused = world > 1 and args.zero != "allgather"
     plan = LayoutPlan(wl["sizes"], pad_to=16 * max(world, 1))
     hp_np, hg_np = make_host_state(wl)
@@ -505,7 +507,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
 
     state = {"step": 0, "ns_ms": []}
     ns_ev = []
-    exchange = "allgather" if args.zero == "allgather" else "peers"
+    exchange = {"fused": "peers", "copy": "copy", "auto": "copy"}.get(args.zero, "allgather")
     if world > 1:
         # Muon matrices LPT-assigned to ranks (MuonShard); AdamW leaves ZeRO-1;
         # with "peers" both update kernels store into every rank's arena over
@@ -517,7 +519,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         mine = ms.mine
         g_mu = {i: torch.empty(sizes[i], dtype=bf, device=dev).normal_(0, 1e-3, generator=gen)
                 for i in mine}
-        aw_peer = PeerArena(p_aw) if exchange == "peers" else None
+        aw_peer = PeerArena(p_aw) if exchange != "allgather" else None
         all_aw = aw_leaves(segs)
         barrier = torch.zeros(1, dtype=torch.float64, device=dev)
 
@@ -628,8 +630,11 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
                    "muon_matrices": len(mats), "adamw_leaves": len(wl["adamw"]),
                    "parallelism": "single GPU" if world == 1 else
                    f"muon-lpt{world}+zero1-dp{world}, " + (
-                       "update kernels store into peer arenas over NVLink" if exchange == "peers"
-                       else "all-gathers after the updates"),
+                       {"peers": "update kernels store into peer arenas over NVLink",
+                        "copy": "a copy kernel on 16 reserved SMs stores each finished Muon "
+                                "batch into peer arenas during the next batch; the AdamW update "
+                                "kernel stores into them",
+                        "allgather": "all-gathers after the updates"}[exchange]),
                    "l2": "inputs larger than L2; no flush"},
         "roofline": {"bound": "tensor", "kernel": "gemm_tn_kernel (Newton-Schulz GEMMs)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
@@ -652,10 +657,11 @@ def main():
     ap.add_argument("--workload", default="gpt2-small-clip", choices=sorted(WORKLOADS) + sorted(MUON))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--zero", default="fused", choices=["fused", "copy", "allgather"],
-                    help="multi-GPU AdamW exchange: peer stores from the update kernel, "
-                         "copy-engine peer copies of each updated chunk, or an all-gather "
-                         "after the update")
+    ap.add_argument("--zero", default="auto", choices=["auto", "fused", "copy", "allgather"],
+                    help="multi-GPU exchange of updated parameters: peer stores from the update "
+                         "kernel (fused), copies beside the next batch's work (copy: the copy "
+                         "engines for AdamW chunks, a copy kernel on reserved SMs for Muon "
+                         "batches), or all-gathers; auto = fused for AdamW, copy for Muon")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -234,7 +234,8 @@ TK_API int tk_device_status(int* status_out);
 /* tk_muon_step for a Muon group sharded by matrix across GPUs: the final
  * Newton-Schulz GEMM's epilogue stores each updated parameter both locally
  * and into n_peers (<= 7) other GPUs' copies at byte offset peer_deltas[i]
- * from the local address (peer memory mapped with tk_ipc_import), so the
+ * (a multiple of 16) from the local address (peer memory mapped with
+ * tk_ipc_import), so the
  * parameter exchange overlaps the tensor-core work.  The stores are visible
  * system-wide when the kernels end; order the peers' reads after them with a
  * cross-GPU barrier (an all-reduce).  No reference counterpart: the
@@ -243,10 +244,23 @@ TK_API int tk_muon_step_peers(const tk_muon_leaf* leaves, size_t n_leaves,
                               const tk_muon_hparams* hp, const int64_t* peer_deltas, int n_peers,
                               void* stream);
 
+/* The same exchange overlapped with the next batch's tensor-core work: shape
+ * groups run largest first, and after each batch of matrices finishes, a copy
+ * kernel on a side stream -- on SMs the Newton-Schulz GEMMs leave free
+ * (TIKUN_MUON_COPY_SMS, default 16) -- loads each parameter once and stores
+ * it into every peer's copy over NVLink, while the next batch computes.  With
+ * TIKUN_MUON_COPY_ENGINE=1 the copy engines do it instead (one stream per
+ * peer).  The caller's stream waits for every copy before the call's work
+ * completes. */
+TK_API int tk_muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves,
+                             const tk_muon_hparams* hp, const int64_t* peer_deltas, int n_peers,
+                             void* stream);
+
 /* tk_apply_pointwise for ZeRO-1 without a separate all-gather: the updated
  * parameters of these leaves are also stored into n_peers (<= 7) other GPUs'
  * copies of the same layout, at byte offset peer_deltas[i] from each local
- * parameter address (peer memory mapped into this process, tk_ipc_import).
+ * parameter address (peer memory mapped into this process, tk_ipc_import);
+ * each delta must be a multiple of 16 bytes (TK_ERR_INVALID otherwise).
  * The stores are made visible system-wide before the kernel ends; a caller
  * orders the peers' later reads after it with any cross-GPU barrier (an
  * all-reduce).  Device leaves only. */

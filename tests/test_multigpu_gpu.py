@@ -247,6 +247,9 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    if exchange == "copy-engine":
+        os.environ["TIKUN_MUON_COPY_ENGINE"] = "1"
+        exchange = "copy"
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
@@ -286,10 +289,13 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("exchange,dtype_name", [("peers", "bfloat16"), ("peers", "float32"),
+                                                 ("copy", "bfloat16"), ("copy", "float32"),
+                                                 ("copy-engine", "bfloat16"),
                                                  ("allgather", "bfloat16")])
 def test_muon_shard_two_gpus_matches_single_gpu(exchange, dtype_name):
-    """MuonShard (LPT-assigned matrices, peer stores from the final
-    Newton-Schulz epilogue or an all-gather) equals tk_muon_step of every
+    """MuonShard (LPT-assigned matrices; peer stores from the final
+    Newton-Schulz epilogue, a copy kernel or the copy engines beside the next
+    batch, or an all-gather) equals tk_muon_step of every
     matrix on one GPU bit for bit, on both ranks: each matrix's arithmetic is
     independent of which batch or GPU it runs in."""
     ctx = mp.get_context("spawn")

@@ -836,6 +836,10 @@ int tk_apply_pointwise_peers(const tk_leaf* leaves, size_t n_leaves, int32_t kin
   if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
     return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
+  for (int i = 0; i < n_peers; ++i)  // the kernel's vector stores keep their alignment
+    if (peer_deltas[i] % 16 != 0)
+      return set_error(TK_ERR_INVALID, "peer delta %lld is not a multiple of 16 bytes",
+                       (long long)peer_deltas[i]);
   Residency where;
   TK_TRY(validate_leaves(leaves, n_leaves, kind, &where));
   if (where == Residency::kHost)

@@ -707,6 +707,10 @@ static int make_map(CUtensorMap* map, const void* base, int fmt, int64_t inner, 
   return TK_OK;
 }
 
+static thread_local int g_gemm_reserved_sms = 0;
+
+void set_gemm_reserved_sms(int n) { g_gemm_reserved_sms = n < 0 ? 0 : n; }
+
 template <int EPI, int FMT>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
                        cudaStream_t s) {
@@ -723,7 +727,7 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
   TK_TRY(sm_count(&sms));
   const int n_tiles = g.batch * g.tiles_per_mat;
   if (n_tiles == 0) return TK_OK;
-  const int grid = std::min(n_tiles, sms);
+  const int grid = std::min(n_tiles, std::max(1, sms - g_gemm_reserved_sms));
   gemm_tn_kernel<EPI, FMT><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, g);
   TK_CUDA_TRY(cudaGetLastError());
   return TK_OK;
@@ -932,6 +936,64 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       TK_TRY(launch_gemm_epi(EPI_FINAL, fmt, mXT128[cur_xt], mB256, h, s));
     }
   }
+  return TK_OK;
+}
+
+// ------------------------------------------------------------------ peer copies
+constexpr int kCopyThreads = 512;
+constexpr int kCopyUnroll = 4;
+
+__global__ void __launch_bounds__(kCopyThreads)
+peer_copy_kernel(const __grid_constant__ PeerCopyList list, const __grid_constant__ PeerSet peers) {
+  const uint64_t total = list.unit0[list.n];
+  const uint64_t per = (total + gridDim.x - 1) / gridDim.x;
+  const uint64_t u0 = (uint64_t)blockIdx.x * per;
+  const uint64_t u1 = u0 + per < total ? u0 + per : total;
+  int e = 0;
+  for (uint64_t base = u0; base < u1; base += (uint64_t)kCopyThreads * kCopyUnroll) {
+    uint4 v[kCopyUnroll];
+    const uint8_t* src[kCopyUnroll];
+    uint32_t len[kCopyUnroll];  // bytes of the unit (16 but at an entry's end)
+#pragma unroll
+    for (int k = 0; k < kCopyUnroll; ++k) {
+      const uint64_t u = base + (uint64_t)k * kCopyThreads + threadIdx.x;
+      len[k] = 0;
+      src[k] = nullptr;
+      if (u >= u1) continue;
+      while (e + 1 < list.n && list.unit0[e + 1] <= u) ++e;
+      const uint64_t off = (u - list.unit0[e]) * 16;
+      const uint64_t rem = list.bytes[e] - off;
+      src[k] = list.src[e] + off;
+      len[k] = rem >= 16 ? 16u : (uint32_t)rem;
+      if (len[k] == 16) v[k] = *reinterpret_cast<const uint4*>(src[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < kCopyUnroll; ++k) {
+      if (len[k] == 0) continue;
+      for (int q = 0; q < peers.n; ++q) {
+        uint8_t* dst = const_cast<uint8_t*>(src[k]) + peers.delta[q];
+        if (len[k] == 16) *reinterpret_cast<uint4*>(dst) = v[k];
+        else
+          for (uint32_t b = 0; b < len[k]; ++b) dst[b] = src[k][b];
+      }
+    }
+  }
+  __threadfence_system();  // peer stores visible before the kernel ends
+}
+
+int launch_peer_copy(const PeerCopyList& list, const PeerSet& peers, int blocks, cudaStream_t s) {
+  if (list.n <= 0 || peers.n <= 0 || list.unit0[list.n] == 0) return TK_OK;
+  if (list.n > kMaxBatch || peers.n > kMaxPeers)
+    return set_error(TK_ERR_INVALID, "peer copy list of %d entries to %d peers", list.n, peers.n);
+  for (int i = 0; i < list.n; ++i)
+    if ((reinterpret_cast<uintptr_t>(list.src[i]) & 15) != 0)
+      return set_error(TK_ERR_INVALID, "peer copy source %p is not 16-byte aligned", list.src[i]);
+  for (int q = 0; q < peers.n; ++q)
+    if (peers.delta[q] % 16 != 0)
+      return set_error(TK_ERR_INVALID, "peer delta %lld is not a multiple of 16",
+                       (long long)peers.delta[q]);
+  peer_copy_kernel<<<std::max(1, blocks), kCopyThreads, 0, s>>>(list, peers);
+  TK_CUDA_TRY(cudaGetLastError());
   return TK_OK;
 }
 

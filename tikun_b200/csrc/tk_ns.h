@@ -69,6 +69,22 @@ struct PrepArgs {
 int run_group(const GroupLayout& layout, const GroupIO& io, int steps, int fmt, void* scratch,
               int* err_dev, cudaStream_t s);
 
+// Newton-Schulz GEMM grids leave this many SMs free (per calling thread), for
+// a copy kernel running beside them.
+void set_gemm_reserved_sms(int n);
+
+// Copies of finished parameters into the peers' copies by an SM kernel (16-byte
+// loads once, a store per peer): the entries' 16-byte units are split evenly
+// over `blocks` CTAs.  src must be 16-byte aligned and every delta a multiple
+// of 16.
+struct PeerCopyList {
+  int n;
+  const uint8_t* src[kMaxBatch];
+  uint64_t bytes[kMaxBatch];
+  uint64_t unit0[kMaxBatch + 1];  // first 16-byte unit of each entry; unit0[n] = total
+};
+int launch_peer_copy(const PeerCopyList& list, const PeerSet& peers, int blocks, cudaStream_t s);
+
 // D = alpha * P Q^T (batched, half precision), for the GEMM kernel's tests.
 int plain_gemm(const uint16_t* P, const uint16_t* Q, uint16_t* D, int batch, int M, int N, int K,
                int64_t ldp, int64_t ldq, int64_t ldd, float alpha, int fmt, int* err_dev,

@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <tuple>
 #include <vector>
 
@@ -46,13 +47,65 @@ static int check_status(cudaStream_t s) {
   return TK_OK;
 }
 
+// Copy-engine exchange of finished parameters: one non-blocking stream per
+// peer (per device), fed after each wave of a Muon step.
+// By default the copies are made by an SM kernel on a side stream (stream[0])
+// that runs on SMs the Newton-Schulz GEMMs leave free; with
+// TIKUN_MUON_COPY_ENGINE=1, by the copy engines, one stream per peer.
+struct PeerCopy {
+  int n = 0;
+  const int64_t* delta = nullptr;
+  bool engines = false;
+  int sms = 0;  // SMs left to the copy kernel
+  cudaStream_t stream[kMaxPeers] = {};
+  cudaEvent_t wave_done = nullptr;
+  cudaEvent_t done[kMaxPeers] = {};
+};
+
+static int peer_copy_streams(PeerCopy* pc) {
+  struct PerDevice {
+    bool ready = false;
+    cudaStream_t stream[kMaxPeers];
+    cudaEvent_t wave_done;
+    cudaEvent_t done[kMaxPeers];
+  };
+  static PerDevice devs[64];
+  static std::mutex mu;
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  const char* e = std::getenv("TIKUN_MUON_COPY_ENGINE");
+  pc->engines = e != nullptr && e[0] == '1';
+  const char* k = std::getenv("TIKUN_MUON_COPY_SMS");
+  pc->sms = k ? std::max(1, std::atoi(k)) : 16;
+  std::lock_guard<std::mutex> lock(mu);
+  PerDevice& d = devs[dev];
+  if (!d.ready) {
+    for (int j = 0; j < kMaxPeers; ++j) {
+      TK_CUDA_TRY(cudaStreamCreateWithFlags(&d.stream[j], cudaStreamNonBlocking));
+      TK_CUDA_TRY(cudaEventCreateWithFlags(&d.done[j], cudaEventDisableTiming));
+    }
+    TK_CUDA_TRY(cudaEventCreateWithFlags(&d.wave_done, cudaEventDisableTiming));
+    d.ready = true;
+  }
+  for (int j = 0; j < kMaxPeers; ++j) {
+    pc->stream[j] = d.stream[j];
+    pc->done[j] = d.done[j];
+  }
+  pc->wave_done = d.wave_done;
+  return TK_OK;
+}
+
 // Runs NS over matrices that are all m x n or n x m, in waves that fit the
-// scratch budget and the per-launch pointer capacity.
+// scratch budget and the per-launch pointer capacity.  With `copy`, each
+// wave's finished parameters are copied into the peers' copies by the copy
+// engines while the next wave computes.
 static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src,
                        const std::vector<void*>& dst, const std::vector<float*>* mom,
                        const std::vector<uint8_t>& tall, int src_dtype, int dst_dtype, int update,
                        float scale_wide, float scale_tall, float mu, float om, int nesterov,
-                       int steps, int fmt, cudaStream_t s, const PeerSet* peers = nullptr) {
+                       int steps, int fmt, cudaStream_t s, const PeerSet* peers = nullptr,
+                       PeerCopy* copy = nullptr) {
   const int64_t count = (int64_t)src.size();
   const ns::GroupLayout one = ns::group_layout(m, n, 1);
   const int64_t per_wave = std::max<int64_t>(
@@ -80,6 +133,42 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
     io.nesterov = nesterov;
     io.peers = peers;
     TK_TRY(ns::run_group(L, io, steps, fmt, scratch.get(), status, s));
+    if (copy != nullptr && copy->n > 0) {
+      const size_t bytes = (size_t)m * (size_t)n * (dst_dtype == TK_F32 ? 4 : 2);
+      TK_CUDA_TRY(cudaEventRecord(copy->wave_done, s));
+      if (copy->engines) {
+        for (int j = 0; j < copy->n; ++j) {
+          TK_CUDA_TRY(cudaStreamWaitEvent(copy->stream[j], copy->wave_done, 0));
+          for (int64_t i = first; i < first + nb; ++i)
+            TK_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(dst[i]) + copy->delta[j], dst[i],
+                                        bytes, cudaMemcpyDeviceToDevice, copy->stream[j]));
+        }
+      } else {
+        cudaStream_t cs = copy->stream[0];
+        TK_CUDA_TRY(cudaStreamWaitEvent(cs, copy->wave_done, 0));
+        static thread_local ns::PeerCopyList list;
+        list.n = 0;
+        list.unit0[0] = 0;
+        PeerSet peers;
+        std::memset(&peers, 0, sizeof(peers));
+        peers.n = copy->n;
+        for (int j = 0; j < copy->n; ++j) peers.delta[j] = copy->delta[j];
+        for (int64_t i = first; i < first + nb; ++i) {
+          const uint8_t* src = static_cast<const uint8_t*>(dst[i]);
+          if ((reinterpret_cast<uintptr_t>(src) & 15) != 0) {  // rare: the engines copy it
+            for (int j = 0; j < copy->n; ++j)
+              TK_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(dst[i]) + copy->delta[j], dst[i],
+                                          bytes, cudaMemcpyDeviceToDevice, cs));
+            continue;
+          }
+          list.src[list.n] = src;
+          list.bytes[list.n] = bytes;
+          list.unit0[list.n + 1] = list.unit0[list.n] + (bytes + 15) / 16;
+          ++list.n;
+        }
+        TK_TRY(ns::launch_peer_copy(list, peers, 2 * copy->sms, cs));
+      }
+    }
   }
   return TK_OK;
 }
@@ -144,7 +233,7 @@ int tk_newton_schulz_3d(void* tensor, int64_t num_heads, int64_t head_dim_out,
 }
 
 static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
-                     const PeerSet* peers, void* stream) {
+                     const PeerSet* peers, PeerCopy* copy, void* stream) {
   if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
   if (n_leaves > 0 && leaves == nullptr) return set_error(TK_ERR_INVALID, "leaves is NULL");
   const int fmt = fmt_of(hp->precision);
@@ -212,7 +301,17 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
   // p += (-lr * scale) * U
   const float mu = (float)hp->momentum;
   const float om = (float)(1.0 - hp->momentum);
-  for (auto& kv : groups) {
+  // largest groups first, so that with a copy-engine exchange the bulk of
+  // the parameters crosses NVLink while the smaller groups compute
+  std::vector<std::pair<double, decltype(groups)::iterator>> order;
+  for (auto it = groups.begin(); it != groups.end(); ++it) {
+    const double m = (double)std::get<0>(it->first), n = (double)std::get<1>(it->first);
+    order.emplace_back(-(double)it->second.g.size() * (4.0 * m * m * n + 2.0 * m * m * m), it);
+  }
+  std::stable_sort(order.begin(), order.end(),
+                   [](const auto& a, const auto& b) { return a.first < b.first; });
+  for (auto& ord : order) {
+    auto& kv = *ord.second;
     const int64_t m = std::get<0>(kv.first), n = std::get<1>(kv.first);
     const int pdt = std::get<2>(kv.first), gdt = std::get<3>(kv.first);
     // rows/cols is m/n (<= 1) for a wide matrix and n/m for a tall one
@@ -220,25 +319,59 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
     const float upd_tall = (float)(-hp->lr * std::sqrt(std::max(1.0, (double)n / (double)m)));
     TK_TRY(run_batches(m, n, kv.second.g, kv.second.p, &kv.second.mom, kv.second.tall, gdt, pdt,
                        1, upd_wide, upd_tall, mu, om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s,
-                       peers));
+                       peers, copy));
+  }
+  if (copy != nullptr) {
+    const int streams = copy->engines ? copy->n : (copy->n > 0 ? 1 : 0);
+    for (int j = 0; j < streams; ++j) {  // the caller's stream waits for every copy
+      TK_CUDA_TRY(cudaEventRecord(copy->done[j], copy->stream[j]));
+      TK_CUDA_TRY(cudaStreamWaitEvent(s, copy->done[j], 0));
+    }
   }
   return TK_OK;
 }
 
 int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
                  void* stream) {
-  return muon_step(leaves, n_leaves, hp, nullptr, stream);
+  return muon_step(leaves, n_leaves, hp, nullptr, nullptr, stream);
 }
 
 int tk_muon_step_peers(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
                        const int64_t* peer_deltas, int n_peers, void* stream) {
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
     return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
+  for (int i = 0; i < n_peers; ++i)  // vector stores into the peers keep their alignment
+    if (peer_deltas[i] % 16 != 0)
+      return set_error(TK_ERR_INVALID, "peer delta %lld is not a multiple of 16 bytes",
+                       (long long)peer_deltas[i]);
   PeerSet peers;
   std::memset(&peers, 0, sizeof(peers));
   peers.n = n_peers;
   for (int i = 0; i < n_peers; ++i) peers.delta[i] = peer_deltas[i];
-  return muon_step(leaves, n_leaves, hp, &peers, stream);
+  return muon_step(leaves, n_leaves, hp, &peers, nullptr, stream);
+}
+
+int tk_muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
+                      const int64_t* peer_deltas, int n_peers, void* stream) {
+  if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
+    return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
+  for (int i = 0; i < n_peers; ++i)  // vector stores into the peers keep their alignment
+    if (peer_deltas[i] % 16 != 0)
+      return set_error(TK_ERR_INVALID, "peer delta %lld is not a multiple of 16 bytes",
+                       (long long)peer_deltas[i]);
+  PeerCopy copy;
+  TK_TRY(peer_copy_streams(&copy));
+  copy.n = n_peers;
+  copy.delta = peer_deltas;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the copy streams start after the caller's earlier work
+  TK_CUDA_TRY(cudaEventRecord(copy.wave_done, s));
+  for (int j = 0; j < n_peers; ++j) TK_CUDA_TRY(cudaStreamWaitEvent(copy.stream[j], copy.wave_done, 0));
+  // the GEMMs leave SMs free for the copy kernel
+  if (!copy.engines && n_peers > 0) ns::set_gemm_reserved_sms(copy.sms);
+  const int st = muon_step(leaves, n_leaves, hp, nullptr, &copy, stream);
+  ns::set_gemm_reserved_sms(0);
+  return st;
 }
 
 int tk_device_status(int* status_out) {

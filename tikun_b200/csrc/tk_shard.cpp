@@ -310,6 +310,10 @@ int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_
       if (ist != TK_OK) return fail(ist);
       sh->peer_ptrs.push_back(ptr);
       sh->deltas.push_back((int64_t)((char*)ptr - (char*)p_arena));
+      if (sh->deltas.back() % 16 != 0)
+        return fail(set_error(TK_ERR_UNSUPPORTED,
+                              "rank %d's arena is not at the same address modulo 16 bytes as "
+                              "this rank's; use TK_SHARD_ALLGATHER", r));
     }
   if (exchange == TK_SHARD_COPY && world > 1) {
     // chunks of about kChunkElems, on 16-element boundaries

@@ -331,6 +331,8 @@ class MuonShard:
     matrix) and exchanges them: with ``exchange="peers"`` the final GEMM's
     epilogue stores each updated matrix into every rank's arena over NVLink
     (tk_muon_step_peers) and one 8-byte all-reduce closes the step; with
+    ``"copy"`` the copy engines copy each finished batch of matrices into every
+    rank's arena while the next batch computes (tk_muon_step_copy); with
     ``"allgather"`` an all-gather of the owner-major arena follows."""
 
     def __init__(self, shapes, dtype: torch.dtype, device, lr: float, momentum: float = 0.95,
@@ -356,9 +358,10 @@ class MuonShard:
                                         _native.DEFAULT_NS_PRECISION if precision is None
                                         else precision)
         self.exchange = exchange if self.world > 1 else "none"
-        if self.exchange not in ("peers", "allgather", "none"):
+        if self.exchange not in ("peers", "copy", "allgather", "none"):
             raise ValueError(f"unknown exchange {exchange!r}")
-        self.peers = PeerArena(self.params, group) if self.exchange == "peers" else None
+        self.peers = (PeerArena(self.params, group) if self.exchange in ("peers", "copy")
+                      else None)
         self.barrier_buf = torch.zeros(1, dtype=torch.float64, device=self.device)
 
     def param(self, i: int) -> torch.Tensor:
@@ -382,13 +385,14 @@ class MuonShard:
                 raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
             arr[k] = _native.TkMuonLeaf(self.param(i).data_ptr(), g.data_ptr(),
                                         self.momentum[i].data_ptr(), 1, r, c, pdt, gdt[g.dtype])
-        if self.exchange == "peers":
+        if self.exchange in ("peers", "copy"):
             # the peers are done reading this step's destination ranges
             dist.all_reduce(self.barrier_buf, group=self.group)
             if events:
                 events[0].record()
-            _native.check(L.tk_muon_step_peers(arr, len(self.mine), ctypes.byref(self.hp),
-                                               self.peers.deltas, self.peers.n, s))
+            fn = L.tk_muon_step_peers if self.exchange == "peers" else L.tk_muon_step_copy
+            _native.check(fn(arr, len(self.mine), ctypes.byref(self.hp), self.peers.deltas,
+                             self.peers.n, s))
             if events:
                 events[1].record()
             dist.all_reduce(self.barrier_buf, group=self.group)
