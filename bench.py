@@ -617,7 +617,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     launches = 0
     for (r, c), cnt in groups.items():
         m, n = min(r, c), max(r, c)
-        per_mat = 2 * (3 * m * n + 2 * m * m) + 2048
+        per_mat = 2 * (3 * m * n + 3 * m * m) + 2048
         per_wave = max(1, min(cnt, (8 << 30) // per_mat))
         waves = -(-cnt // per_wave)
         launches += waves * (2 + 15)

@@ -50,25 +50,37 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_TILE_BYTES = BM * BK * 2;
 constexpr int B_TILE_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr int THREADS = 192;
+// per epilogue warp: a 32 x 33-word tile for transposing a 32 x 32 block
+constexpr int TRANS_WORDS = 32 * 33;
+constexpr int EPI_WARPS = 8;
+constexpr int TRANS_BYTES = EPI_WARPS * TRANS_WORDS * 4;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + TRANS_BYTES + 1024;
+constexpr int THREADS = 64 + 32 * 8;  // producer, MMA issuer, 8 epilogue warps
 constexpr uint32_t TMEM_COLS = 512;
 
 constexpr float NS_A = 3.4445f, NS_B = -4.7750f, NS_C = 2.0315f;
 
-enum Epi { EPI_PLAIN = 0, EPI_GRAM = 1, EPI_POLY = 2, EPI_XUPD = 3, EPI_FINAL = 4 };
+// Epilogues, each on v = alpha*acc (+ gamma*aux when aux is set: a second
+// matrix of the output's shape, read in the epilogue).  SYM: a symmetric
+// product (upper tiles only, mirrored), stored as v + beta*I and, when out2 is
+// set, also as alpha2*acc + beta2*I.  XUPD: v stored row-wise to out and
+// transposed to out2.  FINAL: v applied to the Newton-Schulz output or the
+// parameter.
+enum Epi { EPI_PLAIN = 0, EPI_SYM = 1, EPI_XUPD = 3, EPI_FINAL = 4 };
 
 struct GemmArgs {
   int M, N, K;
   int batch;
   int tiles_m, tiles_n, tiles_per_mat;
   int symmetric;
-  float alpha, beta;
-  const uint16_t* aux;  // GEMM2: A; GEMM3: X^T (current)
+  float alpha, beta;    // SYM: out = alpha*acc + beta*I; XUPD/FINAL: alpha*acc
+  float alpha2, beta2;  // SYM with out2: out2 = alpha2*acc + beta2*I
+  float gamma;          // weight of aux
+  const uint16_t* aux;  // optional; same layout as the output
   int64_t aux_ld, aux_bs;
-  uint16_t* out;  // GEMM1: A; GEMM2: B; GEMM3: X^T (next)
+  uint16_t* out;  // GEMM1: A; GEMM2: B'; GEMM3: X^T (next)
   int64_t out_ld, out_bs;
-  uint16_t* out2;  // GEMM3: X (transposed store)
+  uint16_t* out2;  // GEMM1: A' = c A + b I; GEMM3: X (transposed store)
   int64_t out2_ld, out2_bs;
   int* err;
   // final iteration: per-matrix destination (NS output or parameter).  A tall
@@ -151,95 +163,225 @@ __device__ __forceinline__ bool wait_no_abort(uint64_t* bar, uint32_t parity) {
 }
 
 // ------------------------------------------------------------------ epilogue
+// The epilogue runs on 8 warps, two per TMEM lane quadrant (32 accumulator
+// rows each), each converting half of the tile's 256 columns in chunks of 32.
+// Within a chunk lane l holds row r0 + l, columns c0 .. c0 + 31.
+
+// Two f32 values -> one word of two 16-bit values (lo in the low half).
+template <int FMT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (FMT == 0) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+__device__ __forceinline__ uint16_t half_at(const uint32_t (&w)[16], int j) {
+  return (uint16_t)(w[j >> 1] >> ((j & 1) * 16));
+}
+
+// 32 16-bit values (16 words) -> four 16-byte stores; dst 16-byte aligned.
+__device__ __forceinline__ void store_words16(uint16_t* dst, const uint32_t (&w)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
+// Transposes the warp's 32 x 32 block of 16-bit values held as pairs along
+// the row (lane l: row l, w[k] = columns 2k, 2k+1) into pairs along the column
+// (lane l: column l, w[k] = rows 2k, 2k+1) through shared memory.  Row stride
+// 17 words: the stores are free of bank conflicts, and each load touches 16
+// words with two lanes per word.
+__device__ __forceinline__ void warp_transpose16(uint32_t* sm, uint32_t (&w)[16]) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 16; ++k) sm[lane * 17 + k] = w[k];
+  __syncwarp();
+  const uint32_t sel = (lane & 1) ? 0x7632u : 0x5410u;  // high or low halves
+#pragma unroll
+  for (int k = 0; k < 16; ++k)
+    w[k] = __byte_perm(sm[(2 * k) * 17 + (lane >> 1)], sm[(2 * k + 1) * 17 + (lane >> 1)], sel);
+  __syncwarp();
+}
+
+// Stores the warp's 32 x 32 block of 16-bit values (lane l: row l, 16 words)
+// to dst + row*ld (rows r0 .. r0+31, columns c0 .. c0+31 of the output) with
+// each store instruction covering 8 rows x 64 contiguous bytes, instead of 32
+// rows x 16 bytes: the block passes through shared memory (64-byte rows, the
+// 16-byte granules of row i rotated by (i/2)%4, so both phases are free of
+// bank conflicts).  Rows from `rows` on are not written; the block must be 32
+// columns wide.  dst + row*ld + c0 must be 16-byte aligned.
+__device__ __forceinline__ void store_block16(uint16_t* dst, int64_t ld, int r0, int c0, int rows,
+                                              const uint32_t (&w)[16], uint32_t* sm) {
+  const int lane = threadIdx.x & 31;
+  uint4* buf = reinterpret_cast<uint4*>(sm);  // 32 rows x 4 granules
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    buf[lane * 4 + (q ^ ((lane >> 1) & 3))] =
+        make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  __syncwarp();
+  const int j = lane & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int i = 8 * q + (lane >> 2);
+    const uint4 val = buf[i * 4 + (j ^ ((i >> 1) & 3))];
+    if (i < rows) reinterpret_cast<uint4*>(dst + (int64_t)(r0 + i) * ld + c0)[j] = val;
+  }
+  __syncwarp();
+}
+
+// The same for 32-bit values (row stride 33 words).
+__device__ __forceinline__ void warp_transpose32(uint32_t* sm, uint32_t (&x)[32]) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) sm[lane * 33 + j] = x[j];
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) x[i] = sm[i * 33 + lane];
+  __syncwarp();
+}
+
+// acc[j] = alpha*acc[j] (+ gamma*aux[r][c0+j] when aux is set).
+template <int FMT>
+__device__ __forceinline__ void scale_add_aux(const GemmArgs& a, int b, int r, int c0, bool full,
+                                              float (&acc)[32]) {
+  if (a.aux == nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = a.alpha * acc[j];
+    return;
+  }
+  const uint16_t* src = a.aux + (int64_t)b * a.aux_bs + (int64_t)r * a.aux_ld + c0;
+  if (full) {
+    uint4 raw[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) raw[q] = reinterpret_cast<const uint4*>(src)[q];
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(raw);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc[j] = a.alpha * acc[j] + a.gamma * from_half_bits<FMT>(h[j]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      acc[j] = a.alpha * acc[j] + (c0 + j < a.N ? a.gamma * from_half_bits<FMT>(src[j]) : 0.f);
+  }
+}
+
+// A chunk of a symmetric product: the row part on or above the diagonal, and
+// its mirror (c, r) for c > r -- transposed through shared memory when the
+// whole 32 x 32 block lies above the diagonal.  w is consumed.
+__device__ __forceinline__ void sym_store(const GemmArgs& a, uint16_t* base, int64_t ld,
+                                          uint32_t (&w)[16], int r, int r0, int c0, bool full,
+                                          bool wfull, uint32_t* tsm) {
+  if (wfull && c0 >= r0 + 32) {  // the block lies above the diagonal
+    store_block16(base, ld, r0, c0, 32, w, tsm);
+    warp_transpose16(tsm, w);
+    store_block16(base, ld, c0, r0, 32, w, tsm);
+    return;
+  }
+  if (full && c0 >= r) {
+    store_words16(base + (int64_t)r * ld + c0, w);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (r < a.M && c0 + j < a.N && c0 + j >= r) base[(int64_t)r * ld + c0 + j] = half_at(w, j);
+  }
+  if (!(wfull && c0 + 32 <= r0)) {  // consecutive lanes write consecutive r
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (r < a.M && c0 + j < a.N && c0 + j > r) base[(int64_t)(c0 + j) * ld + r] = half_at(w, j);
+  }
+}
+
+// One 32-column chunk.  Stores that run along columns (the mirror of a
+// symmetric product, X = (X^T)^T, a wide matrix's parameter) go through a warp
+// transpose when the whole 32 x 32 block is in range, so that each lane writes
+// 64 contiguous bytes.
 template <int EPI, int FMT>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, int c0,
-                                               const uint32_t (&v)[32]) {
-  if (r >= a.M) return;
+                                               const uint32_t (&v)[32], uint32_t* tsm) {
+  const int lane = threadIdx.x & 31;
+  const int r0 = r - lane;
+  const bool full = c0 + 32 <= a.N;
+  const bool wfull = full && r0 + 32 <= a.M;  // warp-uniform
+  if (!wfull && r >= a.M) return;
   float acc[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
-  const bool full = c0 + 32 <= a.N;
 
   if constexpr (EPI == EPI_PLAIN) {
-    uint16_t* dst = a.out + (int64_t)b * a.out_bs + (int64_t)r * a.out_ld + c0;
+    uint16_t* base = a.out + (int64_t)b * a.out_bs;
+    if (wfull && (a.out_ld & 7) == 0 && (a.out_bs & 7) == 0 &&
+        (reinterpret_cast<uintptr_t>(a.out) & 15) == 0) {
+      uint32_t w[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(a.alpha * acc[2 * k], a.alpha * acc[2 * k + 1]);
+      store_block16(base, a.out_ld, r0, c0, 32, w, tsm);
+      return;
+    }
+    uint16_t* dst = base + (int64_t)r * a.out_ld + c0;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
       if (full || c0 + j < a.N) dst[j] = to_half_bits<FMT>(a.alpha * acc[j]);
     return;
   }
 
-  if constexpr (EPI == EPI_GRAM || EPI == EPI_POLY) {
-    float o[32];
-    if constexpr (EPI == EPI_POLY) {
-      const uint16_t* src = a.aux + (int64_t)b * a.aux_bs + (int64_t)r * a.aux_ld + c0;
-      if (full) {
-        uint4 raw[4];
+  if constexpr (EPI == EPI_SYM) {
+    {  // out = alpha*acc (+ gamma*aux) + beta*I
+      float o[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) raw[q] = reinterpret_cast<const uint4*>(src)[q];
-        const uint16_t* h = reinterpret_cast<const uint16_t*>(raw);
+      for (int j = 0; j < 32; ++j) o[j] = acc[j];
+      scale_add_aux<FMT>(a, b, r, c0, full, o);
+      uint32_t w[16];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] = a.beta * from_half_bits<FMT>(h[j]) + a.alpha * acc[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          o[j] = (c0 + j < a.N) ? a.beta * from_half_bits<FMT>(src[j]) + a.alpha * acc[j] : 0.f;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[j] = a.alpha * acc[j];
+      for (int k = 0; k < 16; ++k)
+        w[k] = pack2<FMT>(o[2 * k] + (c0 + 2 * k == r ? a.beta : 0.f),
+                          o[2 * k + 1] + (c0 + 2 * k + 1 == r ? a.beta : 0.f));
+      sym_store(a, a.out + (int64_t)b * a.out_bs, a.out_ld, w, r, r0, c0, full, wfull, tsm);
     }
-    uint16_t* base = a.out + (int64_t)b * a.out_bs;
-    uint16_t hb[32];
+    if (a.out2 != nullptr) {  // out2 = alpha2*acc + beta2*I
+      uint32_t w[16];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) hb[j] = to_half_bits<FMT>(o[j]);
-    if (full && c0 >= r) {
-      uint4* dst = reinterpret_cast<uint4*>(base + (int64_t)r * a.out_ld + c0);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<const uint4*>(hb)[q];
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < a.N && c0 + j >= r) base[(int64_t)r * a.out_ld + c0 + j] = hb[j];
+      for (int k = 0; k < 16; ++k)
+        w[k] = pack2<FMT>(a.alpha2 * acc[2 * k] + (c0 + 2 * k == r ? a.beta2 : 0.f),
+                          a.alpha2 * acc[2 * k + 1] + (c0 + 2 * k + 1 == r ? a.beta2 : 0.f));
+      sym_store(a, a.out2 + (int64_t)b * a.out2_bs, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
     }
-    // mirror: (c, r) for c > r; consecutive lanes write consecutive r
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (c0 + j < a.N && c0 + j > r) base[(int64_t)(c0 + j) * a.out_ld + r] = hb[j];
     return;
   }
 
   if constexpr (EPI == EPI_XUPD || EPI == EPI_FINAL) {
-    const uint16_t* src = a.aux + (int64_t)b * a.aux_bs + (int64_t)r * a.aux_ld + c0;
     float o[32];
-    if (full) {
-      uint4 raw[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) raw[q] = reinterpret_cast<const uint4*>(src)[q];
-      const uint16_t* h = reinterpret_cast<const uint16_t*>(raw);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) o[j] = a.alpha * acc[j] + a.beta * from_half_bits<FMT>(h[j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        o[j] = (c0 + j < a.N) ? a.alpha * acc[j] + a.beta * from_half_bits<FMT>(src[j]) : 0.f;
-    }
+    for (int j = 0; j < 32; ++j) o[j] = acc[j];
+    scale_add_aux<FMT>(a, b, r, c0, full, o);
     if constexpr (EPI == EPI_XUPD) {
-      uint16_t hb[32];
+      uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) hb[j] = to_half_bits<FMT>(o[j]);
+      for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
       uint16_t* d1 = a.out + (int64_t)b * a.out_bs + (int64_t)r * a.out_ld + c0;
-      if (full) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(d1)[q] = reinterpret_cast<const uint4*>(hb)[q];
+      if (wfull) {
+        store_block16(a.out + (int64_t)b * a.out_bs, a.out_ld, r0, c0, 32, w, tsm);
+      } else if (full) {
+        store_words16(d1, w);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (c0 + j < a.N) d1[j] = hb[j];
+          if (c0 + j < a.N) d1[j] = half_at(w, j);
       }
       uint16_t* d2 = a.out2 + (int64_t)b * a.out2_bs;
+      if (wfull) {
+        warp_transpose16(tsm, w);
+        store_block16(d2, a.out2_ld, c0, r0, 32, w, tsm);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (c0 + j < a.N) d2[(int64_t)(c0 + j) * a.out2_ld + r] = hb[j];
+        for (int j = 0; j < 32; ++j)
+          if (c0 + j < a.N) d2[(int64_t)(c0 + j) * a.out2_ld + r] = half_at(w, j);
+      }
     } else {
       void* dst = a.fin_ptrs[b];
       const bool tall = bit_of(a.fin_tall, b);
@@ -289,42 +431,85 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
         }
         return;
       }
-      // all 32 parameter loads are issued before any store, so their
-      // latencies overlap instead of serialising behind possible aliasing
-      int64_t idx[32];
+      // A wide matrix's parameter row c holds this warp's block column c:
+      // after a transpose, lane l owns 32 contiguous elements of row c0 + l.
+      const size_t esz = a.fin_dtype == TK_F32 ? 4 : 2;
+      if (!tall && wfull && ((size_t)a.M * esz) % 16 == 0 &&
+          (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        uint32_t t[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        idx[j] = tall ? (int64_t)r * a.N + c0 + j : (int64_t)(c0 + j) * a.M + r;
+        for (int j = 0; j < 32; ++j) t[j] = __float_as_uint(o[j]);
+        warp_transpose32(tsm, t);
+        const int64_t at = (int64_t)(c0 + lane) * a.M + r0;
+        if (a.fin_dtype == TK_F32) {
+          float4* row = reinterpret_cast<float4*>(static_cast<float*>(dst) + at);
+          float4 v4[8];
+          float* pv = reinterpret_cast<float*>(v4);
+          if (a.fin_update) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) v4[q] = row[q];
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float oj = __uint_as_float(t[j]);
+            pv[j] = a.fin_update ? __fadd_rn(pv[j], __fmul_rn(scale, oj)) : oj;
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) row[q] = v4[q];
+          for (int k = 0; k < a.fin_npeers; ++k) {
+            float4* pr = reinterpret_cast<float4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) pr[q] = v4[q];
+          }
+        } else {
+          uint4* row = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + at);
+          uint4 in4[4], out4[4];
+          const uint16_t* h = reinterpret_cast<const uint16_t*>(in4);
+          uint16_t* w = reinterpret_cast<uint16_t*>(out4);
+          if (a.fin_update) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) in4[q] = row[q];
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float oj = __uint_as_float(t[j]);
+            w[j] = f32_to_bf16_bits(
+                a.fin_update ? __fadd_rn(bf16_bits_to_f32(h[j]), __fmul_rn(scale, oj)) : oj);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) row[q] = out4[q];
+          for (int k = 0; k < a.fin_npeers; ++k) {
+            uint4* pr = reinterpret_cast<uint4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) pr[q] = out4[q];
+          }
+        }
+        return;
+      }
+      // edges and unaligned parameters: element by element; element j is at
+      // i0 + j * stride
+      const int64_t i0 = tall ? (int64_t)r * a.N + c0 : (int64_t)c0 * a.M + r;
+      const int64_t stride = tall ? 1 : a.M;
       if (a.fin_dtype == TK_F32) {
         float* p = static_cast<float*>(dst);
-        float cur[32];
-        if (a.fin_update) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) cur[j] = (c0 + j < a.N) ? p[idx[j]] : 0.f;
-        }
-#pragma unroll
         for (int j = 0; j < 32; ++j)
           if (c0 + j < a.N) {
-            const float val = a.fin_update ? __fadd_rn(cur[j], __fmul_rn(scale, o[j])) : o[j];
-            p[idx[j]] = val;
+            float* pj = p + i0 + j * stride;
+            const float val = a.fin_update ? __fadd_rn(*pj, __fmul_rn(scale, o[j])) : o[j];
+            *pj = val;
             for (int q = 0; q < a.fin_npeers; ++q)
-              *reinterpret_cast<float*>(reinterpret_cast<char*>(p + idx[j]) + a.fin_peer_delta[q]) = val;
+              *reinterpret_cast<float*>(reinterpret_cast<char*>(pj) + a.fin_peer_delta[q]) = val;
           }
       } else {
         uint16_t* p = static_cast<uint16_t*>(dst);
-        uint32_t raw[32];
-        if (a.fin_update) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) raw[j] = (c0 + j < a.N) ? p[idx[j]] : 0u;
-        }
-#pragma unroll
         for (int j = 0; j < 32; ++j)
           if (c0 + j < a.N) {
+            uint16_t* pj = p + i0 + j * stride;
             const uint16_t val = f32_to_bf16_bits(
-                a.fin_update ? __fadd_rn(bf16_bits_to_f32(raw[j]), __fmul_rn(scale, o[j])) : o[j]);
-            p[idx[j]] = val;
+                a.fin_update ? __fadd_rn(bf16_bits_to_f32(*pj), __fmul_rn(scale, o[j])) : o[j]);
+            *pj = val;
             for (int q = 0; q < a.fin_npeers; ++q)
-              *reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(p + idx[j]) + a.fin_peer_delta[q]) = val;
+              *reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(pj) + a.fin_peer_delta[q]) = val;
           }
       }
     }
@@ -355,7 +540,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&tfull[s], 1);
-      mbar_init(&tempty[s], 4);
+      mbar_init(&tempty[s], EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -452,9 +637,13 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       if (!wait_no_abort(drain, 0) && args.err) atomicCAS(args.err, 0, 4);
     }
   } else {
-    // ---------------- epilogue: warps 2..5, one accumulator row per thread
+    // ---------------- epilogue: warps 2..9, one accumulator row per thread;
+    // warp w reads TMEM lanes 32*(w%4) .. +31 and half of the columns
     const int q = warp & 3;
+    const int col0 = ((warp - 2) >> 2) * (BN / 2);
     const int row_in_tile = q * 32 + lane;
+    uint32_t* tsm = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES + 256) +
+                    (warp - 2) * TRANS_WORDS;
     int it = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
@@ -465,13 +654,13 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       decode_tile(args, t, b, tm, tn);
       const int r = tm * BM + row_in_tile;
       const int c_base = tn * BN;
-      for (int cc = 0; cc < BN; cc += 32) {
+      for (int cc = col0; cc < col0 + BN / 2; cc += 32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + cc) +
                                (static_cast<uint32_t>(q * 32) << 16),
                            v);
         tmem_ld_wait();
-        if (c_base + cc < args.N) epilogue_chunk<EPI, FMT>(args, b, r, c_base + cc, v);
+        if (c_base + cc < args.N) epilogue_chunk<EPI, FMT>(args, b, r, c_base + cc, v, tsm);
       }
       tc_fence_before();
       __syncwarp();
@@ -743,8 +932,7 @@ static int launch_gemm_epi(int epi, int fmt, const CUtensorMap& ma, const CUtens
                            const GemmArgs& g, cudaStream_t s) {
   switch (epi) {
     case EPI_PLAIN: return launch_gemm_fmt<EPI_PLAIN>(fmt, ma, mb, g, s);
-    case EPI_GRAM: return launch_gemm_fmt<EPI_GRAM>(fmt, ma, mb, g, s);
-    case EPI_POLY: return launch_gemm_fmt<EPI_POLY>(fmt, ma, mb, g, s);
+    case EPI_SYM: return launch_gemm_fmt<EPI_SYM>(fmt, ma, mb, g, s);
     case EPI_XUPD: return launch_gemm_fmt<EPI_XUPD>(fmt, ma, mb, g, s);
     case EPI_FINAL: return launch_gemm_fmt<EPI_FINAL>(fmt, ma, mb, g, s);
   }
@@ -766,7 +954,7 @@ GroupLayout group_layout(int64_t m, int64_t n, int64_t batch) {
   L.xt_bytes = align256((size_t)(batch * L.n * L.ldm * 2));
   L.a_bytes = align256((size_t)(batch * L.m * L.ldm * 2));
   L.nblk = (int)std::max<int64_t>(1, std::min<int64_t>(256, (m * n + 16383) / 16384));
-  L.scratch_bytes = L.x_bytes + 2 * L.xt_bytes + 2 * L.a_bytes +
+  L.scratch_bytes = L.x_bytes + 2 * L.xt_bytes + 3 * L.a_bytes +
                     align256(sizeof(double) * batch * L.nblk) + align256(sizeof(float) * batch) +
                     256;
   return L;
@@ -794,6 +982,8 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   uint16_t* Am = reinterpret_cast<uint16_t*>(cur);
   cur += L.a_bytes;
   uint16_t* Bm = reinterpret_cast<uint16_t*>(cur);
+  cur += L.a_bytes;
+  uint16_t* Ap = reinterpret_cast<uint16_t*>(cur);
   cur += L.a_bytes;
   double* partials = reinterpret_cast<double*>(cur);
   cur += align256(sizeof(double) * L.batch * L.nblk);
@@ -855,11 +1045,24 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   }
   if (steps == 0) return TK_OK;
 
-  CUtensorMap mX128, mX256, mA128, mA256, mB256, mXT128[2];
+  // One iteration with f16 operands, with A' = c A + b I and
+  // B' = a I + b A + c A^2 = A A' + a I:
+  //   GEMM1  A = X X^T, A' = c A + b I   (one product, two symmetric stores)
+  //   GEMM2  B' = A A' + a I             (A' is symmetric, so A A'^T = A A')
+  //   GEMM3  X_new^T = X^T B'            (B' is symmetric: X_new = B' X)
+  // No epilogue reads a second matrix, so none waits on memory.  Rounding
+  // a + B_ii and c A_ij + b to 16 bits costs accuracy: with bf16 operands
+  // about 0.5 % more Newton-Schulz error, and with f16 operands on matrices
+  // under 256 rows a parameter drift over 10 Muon steps close to 1e-3 (it is
+  // below 3e-4 from 256 rows up).  There the epilogues add b A and a X^T in
+  // f32 instead: GEMM2 B = c A A + b A, GEMM3 X_new^T = X^T B + a X^T.
+  const bool fold = fmt == 0 && L.m >= 256;
+  CUtensorMap mX128, mX256, mA128, mA256, mAp256, mB256, mXT128[2];
   TK_TRY(make_map(&mX128, X, fmt, L.n, L.m, L.ldx, L.batch, 128));
   TK_TRY(make_map(&mX256, X, fmt, L.n, L.m, L.ldx, L.batch, 256));
   TK_TRY(make_map(&mA128, Am, fmt, L.m, L.m, L.ldm, L.batch, 128));
   TK_TRY(make_map(&mA256, Am, fmt, L.m, L.m, L.ldm, L.batch, 256));
+  TK_TRY(make_map(&mAp256, Ap, fmt, L.m, L.m, L.ldm, L.batch, 256));
   TK_TRY(make_map(&mB256, Bm, fmt, L.m, L.m, L.ldm, L.batch, 256));
   TK_TRY(make_map(&mXT128[0], XT[0], fmt, L.m, L.n, L.ldm, L.batch, 128));
   TK_TRY(make_map(&mXT128[1], XT[1], fmt, L.m, L.n, L.ldm, L.batch, 128));
@@ -873,7 +1076,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     std::memset(&g, 0, sizeof(g));
     g.batch = (int)L.batch;
     g.err = err_dev;
-    // GEMM1: A = X X^T
+    // GEMM1: A = X X^T and A' = c A + b I
     g.M = g.N = (int)L.m;
     g.K = (int)L.n;
     g.tiles_m = tm_sq;
@@ -881,20 +1084,35 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     g.tiles_per_mat = sym_tiles(tm_sq, tn_sq);
     g.symmetric = 1;
     g.alpha = it == 0 ? inv_pre2 : 1.0f;
+    g.beta = 0.0f;
     g.out = Am;
     g.out_ld = L.ldm;
     g.out_bs = L.m * L.ldm;
-    TK_TRY(launch_gemm_epi(EPI_GRAM, fmt, mX128, mX256, g, s));
-    // GEMM2: B = b A + c A A
+    if (fold) {
+      g.alpha2 = NS_C * g.alpha;
+      g.beta2 = NS_B;
+      g.out2 = Ap;
+      g.out2_ld = L.ldm;
+      g.out2_bs = L.m * L.ldm;
+    }
+    TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mX128, mX256, g, s));
+    // GEMM2: B' = A A' + a I  (bf16: B = c A A + b A)
     g.K = (int)L.m;
-    g.alpha = NS_C;
-    g.beta = NS_B;
-    g.aux = Am;
-    g.aux_ld = L.ldm;
-    g.aux_bs = L.m * L.ldm;
     g.out = Bm;
-    TK_TRY(launch_gemm_epi(EPI_POLY, fmt, mA128, mA256, g, s));
-    // GEMM3: X_new^T = post (a X^T + X^T B)
+    g.out2 = nullptr;
+    if (fold) {
+      g.alpha = 1.0f;
+      g.beta = NS_A;
+      TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mA128, mAp256, g, s));
+    } else {
+      g.alpha = NS_C;
+      g.gamma = NS_B;
+      g.aux = Am;
+      g.aux_ld = L.ldm;
+      g.aux_bs = L.m * L.ldm;
+      TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mA128, mA256, g, s));
+    }
+    // GEMM3: X_new^T = post * X^T B' (post undoes the first iterate's pre-scale)
     std::memset(&h, 0, sizeof(h));
     h.batch = (int)L.batch;
     h.err = err_dev;
@@ -905,12 +1123,13 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     h.tiles_n = tn_sq;
     h.tiles_per_mat = tm_x * tn_sq;
     h.symmetric = 0;
-    const float post = it == 0 ? inv_pre : 1.0f;
-    h.alpha = post;
-    h.beta = NS_A * post;
-    h.aux = XT[cur_xt];
-    h.aux_ld = L.ldm;
-    h.aux_bs = L.n * L.ldm;
+    h.alpha = it == 0 ? inv_pre : 1.0f;
+    if (!fold) {  // + a X^T
+      h.gamma = NS_A * h.alpha;
+      h.aux = XT[cur_xt];
+      h.aux_ld = L.ldm;
+      h.aux_bs = L.n * L.ldm;
+    }
     if (it + 1 < steps) {
       h.out = XT[cur_xt ^ 1];
       h.out_ld = L.ldm;
