@@ -297,6 +297,100 @@ __device__ __forceinline__ void sym_store(const GemmArgs& a, uint16_t* base, int
   }
 }
 
+// The final parameter update of a 32 x 32 block whose lane l holds the
+// Newton-Schulz output for parameter row row0 + l, columns col0 .. col0+31:
+// p = p + scale * o (or p = o), in the parameter's dtype, locally and into
+// the peers' copies.  The block passes through shared memory (128-byte rows,
+// 16-byte granules of row i rotated by i % 8) so that each access instruction
+// covers 4 rows x 128 bytes (f32) or 8 rows x 64 bytes (bf16).
+__device__ __forceinline__ void final_block(const GemmArgs& a, void* dst, int64_t ld, int row0,
+                                            int col0, const float (&o)[32], float scale,
+                                            uint32_t* sm) {
+  const int lane = threadIdx.x & 31;
+  float4* buf = reinterpret_cast<float4*>(sm);  // 32 rows x 8 granules
+  __syncwarp();
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    buf[lane * 8 + (g ^ (lane & 7))] = make_float4(o[4 * g], o[4 * g + 1], o[4 * g + 2], o[4 * g + 3]);
+  __syncwarp();
+  if (a.fin_dtype == TK_F32) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int i = 4 * q + (lane >> 3), g = lane & 7;
+      const float4 ov = buf[i * 8 + (g ^ (i & 7))];
+      float4* pp = reinterpret_cast<float4*>(static_cast<float*>(dst) + (int64_t)(row0 + i) * ld + col0) + g;
+      float4 pv = ov;
+      if (a.fin_update) {
+        pv = *pp;
+        pv.x = __fadd_rn(pv.x, __fmul_rn(scale, ov.x));
+        pv.y = __fadd_rn(pv.y, __fmul_rn(scale, ov.y));
+        pv.z = __fadd_rn(pv.z, __fmul_rn(scale, ov.z));
+        pv.w = __fadd_rn(pv.w, __fmul_rn(scale, ov.w));
+      }
+      *pp = pv;
+      for (int k = 0; k < a.fin_npeers; ++k)
+        *reinterpret_cast<float4*>(reinterpret_cast<char*>(pp) + a.fin_peer_delta[k]) = pv;
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = 8 * q + (lane >> 2), g = lane & 3;  // 8 bf16 = granules 2g, 2g+1 of o
+      const float4 o0 = buf[i * 8 + ((2 * g) ^ (i & 7))];
+      const float4 o1 = buf[i * 8 + ((2 * g + 1) ^ (i & 7))];
+      const float ov[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+      uint4* pp = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + (int64_t)(row0 + i) * ld + col0) + g;
+      uint4 in = make_uint4(0u, 0u, 0u, 0u);
+      if (a.fin_update) in = *pp;
+      const uint32_t iw[4] = {in.x, in.y, in.z, in.w};
+      uint32_t ow[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float lo = ov[2 * h], hi = ov[2 * h + 1];
+        if (a.fin_update) {
+          lo = __fadd_rn(bf16_bits_to_f32(iw[h] & 0xffffu), __fmul_rn(scale, lo));
+          hi = __fadd_rn(bf16_bits_to_f32(iw[h] >> 16), __fmul_rn(scale, hi));
+        }
+        ow[h] = (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+      }
+      const uint4 out = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+      *pp = out;
+      for (int k = 0; k < a.fin_npeers; ++k)
+        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(pp) + a.fin_peer_delta[k]) = out;
+    }
+  }
+  __syncwarp();
+}
+
+// Prefetches into L2 the parameter lines of the 32 x 128 region (accumulator
+// rows r0 .., columns c0 ..) that a final-epilogue warp will update, while
+// the tile's MMAs run.  In-range addresses only.
+__device__ __forceinline__ void prefetch_final(const GemmArgs& a, int b, int r0, int c0) {
+  if (!a.fin_update) return;
+  const int lane = threadIdx.x & 31;
+  const bool tall = bit_of(a.fin_tall, b);
+  const int esz = a.fin_dtype == TK_F32 ? 4 : 2;
+  const char* p = static_cast<const char*>(a.fin_ptrs[b]);
+  if (tall) {  // parameter row r, columns c0 .. c0+127: one lane per row
+    const int r = r0 + lane;
+    if (r >= a.M || c0 >= a.N) return;
+    const int c1 = min(c0 + 128, a.N);
+    const char* lo = p + ((int64_t)r * a.N + c0) * esz;
+    const char* hi = p + ((int64_t)r * a.N + c1) * esz;
+    for (const char* x = lo; x < hi; x += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(x));
+  } else {  // parameter rows c0 .. c0+127, columns r0 .. r0+31: four rows per lane
+    if (r0 >= a.M) return;
+    const int r1 = min(r0 + 32, a.M);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = c0 + lane + 32 * k;
+      if (c >= a.N) break;
+      const char* lo = p + ((int64_t)c * a.M + r0) * esz;
+      const char* hi = p + ((int64_t)c * a.M + r1) * esz;
+      for (const char* x = lo; x < hi; x += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(x));
+    }
+  }
+}
+
 // One 32-column chunk.  Stores that run along columns (the mirror of a
 // symmetric product, X = (X^T)^T, a wide matrix's parameter) go through a warp
 // transpose when the whole 32 x 32 block is in range, so that each lane writes
@@ -386,104 +480,22 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
       void* dst = a.fin_ptrs[b];
       const bool tall = bit_of(a.fin_tall, b);
       const float scale = tall ? a.fin_scale_tall : a.fin_scale_wide;
-      // A tall matrix's 32 outputs of this thread are contiguous in the
-      // parameter (row r, columns c0 .. c0+31): 16-byte vector accesses,
-      // locally and into the peers' copies.
-      if (tall && full && (a.N & 7) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-        if (a.fin_dtype == TK_F32) {
-          float4* row = reinterpret_cast<float4*>(static_cast<float*>(dst) + (int64_t)r * a.N + c0);
-          float4 v4[8];
-          float* v = reinterpret_cast<float*>(v4);
-          if (a.fin_update) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) v4[q] = row[q];
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            v[j] = a.fin_update ? __fadd_rn(v[j], __fmul_rn(scale, o[j])) : o[j];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) row[q] = v4[q];
-          for (int k = 0; k < a.fin_npeers; ++k) {
-            float4* pr = reinterpret_cast<float4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) pr[q] = v4[q];
-          }
-        } else {
-          uint4* row = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + (int64_t)r * a.N + c0);
-          uint4 in4[4], out4[4];
-          const uint16_t* h = reinterpret_cast<const uint16_t*>(in4);
-          uint16_t* w = reinterpret_cast<uint16_t*>(out4);
-          if (a.fin_update) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) in4[q] = row[q];
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            w[j] = f32_to_bf16_bits(
-                a.fin_update ? __fadd_rn(bf16_bits_to_f32(h[j]), __fmul_rn(scale, o[j])) : o[j]);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) row[q] = out4[q];
-          for (int k = 0; k < a.fin_npeers; ++k) {
-            uint4* pr = reinterpret_cast<uint4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) pr[q] = out4[q];
-          }
-        }
-        return;
-      }
-      // A wide matrix's parameter row c holds this warp's block column c:
-      // after a transpose, lane l owns 32 contiguous elements of row c0 + l.
+      // Blocks fully in range with 16-byte aligned parameter rows: the
+      // parameter's rows are the block's rows (tall) or, after a warp
+      // transpose, its columns (wide); final_block updates them with
+      // coalesced accesses.
       const size_t esz = a.fin_dtype == TK_F32 ? 4 : 2;
-      if (!tall && wfull && ((size_t)a.M * esz) % 16 == 0 &&
-          (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-        uint32_t t[32];
+      const int64_t prow = tall ? a.N : a.M;  // parameter row length
+      if (wfull && ((size_t)prow * esz) % 16 == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        if (!tall) {
+          uint32_t t[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) t[j] = __float_as_uint(o[j]);
-        warp_transpose32(tsm, t);
-        const int64_t at = (int64_t)(c0 + lane) * a.M + r0;
-        if (a.fin_dtype == TK_F32) {
-          float4* row = reinterpret_cast<float4*>(static_cast<float*>(dst) + at);
-          float4 v4[8];
-          float* pv = reinterpret_cast<float*>(v4);
-          if (a.fin_update) {
+          for (int k = 0; k < 32; ++k) t[k] = __float_as_uint(o[k]);
+          warp_transpose32(tsm, t);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) v4[q] = row[q];
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float oj = __uint_as_float(t[j]);
-            pv[j] = a.fin_update ? __fadd_rn(pv[j], __fmul_rn(scale, oj)) : oj;
-          }
-#pragma unroll
-          for (int q = 0; q < 8; ++q) row[q] = v4[q];
-          for (int k = 0; k < a.fin_npeers; ++k) {
-            float4* pr = reinterpret_cast<float4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) pr[q] = v4[q];
-          }
-        } else {
-          uint4* row = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + at);
-          uint4 in4[4], out4[4];
-          const uint16_t* h = reinterpret_cast<const uint16_t*>(in4);
-          uint16_t* w = reinterpret_cast<uint16_t*>(out4);
-          if (a.fin_update) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) in4[q] = row[q];
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float oj = __uint_as_float(t[j]);
-            w[j] = f32_to_bf16_bits(
-                a.fin_update ? __fadd_rn(bf16_bits_to_f32(h[j]), __fmul_rn(scale, oj)) : oj);
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) row[q] = out4[q];
-          for (int k = 0; k < a.fin_npeers; ++k) {
-            uint4* pr = reinterpret_cast<uint4*>(reinterpret_cast<char*>(row) + a.fin_peer_delta[k]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) pr[q] = out4[q];
-          }
+          for (int k = 0; k < 32; ++k) o[k] = __uint_as_float(t[k]);
         }
+        final_block(a, dst, prow, tall ? r0 : c0, tall ? c0 : r0, o, scale, tsm);
         return;
       }
       // edges and unaligned parameters: element by element; element j is at
@@ -648,10 +660,12 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++it) {
       const int acc = it & 1;
       const uint32_t use = static_cast<uint32_t>(it >> 1);
-      if (!mbar_wait(&tfull[acc], use & 1, abort_flag, args.err, 5)) break;
-      tc_fence_after();
       int b, tm, tn;
       decode_tile(args, t, b, tm, tn);
+      if constexpr (EPI == EPI_FINAL)  // the parameters this warp will update, into L2
+        prefetch_final(args, b, tm * BM + q * 32, tn * BN + col0);
+      if (!mbar_wait(&tfull[acc], use & 1, abort_flag, args.err, 5)) break;
+      tc_fence_after();
       const int r = tm * BM + row_in_tile;
       const int c_base = tn * BN;
       for (int cc = col0; cc < col0 + BN / 2; cc += 32) {
