@@ -78,6 +78,10 @@ def lib() -> ctypes.CDLL:
         L.tko_step_two_tier.argtypes = [
             ctypes.POINTER(_Leaf), ctypes.c_size_t, ctypes.c_int32, ctypes.POINTER(_HParams),
             ctypes.c_uint64, ctypes.c_float, ctypes.c_int]
+        L.tko_pointwise_leaf.restype = None
+        L.tko_pointwise_leaf.argtypes = [ctypes.POINTER(_Leaf), ctypes.c_int32,
+                                         ctypes.POINTER(_HParams), ctypes.c_uint64,
+                                         ctypes.c_float]
         L.tko_polar_step.restype = None
         L.tko_polar_step.argtypes = [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_uint64,
                                      ctypes.c_uint64, ctypes.c_int]
@@ -125,6 +129,19 @@ def step_two_tier(params: Sequence[np.ndarray], grads: Sequence[np.ndarray],
     hp = _HParams(lr, b1, b2, eps, decay)
     return float(lib().tko_step_two_tier(leaves, n, kind, ctypes.byref(hp), step,
                                          max_norm, nthreads))
+
+
+def pointwise_leaf(p: np.ndarray, g: np.ndarray, m: np.ndarray, v: np.ndarray | None,
+                   kind: int, lr: float, b1: float, b2: float, eps: float, decay: float,
+                   step: int, clip_scale: float) -> None:
+    """Tier 2 over one numpy leaf with a given clip scale, in place
+    (crates/tikun-cpu/src/lib.rs:143-428)."""
+    for a in (p, g, m) + ((v,) if v is not None else ()):
+        assert a.flags.c_contiguous
+    leaf = _Leaf(p.ctypes.data, g.ctypes.data, m.ctypes.data,
+                 v.ctypes.data if v is not None else 0, p.size, _dtype_code(p), _dtype_code(g))
+    hp = _HParams(lr, b1, b2, eps, decay)
+    lib().tko_pointwise_leaf(ctypes.byref(leaf), kind, ctypes.byref(hp), step, clip_scale)
 
 
 def step_fast_buffers(param_ptrs, grad_ptrs, m1_ptrs, m2_ptrs, lengths, max_norm,
