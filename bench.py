@@ -203,6 +203,57 @@ def run_reference(args, wl, rank):
     }), flush=True)
 
 
+def cpu_muon_run(wl, nthreads, budget_flops=1.5e11):
+    """The oracle on host cores for a Muon workload, as a bounded sample: per
+    shape group, the momentum/Nesterov update and the f32 Newton-Schulz of one
+    matrix (tensor_engine.rs:12-77, GEMM rows over `nthreads`) are timed and
+    multiplied by the group's count; a matrix whose Newton-Schulz exceeds
+    `budget_flops` is timed at a scaled-down size of the same aspect ratio and
+    extrapolated by FLOP ratio.  The AdamW leaves (bf16 parameters) run in
+    full through the oracle's two-tier step, threads over leaves.  Returns
+    (params/s, ms per step, sample description)."""
+    import oracle
+
+    from tikun_b200.sharding import ns_dense_flops
+
+    rng = np.random.default_rng(7)
+    groups = {}
+    for rc in wl["mats"]:
+        groups[rc] = groups.get(rc, 0) + 1
+    total_s, notes, extrapolated = 0.0, [], False
+    for (r, c), cnt in groups.items():
+        f = 1
+        while ns_dense_flops(r // f, c // f) > budget_flops and min(r, c) // f >= 64:
+            f *= 2
+        rr, cc = r // f, c // f
+        g = (rng.standard_normal((rr, cc)) * 1e-3).astype(np.float32)
+        buf = np.zeros_like(g)
+        t0 = time.perf_counter()
+        u = oracle.muon_momentum(buf, g, MUON_HP["momentum"], True)
+        x = np.ascontiguousarray(u, dtype=np.float32)
+        oracle.polar_step(x, 5, nthreads)
+        dt = time.perf_counter() - t0
+        scale = ns_dense_flops(r, c) / ns_dense_flops(rr, cc)
+        extrapolated |= f > 1
+        total_s += dt * scale * cnt
+        notes.append(f"{cnt}x{r}x{c}" + (f" (timed at {rr}x{cc})" if f > 1 else ""))
+    # AdamW leaves in full: bf16 p and g as uint16, f32 m and v
+    sizes = wl["adamw"]
+    p = [oracle.f32_to_bf16((rng.standard_normal(n) * 0.02).astype(np.float32)) for n in sizes]
+    gr = [oracle.f32_to_bf16((rng.standard_normal(n) * 1e-3).astype(np.float32)) for n in sizes]
+    m = [np.zeros(n, np.float32) for n in sizes]
+    v = [np.zeros(n, np.float32) for n in sizes]
+    t0 = time.perf_counter()
+    oracle.step_two_tier(p, gr, m, v, oracle.ADAMW, HP["lr"], HP["b1"], HP["b2"], HP["eps"],
+                         HP["decay"], 1, 0.0, nthreads)
+    total_s += time.perf_counter() - t0
+    n_params = sum(r * c for r, c in wl["mats"]) + sum(sizes)
+    sample = ("Newton-Schulz of one matrix per shape group, times the group's count: " +
+              ", ".join(notes) + f"; AdamW leaves ({sum(sizes):,} params) in full; "
+              f"{nthreads} threads" + ("; extrapolated by FLOP ratio" if extrapolated else ""))
+    return n_params / total_s, total_s * 1e3, sample
+
+
 def muon_workloads():
     """Muon configurations: (rows, cols) of the hidden matrices and AdamW leaf sizes."""
     def gpt2(d=768, layers=12, vocab=50257):
@@ -622,6 +673,12 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         waves = -(-cnt // per_wave)
         launches += waves * (2 + 15)
     launches = (launches + (wl["layers"] + 1 if wl["inbackward"] and world == 1 else 1)) * args.steps
+    cpu = None
+    if not args.no_cpu_baseline and world == 1 and rank == 0:
+        nthreads = os.cpu_count() or 1
+        cval, cms, csample = cpu_muon_run(wl, nthreads)
+        cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
+               "sample": f"{csample} ({cms:.0f} ms/step)"}
     return {
         "value": value, "ms_per_step": ms_step, "dtype": "bf16 params, f16 tensor-core operands",
         "scaling": "strong",
@@ -644,7 +701,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
                      "issued_tflops": my_issued / (ns_ms / 1e3) / 1e12,
                      "issued_frac": my_issued / (ns_ms / 1e3) / 1e12 / peak,
                      "ns_dense_tflop_per_step_this_rank": my_dense / 1e12},
-        "gpu_launches": launches, "clocks": clocks, "e2e": None, "cpu_baseline": None,
+        "gpu_launches": launches, "clocks": clocks, "e2e": None, "cpu_baseline": cpu,
     }
 
 
@@ -670,13 +727,21 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
-        if args.workload not in WORKLOADS:
-            if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable":
-                                  "the CPU reference arm covers the pointwise workloads; "
-                                  "Muon workloads are timed on the GPU only"}), flush=True)
-            return
-        run_reference(args, WORKLOADS[args.workload], rank)
+        if args.workload in WORKLOADS:
+            run_reference(args, WORKLOADS[args.workload], rank)
+        elif rank == 0:
+            nthreads = os.cpu_count() or 1
+            value, ms, sample = cpu_muon_run(MUON[args.workload], nthreads)
+            print(json.dumps({
+                "impl": "reference", "metric": METRIC, "value": value, "unit": "params/s",
+                "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32 Newton-Schulz, bf16 params", "data": "synthetic",
+                "config": {"workload": args.workload, "desc": MUON[args.workload]["desc"]},
+                "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads,
+                                 "kind": "port", "sample": sample},
+                "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}), flush=True)
         return
 
     import torch
