@@ -568,11 +568,52 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         ms = MuonShard(mats, bf, dev, MUON_HP["lr"], MUON_HP["momentum"], exchange=exchange)
         ms.params.normal_(0, 0.02, generator=gen)
         mine = ms.mine
-        g_mu = {i: torch.empty(sizes[i], dtype=bf, device=dev).normal_(0, 1e-3, generator=gen)
-                for i in mine}
+        if not wl["inbackward"]:
+            g_mu = {i: torch.empty(sizes[i], dtype=bf, device=dev).normal_(0, 1e-3,
+                                                                          generator=gen)
+                    for i in mine}
         aw_peer = PeerArena(p_aw) if exchange != "allgather" else None
         all_aw = aw_leaves(segs)
         barrier = torch.zeros(1, dtype=torch.float64, device=dev)
+
+        if wl["inbackward"]:
+            # layer l's grads come from a generator kernel on the main stream
+            # (standing in for backward), in reverse layer order; the side
+            # stream steps the rank's matrices of that layer as they appear
+            side = torch.cuda.Stream(device=dev)
+            per_layer = len(mats) // wl["layers"]
+            layer_ev = [torch.cuda.Event() for _ in range(wl["layers"])]
+            g_all = {i: torch.empty(sizes[i], dtype=bf, device=dev) for i in range(len(mats))}
+
+            def one_step():
+                state["step"] += 1
+                e0, e1 = (torch.cuda.Event(enable_timing=True),
+                          torch.cuda.Event(enable_timing=True))
+                ms.step_begin(side)
+                e0.record(side)
+                for l in reversed(range(wl["layers"])):
+                    for i in range(l * per_layer, (l + 1) * per_layer):
+                        g_all[i].normal_(0, 1e-3, generator=gen)
+                    layer_ev[l].record(stream)
+                    side.wait_event(layer_ev[l])
+                    ms.step_part(range(l * per_layer, (l + 1) * per_layer), g_all, side)
+                # the AdamW leaves (embedding last in backward, then norms)
+                if aw_peer is not None:
+                    _native.check(L.tk_apply_pointwise_peers(
+                        all_aw[0], all_aw[1], _native.TK_ADAMW, ctypes.byref(hp), state["step"],
+                        None, aw_peer.deltas, aw_peer.n, side.cuda_stream))
+                else:
+                    _native.check(L.tk_apply_pointwise(all_aw[0], all_aw[1], _native.TK_ADAMW,
+                                                       ctypes.byref(hp), state["step"], None,
+                                                       side.cuda_stream))
+                    with torch.cuda.stream(side):
+                        dist.all_gather_into_tensor(p_aw, p_aw[lo:hi])
+                ms.step_end(side)
+                e1.record(side)
+                ns_ev.append((e0, e1))
+                stream.wait_stream(side)
+                return -1
+    if world > 1 and not wl["inbackward"]:
 
         def one_step():
             state["step"] += 1
@@ -590,7 +631,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
                                                    s_handle))
                 dist.all_gather_into_tensor(p_aw, p_aw[lo:hi])
             return -1  # counted below from the tile plan
-    elif not wl["inbackward"]:
+    elif world == 1 and not wl["inbackward"]:
         all_mu = mu_leaves(mine)
         all_aw = aw_leaves(segs)
 
@@ -604,7 +645,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
             _native.check(L.tk_apply_pointwise(all_aw[0], all_aw[1], _native.TK_ADAMW,
                                                ctypes.byref(hp), state["step"], None, s_handle))
             return -1  # counted below from the tile plan
-    else:
+    elif world == 1:
         # in-backward (one GPU): layer l's grads are produced on the main stream
         # (a generator kernel standing in for backward), then its Muon and
         # AdamW steps run on a side stream, in reverse layer order
@@ -660,19 +701,30 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     peak = d.get("bf16_tflops_sustained" if long_step else "bf16_tflops", 1590.0)
     peak_kind = ("measured " + ("sustained" if long_step else "burst")) if d else "fallback"
     achieved = my_dense / (ns_ms / 1e3) / 1e12
-    # launches per step: per shape group and wave, 2 prologue + 3 GEMMs x 5
-    # iterations; plus the AdamW update launch(es)
-    groups = {}
-    for i in mine:
-        groups[mats[i]] = groups.get(mats[i], 0) + 1
-    launches = 0
-    for (r, c), cnt in groups.items():
-        m, n = min(r, c), max(r, c)
-        per_mat = 2 * (3 * m * n + 3 * m * m) + 2048
-        per_wave = max(1, min(cnt, (8 << 30) // per_mat))
-        waves = -(-cnt // per_wave)
-        launches += waves * (2 + 15)
-    launches = (launches + (wl["layers"] + 1 if wl["inbackward"] and world == 1 else 1)) * args.steps
+    # launches per step: per call, shape group (m x n and n x m together) and
+    # wave: 3 prologue kernels + 3 GEMMs x 5 iterations (+ the copy kernel when
+    # the exchange is the copy kernel); plus the AdamW update launch(es)
+    def ns_launches(idx):
+        groups = {}
+        for i in idx:
+            key = (min(mats[i]), max(mats[i]))
+            groups[key] = groups.get(key, 0) + 1
+        n = 0
+        for (m, nn), cnt in groups.items():
+            per_mat = 2 * (3 * m * nn + 3 * m * m) + 2048
+            per_wave = max(1, min(cnt, 256, (8 << 30) // per_mat))
+            waves = -(-cnt // per_wave)
+            n += waves * (3 + 15 + (1 if world > 1 and exchange == "copy" else 0))
+        return n
+
+    if wl["inbackward"]:
+        per_layer = len(mats) // wl["layers"]
+        calls = [[i for i in range(l * per_layer, (l + 1) * per_layer) if i in set(mine)]
+                 for l in range(wl["layers"])]
+        launches = sum(ns_launches(c) for c in calls) + (wl["layers"] + 1 if world == 1 else 1)
+    else:
+        launches = ns_launches(mine) + 1
+    launches *= args.steps
     cpu = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
         nthreads = os.cpu_count() or 1

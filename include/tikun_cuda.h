@@ -256,6 +256,15 @@ TK_API int tk_muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves,
                              const tk_muon_hparams* hp, const int64_t* peer_deltas, int n_peers,
                              void* stream);
 
+/* tk_muon_step_copy whose copies may still be running when the call's other
+ * work completes -- for a step issued in several calls (a layer at a time in
+ * backward order): the copies of every call run in order on the device's copy
+ * stream(s), and tk_muon_copy_join makes `stream` wait for all of them. */
+TK_API int tk_muon_step_copy_deferred(const tk_muon_leaf* leaves, size_t n_leaves,
+                                      const tk_muon_hparams* hp, const int64_t* peer_deltas,
+                                      int n_peers, void* stream);
+TK_API int tk_muon_copy_join(void* stream);
+
 /* tk_apply_pointwise for ZeRO-1 without a separate all-gather: the updated
  * parameters of these leaves are also stored into n_peers (<= 7) other GPUs'
  * copies of the same layout, at byte offset peer_deltas[i] from each local

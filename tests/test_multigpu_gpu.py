@@ -250,6 +250,8 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
     if exchange == "copy-engine":
         os.environ["TIKUN_MUON_COPY_ENGINE"] = "1"
         exchange = "copy"
+    parts = exchange.endswith("-parts")
+    exchange = exchange.replace("-parts", "")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
@@ -264,7 +266,15 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
         for i in range(len(MUON_SHAPES)):
             ms.param(i).copy_(p0[i])
         for s in range(3):
-            ms.step({i: grads[s][i].to(dev, dtype).contiguous() for i in ms.mine})
+            gs = {i: grads[s][i].to(dev, dtype).contiguous() for i in ms.mine}
+            if parts:  # in two calls, second half first (as backward would)
+                half = len(MUON_SHAPES) // 2
+                ms.step_begin()
+                ms.step_part(range(half, len(MUON_SHAPES)), gs)
+                ms.step_part(range(half), gs)
+                ms.step_end()
+            else:
+                ms.step(gs)
         torch.cuda.synchronize()
         out = {"shard": [ms.param(i).float().cpu().numpy() for i in range(len(MUON_SHAPES))],
                "mine": ms.mine}
@@ -291,11 +301,14 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
 @pytest.mark.parametrize("exchange,dtype_name", [("peers", "bfloat16"), ("peers", "float32"),
                                                  ("copy", "bfloat16"), ("copy", "float32"),
                                                  ("copy-engine", "bfloat16"),
-                                                 ("allgather", "bfloat16")])
+                                                 ("allgather", "bfloat16"),
+                                                 ("copy-parts", "bfloat16"),
+                                                 ("peers-parts", "float32"),
+                                                 ("allgather-parts", "bfloat16")])
 def test_muon_shard_two_gpus_matches_single_gpu(exchange, dtype_name):
     """MuonShard (LPT-assigned matrices; peer stores from the final
     Newton-Schulz epilogue, a copy kernel or the copy engines beside the next
-    batch, or an all-gather) equals tk_muon_step of every
+    batch, or an all-gather; in one call or in parts as in backward) equals tk_muon_step of every
     matrix on one GPU bit for bit, on both ranks: each matrix's arithmetic is
     independent of which batch or GPU it runs in."""
     ctx = mp.get_context("spawn")

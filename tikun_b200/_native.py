@@ -135,6 +135,10 @@ _SIGNATURES = {
                            ctypes.POINTER(_I64), ctypes.c_int, _P],
     "tk_muon_step_copy": [ctypes.POINTER(TkMuonLeaf), _SZ, ctypes.POINTER(TkMuonHParams),
                           ctypes.POINTER(_I64), ctypes.c_int, _P],
+    "tk_muon_step_copy_deferred": [ctypes.POINTER(TkMuonLeaf), _SZ,
+                                   ctypes.POINTER(TkMuonHParams), ctypes.POINTER(_I64),
+                                   ctypes.c_int, _P],
+    "tk_muon_copy_join": [_P],
     "tk_step_buffers_sharded": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,
                                 ctypes.c_float, ctypes.POINTER(ctypes.c_float), _P, _P],
     "tk_shard_init": [_P, _P, _P, _U64, ctypes.POINTER(_U64), ctypes.POINTER(_U64), _SZ, _I32,

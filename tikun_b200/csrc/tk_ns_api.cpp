@@ -56,7 +56,8 @@ struct PeerCopy {
   int n = 0;
   const int64_t* delta = nullptr;
   bool engines = false;
-  int sms = 0;  // SMs left to the copy kernel
+  bool join = true;  // the caller's stream waits for the copies at the end of the call
+  int sms = 0;       // SMs left to the copy kernel
   cudaStream_t stream[kMaxPeers] = {};
   cudaEvent_t wave_done = nullptr;
   cudaEvent_t done[kMaxPeers] = {};
@@ -321,7 +322,7 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
                        1, upd_wide, upd_tall, mu, om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s,
                        peers, copy));
   }
-  if (copy != nullptr) {
+  if (copy != nullptr && copy->join) {
     const int streams = copy->engines ? copy->n : (copy->n > 0 ? 1 : 0);
     for (int j = 0; j < streams; ++j) {  // the caller's stream waits for every copy
       TK_CUDA_TRY(cudaEventRecord(copy->done[j], copy->stream[j]));
@@ -351,8 +352,8 @@ int tk_muon_step_peers(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muo
   return muon_step(leaves, n_leaves, hp, &peers, nullptr, stream);
 }
 
-int tk_muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
-                      const int64_t* peer_deltas, int n_peers, void* stream) {
+static int muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
+                          const int64_t* peer_deltas, int n_peers, bool join, void* stream) {
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
     return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
   for (int i = 0; i < n_peers; ++i)  // vector stores into the peers keep their alignment
@@ -363,6 +364,7 @@ int tk_muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon
   TK_TRY(peer_copy_streams(&copy));
   copy.n = n_peers;
   copy.delta = peer_deltas;
+  copy.join = join;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the copy streams start after the caller's earlier work
   TK_CUDA_TRY(cudaEventRecord(copy.wave_done, s));
@@ -372,6 +374,28 @@ int tk_muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon
   const int st = muon_step(leaves, n_leaves, hp, nullptr, &copy, stream);
   ns::set_gemm_reserved_sms(0);
   return st;
+}
+
+int tk_muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
+                      const int64_t* peer_deltas, int n_peers, void* stream) {
+  return muon_step_copy(leaves, n_leaves, hp, peer_deltas, n_peers, true, stream);
+}
+
+int tk_muon_step_copy_deferred(const tk_muon_leaf* leaves, size_t n_leaves,
+                               const tk_muon_hparams* hp, const int64_t* peer_deltas, int n_peers,
+                               void* stream) {
+  return muon_step_copy(leaves, n_leaves, hp, peer_deltas, n_peers, false, stream);
+}
+
+int tk_muon_copy_join(void* stream) {
+  PeerCopy copy;
+  TK_TRY(peer_copy_streams(&copy));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int j = 0; j < kMaxPeers; ++j) {
+    TK_CUDA_TRY(cudaEventRecord(copy.done[j], copy.stream[j]));
+    TK_CUDA_TRY(cudaStreamWaitEvent(s, copy.done[j], 0));
+  }
+  return TK_OK;
 }
 
 int tk_device_status(int* status_out) {

@@ -407,6 +407,57 @@ class MuonShard:
                 dist.all_gather_into_tensor(self.params, self.params[lo:lo + self.extent],
                                             group=self.group)
 
+    # -- a step issued in parts (e.g. a layer at a time during backward) --
+    def _leaves(self, idx, grads):
+        gdt = {torch.float32: _native.TK_F32, torch.bfloat16: _native.TK_BF16}
+        pdt = gdt[self.dtype]
+        arr = (_native.TkMuonLeaf * max(len(idx), 1))()
+        for k, i in enumerate(idx):
+            r, c = self.shapes[i]
+            g = grads[i]
+            if g.numel() != r * c or not g.is_contiguous():
+                raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
+            arr[k] = _native.TkMuonLeaf(self.param(i).data_ptr(), g.data_ptr(),
+                                        self.momentum[i].data_ptr(), 1, r, c, pdt, gdt[g.dtype])
+        return arr
+
+    def step_begin(self, stream=None) -> None:
+        """Collective: opens a step issued in parts (step_part)."""
+        with torch.cuda.stream(stream or torch.cuda.current_stream(self.device)):
+            if self.exchange in ("peers", "copy"):
+                dist.all_reduce(self.barrier_buf, group=self.group)
+
+    def step_part(self, idx, grads, stream=None) -> None:
+        """Steps the rank's own matrices among ``idx`` on ``stream``; with the
+        copy exchange their copies into the peers may still run afterwards."""
+        mine = [i for i in idx if self.owner[i] == self.rank]
+        if not mine:
+            return
+        L = _native.lib()
+        s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
+        arr = self._leaves(mine, grads)
+        if self.exchange == "peers":
+            _native.check(L.tk_muon_step_peers(arr, len(mine), ctypes.byref(self.hp),
+                                               self.peers.deltas, self.peers.n, s))
+        elif self.exchange == "copy":
+            _native.check(L.tk_muon_step_copy_deferred(arr, len(mine), ctypes.byref(self.hp),
+                                                       self.peers.deltas, self.peers.n, s))
+        else:
+            _native.check(L.tk_muon_step(arr, len(mine), ctypes.byref(self.hp), s))
+
+    def step_end(self, stream=None) -> None:
+        """Collective: completes the exchange of a step issued in parts."""
+        st = stream or torch.cuda.current_stream(self.device)
+        with torch.cuda.stream(st):
+            if self.exchange == "copy":
+                _native.check(_native.lib().tk_muon_copy_join(st.cuda_stream))
+            if self.exchange in ("peers", "copy"):
+                dist.all_reduce(self.barrier_buf, group=self.group)
+            elif self.exchange == "allgather":
+                lo = self.rank * self.extent
+                dist.all_gather_into_tensor(self.params, self.params[lo:lo + self.extent],
+                                            group=self.group)
+
     def close(self) -> None:
         if self.peers is not None:
             self.peers.close()
