@@ -169,6 +169,59 @@ def test_pinned_host_buffers(kind, max_norm):
         assert_bitexact(a.numpy(), b, "pinned")
 
 
+@pytest.mark.parametrize("kind,max_norm", [("adamw", 1.0), ("sgd", 0.5), ("lion", 0.0)])
+def test_pinned_host_many_small_leaves(kind, max_norm):
+    """Small pinned leaves are gathered into one staging block with zero
+    padding between them; ragged sizes and two large leaves around them must
+    still match the oracle bit for bit, and no byte outside the leaves moves."""
+    rng = np.random.default_rng(11)
+    sizes = [int(x) for x in rng.integers(1, 5000, size=40)] + [70000, 1 << 17]
+    sizes.insert(7, 65536)  # the largest staged size
+    perm = rng.permutation(len(sizes))
+    sizes = [sizes[i] for i in perm]
+    adam = kind == "adamw"
+    # one pinned buffer per array with guard words around every leaf
+    def arena(fill):
+        n = sum(sizes) + 8 * (len(sizes) + 1)
+        t = torch.full((n,), fill, dtype=torch.float32).pin_memory()
+        views, at = [], 8
+        for k in sizes:
+            views.append(t[at:at + k])
+            at += k + 8
+        return t, views
+    P, p = arena(7.0)
+    M, m = arena(7.0)
+    V, v = arena(7.0)
+    for t in p:
+        t.copy_(torch.randn(t.numel()) * 0.02)
+    for t in m + v:
+        t.zero_()
+    rp = [t.numpy().copy() for t in p]
+    rm = [t.numpy().copy() for t in m]
+    rv = [t.numpy().copy() for t in v]
+    guard = [P.numpy().copy(), M.numpy().copy(), V.numpy().copy()]
+    for step in (1, 2):
+        g = [(torch.randn(n) * 0.05).pin_memory() for n in sizes]
+        s = _native.step_fast_buffers([t.data_ptr() for t in p], [t.data_ptr() for t in g],
+                                      [t.data_ptr() for t in m],
+                                      [t.data_ptr() for t in v] if adam else [], sizes,
+                                      max_norm, kind, step, 1e-3, 0.9, 0.99, 1e-8, 0.01)
+        r = oracle.step_two_tier(rp, [t.numpy().copy() for t in g], rm, rv if adam else None,
+                                 oracle.opt_kind(kind), 1e-3, 0.9, 0.99, 1e-8, 0.01, step,
+                                 max_norm)
+        assert s == r
+    for a, b in zip(p + m + (v if adam else []), rp + rm + (rv if adam else [])):
+        assert_bitexact(a.numpy(), b, "staged")
+    # the guard words between the leaves are untouched
+    for T, before in zip((P, M, V), guard):
+        mask = np.ones(T.numel(), bool)
+        at = 8
+        for k in sizes:
+            mask[at:at + k] = False
+            at += k + 8
+        np.testing.assert_array_equal(T.numpy()[mask], before[mask])
+
+
 def test_rejects_aliased_leaves():
     t = torch.zeros(100, device="cuda")
     g = torch.zeros(100, device="cuda")
