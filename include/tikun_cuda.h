@@ -340,6 +340,34 @@ TK_API int tk_shard_info(const tk_shard* shard, uint64_t* lo, uint64_t* hi, floa
 /* Collective; waits for the stream, then unmaps the peers and frees the state. */
 TK_API int tk_shard_destroy(tk_shard* shard, void* stream);
 
+/* Muon across the ranks of nccl_comm (no reference counterpart; the
+ * reference's Muon, python/tikun/muon_nd.py:94-160, is single-process).
+ * tk_muon_layout assigns whole matrices to ranks -- longest-processing-time
+ * bin-packing on their dense Newton-Schulz FLOPs 5(4 m^2 n + 2 m^3), largest
+ * first (ties: lower index), each to the least-loaded rank (ties: lower rank)
+ * -- and lays the parameters out owner-major: rank r's matrices, in index
+ * order at 64-element-aligned offsets, in [r*extent, (r+1)*extent).  The
+ * caller allocates the parameter arena (world * extent elements of p_dtype,
+ * replicated on every rank) and tk_muon_shard_init keeps momentum for the
+ * rank's own matrices.  tk_muon_shard_step reads grads[i] (device, g_dtype)
+ * of the rank's own matrices, runs the Muon step on them and exchanges the
+ * parameters (TK_SHARD_COPY: a copy kernel beside the next batch;
+ * TK_SHARD_PEERS: the last GEMM's epilogue; TK_SHARD_ALLGATHER: an
+ * ncclAllGather of the arena).  Calls other than tk_muon_layout are
+ * collective over nccl_comm. */
+typedef struct tk_muon_shard tk_muon_shard;
+TK_API int tk_muon_layout(size_t n_mats, const int64_t* rows, const int64_t* cols, int world,
+                          int32_t* owner_out, uint64_t* offset_out, uint64_t* extent_out);
+TK_API int tk_muon_shard_init(void* nccl_comm, size_t n_mats, const int64_t* rows,
+                              const int64_t* cols, void* p_arena, int32_t p_dtype,
+                              const tk_muon_hparams* hp, int32_t exchange, void* stream,
+                              tk_muon_shard** out);
+TK_API int tk_muon_shard_info(const tk_muon_shard* shard, int32_t* owner_out, uint64_t* offset_out,
+                              uint64_t* extent_out);
+TK_API int tk_muon_shard_step(tk_muon_shard* shard, const void* const* grads, int32_t g_dtype,
+                              void* stream);
+TK_API int tk_muon_shard_destroy(tk_muon_shard* shard, void* stream);
+
 /* A communicator without PyTorch: rank 0 makes the id (TK_NCCL_ID_BYTES),
  * every rank passes the same bytes to tk_nccl_comm_init. */
 TK_API int tk_nccl_unique_id(void* id_out);

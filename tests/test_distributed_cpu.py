@@ -190,3 +190,27 @@ def test_chunk_major_rejects_unaligned_arena():
 
     with pytest.raises(ValueError):
         chunk_major_pieces(1000, 2, 0, 4)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_native_muon_layout_matches_python(world):
+    """tk_muon_layout (the C ABI's LPT + owner-major layout) assigns and
+    places every matrix exactly as tikun_b200.sharding does."""
+    import ctypes
+
+    from tikun_b200 import _native
+
+    mats = llama8b_mats()[:21] + [(768, 3072), (3072, 768), (96, 40), (17, 45), (768, 768)] * 3
+    n = len(mats)
+    rows = (ctypes.c_int64 * n)(*[r for r, _ in mats])
+    cols = (ctypes.c_int64 * n)(*[c for _, c in mats])
+    owner = (ctypes.c_int32 * n)()
+    offs = (ctypes.c_uint64 * n)()
+    extent = ctypes.c_uint64()
+    _native.check(_native.lib().tk_muon_layout(n, rows, cols, world, owner, offs,
+                                               ctypes.byref(extent)))
+    want_owner = lpt_assign([ns_dense_flops(r, c) for r, c in mats], world)
+    want_offs, want_extent = owner_major_layout([r * c for r, c in mats], want_owner, world)
+    assert list(owner) == want_owner
+    assert list(offs) == want_offs
+    assert extent.value == want_extent

@@ -252,6 +252,8 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
         exchange = "copy"
     parts = exchange.endswith("-parts")
     exchange = exchange.replace("-parts", "")
+    native = exchange.startswith("native-")
+    exchange = exchange.replace("native-", "")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
@@ -262,7 +264,12 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
         p0 = [torch.randn(r, c, generator=gen) * 0.02 for r, c in MUON_SHAPES]
         grads = [[(torch.randn(r, c, generator=gen) * 1e-3) for r, c in MUON_SHAPES]
                  for _ in range(3)]
-        ms = MuonShard(MUON_SHAPES, dtype, dev, lr=0.02, exchange=exchange)
+        if native:
+            from tikun_b200.distributed import NativeMuonShard
+
+            ms = NativeMuonShard(MUON_SHAPES, dtype, dev, lr=0.02, exchange=exchange)
+        else:
+            ms = MuonShard(MUON_SHAPES, dtype, dev, lr=0.02, exchange=exchange)
         for i in range(len(MUON_SHAPES)):
             ms.param(i).copy_(p0[i])
         for s in range(3):
@@ -304,11 +311,15 @@ def _muon_rank(rank, world, port, q, exchange, dtype_name):
                                                  ("allgather", "bfloat16"),
                                                  ("copy-parts", "bfloat16"),
                                                  ("peers-parts", "float32"),
-                                                 ("allgather-parts", "bfloat16")])
+                                                 ("allgather-parts", "bfloat16"),
+                                                 ("native-copy", "bfloat16"),
+                                                 ("native-peers", "float32"),
+                                                 ("native-allgather", "bfloat16")])
 def test_muon_shard_two_gpus_matches_single_gpu(exchange, dtype_name):
     """MuonShard (LPT-assigned matrices; peer stores from the final
     Newton-Schulz epilogue, a copy kernel or the copy engines beside the next
-    batch, or an all-gather; in one call or in parts as in backward) equals tk_muon_step of every
+    batch, or an all-gather; in one call or in parts as in backward; through
+    the Python class or the C ABI's tk_muon_shard_*) equals tk_muon_step of every
     matrix on one GPU bit for bit, on both ranks: each matrix's arithmetic is
     independent of which batch or GPU it runs in."""
     ctx = mp.get_context("spawn")

@@ -148,6 +148,13 @@ _SIGNATURES = {
     "tk_shard_info": [_P, ctypes.POINTER(_U64), ctypes.POINTER(_U64), ctypes.POINTER(_P),
                       ctypes.POINTER(_P)],
     "tk_shard_destroy": [_P, _P],
+    "tk_muon_layout": [_SZ, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.c_int,
+                       ctypes.POINTER(_I32), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "tk_muon_shard_init": [_P, _SZ, ctypes.POINTER(_I64), ctypes.POINTER(_I64), _P, _I32,
+                           ctypes.POINTER(TkMuonHParams), _I32, _P, ctypes.POINTER(_P)],
+    "tk_muon_shard_info": [_P, ctypes.POINTER(_I32), ctypes.POINTER(_U64), ctypes.POINTER(_U64)],
+    "tk_muon_shard_step": [_P, ctypes.POINTER(_P), _I32, _P],
+    "tk_muon_shard_destroy": [_P, _P],
     "tk_nccl_unique_id": [_P],
     "tk_nccl_comm_init": [_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)],
     "tk_nccl_comm_destroy": [_P],

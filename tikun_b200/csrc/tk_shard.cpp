@@ -465,3 +465,282 @@ int tk_shard_destroy(tk_shard* sh, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- Muon shards
+// Whole matrices are owned by one rank each: longest-processing-time
+// bin-packing on their dense Newton-Schulz FLOPs 5(4 m^2 n + 2 m^3) (m = min,
+// n = max) -- largest first (ties: lower index), each to the least-loaded rank
+// (ties: lower rank) -- and an owner-major parameter arena: rank r's matrices,
+// in index order at 64-element-aligned offsets, fill [r*E, (r+1)*E) with the
+// extent E equal for every rank.
+namespace {
+
+uint64_t ns_flops(int64_t r, int64_t c) {
+  const uint64_t m = (uint64_t)std::min(r, c), n = (uint64_t)std::max(r, c);
+  return 5ull * (4ull * m * m * n + 2ull * m * m * m);
+}
+
+}  // namespace
+
+struct tk_muon_shard {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1, device = 0;
+  int32_t p_dtype = TK_BF16, exchange = TK_SHARD_COPY;
+  tk_muon_hparams hp{};
+  char* p = nullptr;  // owner-major arena
+  std::vector<int64_t> rows, cols;
+  std::vector<int32_t> owner;
+  std::vector<uint64_t> offset;
+  uint64_t extent = 0;
+  std::vector<size_t> mine;
+  std::vector<uint64_t> mom_off;  // per own matrix, elements into mom
+  float* mom = nullptr;
+  double* barrier = nullptr;
+  std::vector<void*> peer_ptrs;
+  std::vector<int64_t> deltas;
+};
+
+extern "C" {
+
+int tk_muon_layout(size_t n_mats, const int64_t* rows, const int64_t* cols, int world,
+                   int32_t* owner_out, uint64_t* offset_out, uint64_t* extent_out) {
+  clear_error();
+  if (world < 1) return set_error(TK_ERR_INVALID, "world %d < 1", world);
+  if (n_mats > 0 && (rows == nullptr || cols == nullptr || owner_out == nullptr ||
+                     offset_out == nullptr))
+    return set_error(TK_ERR_INVALID, "null argument");
+  if (extent_out == nullptr) return set_error(TK_ERR_INVALID, "extent_out is NULL");
+  for (size_t i = 0; i < n_mats; ++i)
+    if (rows[i] <= 0 || cols[i] <= 0)
+      return set_error(TK_ERR_INVALID, "matrix %zu has shape %lld x %lld", i,
+                       (long long)rows[i], (long long)cols[i]);
+  std::vector<size_t> order(n_mats);
+  for (size_t i = 0; i < n_mats; ++i) order[i] = i;
+  std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) {
+    return ns_flops(rows[a], cols[a]) > ns_flops(rows[b], cols[b]);
+  });
+  std::vector<uint64_t> load((size_t)world, 0);
+  for (size_t i : order) {
+    int best = 0;
+    for (int r = 1; r < world; ++r)
+      if (load[(size_t)r] < load[(size_t)best]) best = r;
+    owner_out[i] = best;
+    load[(size_t)best] += ns_flops(rows[i], cols[i]);
+  }
+  std::vector<uint64_t> cursor((size_t)world, 0);
+  for (size_t i = 0; i < n_mats; ++i) {
+    const uint64_t sz = (uint64_t)rows[i] * (uint64_t)cols[i];
+    offset_out[i] = cursor[(size_t)owner_out[i]];
+    cursor[(size_t)owner_out[i]] += (sz + 63) / 64 * 64;
+  }
+  uint64_t extent = 64;
+  for (uint64_t c : cursor) extent = std::max(extent, c);
+  extent = (extent + 63) / 64 * 64;
+  for (size_t i = 0; i < n_mats; ++i) offset_out[i] += (uint64_t)owner_out[i] * extent;
+  *extent_out = extent;
+  return TK_OK;
+}
+
+static void muon_shard_free(tk_muon_shard* sh) {
+  for (void* p : sh->peer_ptrs) tk_ipc_close(p);
+  if (sh->mom) cudaFree(sh->mom);
+  if (sh->barrier) cudaFree(sh->barrier);
+  delete sh;
+}
+
+int tk_muon_shard_init(void* nccl_comm, size_t n_mats, const int64_t* rows, const int64_t* cols,
+                       void* p_arena, int32_t p_dtype, const tk_muon_hparams* hp,
+                       int32_t exchange, void* stream, tk_muon_shard** out) {
+  clear_error();
+  if (out == nullptr) return set_error(TK_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  if (nccl_comm == nullptr || p_arena == nullptr || hp == nullptr)
+    return set_error(TK_ERR_INVALID, "null communicator, arena or hparams");
+  if (p_dtype != TK_F32 && p_dtype != TK_BF16)
+    return set_error(TK_ERR_INVALID, "parameter dtype %d is not f32 or bf16", p_dtype);
+  if (exchange != TK_SHARD_ALLGATHER && exchange != TK_SHARD_PEERS && exchange != TK_SHARD_COPY)
+    return set_error(TK_ERR_INVALID, "unknown exchange mode %d", exchange);
+  const Nccl* N = nullptr;
+  TK_TRY(nccl(&N));
+  ncclComm_t comm = static_cast<ncclComm_t>(nccl_comm);
+  int world = 0, rank = 0, cdev = 0, dev = 0;
+  TK_NCCL_TRY(N, N->CommCount(comm, &world));
+  TK_NCCL_TRY(N, N->CommUserRank(comm, &rank));
+  TK_NCCL_TRY(N, N->CommCuDevice(comm, &cdev));
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (cdev != dev)
+    return set_error(TK_ERR_INVALID, "the communicator is on device %d, the current device is %d",
+                     cdev, dev);
+  if (exchange != TK_SHARD_ALLGATHER && world > 1 + kMaxPeers)
+    return set_error(TK_ERR_UNSUPPORTED, "peer stores reach at most %d peers", kMaxPeers);
+  tk_muon_shard* sh = new tk_muon_shard();
+  auto fail = [&](int code) {
+    muon_shard_free(sh);
+    return code;
+  };
+  sh->comm = comm;
+  sh->rank = rank;
+  sh->world = world;
+  sh->device = dev;
+  sh->p_dtype = p_dtype;
+  sh->exchange = exchange;
+  sh->hp = *hp;
+  sh->p = static_cast<char*>(p_arena);
+  sh->rows.assign(rows, rows + n_mats);
+  sh->cols.assign(cols, cols + n_mats);
+  sh->owner.resize(n_mats);
+  sh->offset.resize(n_mats);
+  int st = tk_muon_layout(n_mats, rows, cols, world, sh->owner.data(), sh->offset.data(),
+                          &sh->extent);
+  if (st != TK_OK) return fail(st);
+  uint64_t mom_elems = 0;
+  for (size_t i = 0; i < n_mats; ++i)
+    if (sh->owner[i] == rank) {
+      sh->mine.push_back(i);
+      sh->mom_off.push_back(mom_elems);
+      mom_elems += (uint64_t)rows[i] * (uint64_t)cols[i];
+    }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMalloc(&sh->barrier, 256) != cudaSuccess ||
+      (mom_elems > 0 && cudaMalloc(&sh->mom, sizeof(float) * mom_elems) != cudaSuccess)) {
+    cudaGetLastError();
+    return fail(set_error(TK_ERR_ALLOC, "could not allocate the Muon momentum"));
+  }
+  if (cudaMemsetAsync(sh->barrier, 0, 256, s) != cudaSuccess ||
+      (sh->mom && cudaMemsetAsync(sh->mom, 0, sizeof(float) * mom_elems, s) != cudaSuccess))
+    return fail(set_error(TK_ERR_CUDA, "could not clear the Muon momentum"));
+  if (exchange != TK_SHARD_ALLGATHER && world > 1) {
+    // every rank's arena, gathered through NCCL, then mapped
+    PeerInfo mine;
+    std::memset(&mine, 0, sizeof(mine));
+    mine.n_elems = sh->extent * (uint64_t)world;
+    mine.exchange = exchange;
+    st = tk_ipc_export(p_arena, mine.handle, &mine.offset);
+    if (st != TK_OK) return fail(st);
+    std::vector<PeerInfo> all((size_t)world);
+    void* buf = nullptr;
+    if (cudaMalloc(&buf, sizeof(PeerInfo) * (size_t)(world + 1)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(set_error(TK_ERR_ALLOC, "could not allocate the init exchange buffer"));
+    }
+    char* gathered = static_cast<char*>(buf) + sizeof(PeerInfo);
+    if (cudaMemcpyAsync(buf, &mine, sizeof(mine), cudaMemcpyHostToDevice, s) != cudaSuccess)
+      st = set_error(TK_ERR_CUDA, "init exchange copy failed");
+    ncclResult_t nr = ncclSuccess;
+    if (st == TK_OK) {
+      nr = N->AllGather(buf, gathered, sizeof(PeerInfo), ncclUint8, comm, s);
+      if (nr != ncclSuccess)
+        st = set_error(TK_ERR_CUDA, "ncclAllGather of the arena descriptions failed: %s",
+                       N->GetErrorString(nr));
+    }
+    if (st == TK_OK &&
+        (cudaMemcpyAsync(all.data(), gathered, sizeof(PeerInfo) * (size_t)world,
+                         cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+         cudaStreamSynchronize(s) != cudaSuccess))
+      st = set_error(TK_ERR_CUDA, "init exchange read-back failed");
+    cudaFree(buf);
+    if (st != TK_OK) return fail(st);
+    for (int r = 0; r < world; ++r) {
+      if (all[(size_t)r].n_elems != mine.n_elems || all[(size_t)r].exchange != exchange)
+        return fail(set_error(TK_ERR_INVALID, "rank %d has another layout or exchange", r));
+      if (r == rank) continue;
+      void* ptr = nullptr;
+      st = tk_ipc_import(all[(size_t)r].handle, all[(size_t)r].offset, &ptr);
+      if (st != TK_OK) return fail(st);
+      sh->peer_ptrs.push_back(ptr);
+      sh->deltas.push_back((int64_t)(static_cast<char*>(ptr) - sh->p));
+      if (sh->deltas.back() % 16 != 0)
+        return fail(set_error(TK_ERR_UNSUPPORTED,
+                              "rank %d's arena is not at the same address modulo 16 bytes as "
+                              "this rank's; use TK_SHARD_ALLGATHER", r));
+    }
+  }
+  *out = sh;
+  return TK_OK;
+}
+
+int tk_muon_shard_info(const tk_muon_shard* sh, int32_t* owner_out, uint64_t* offset_out,
+                       uint64_t* extent_out) {
+  clear_error();
+  if (sh == nullptr) return set_error(TK_ERR_INVALID, "shard is NULL");
+  if (owner_out) std::copy(sh->owner.begin(), sh->owner.end(), owner_out);
+  if (offset_out) std::copy(sh->offset.begin(), sh->offset.end(), offset_out);
+  if (extent_out) *extent_out = sh->extent;
+  return TK_OK;
+}
+
+int tk_muon_shard_step(tk_muon_shard* sh, const void* const* grads, int32_t g_dtype,
+                       void* stream) {
+  clear_error();
+  if (sh == nullptr) return set_error(TK_ERR_INVALID, "shard is NULL");
+  if (g_dtype != TK_F32 && g_dtype != TK_BF16)
+    return set_error(TK_ERR_INVALID, "gradient dtype %d is not f32 or bf16", g_dtype);
+  if (!sh->mine.empty() && grads == nullptr) return set_error(TK_ERR_INVALID, "grads is NULL");
+  const Nccl* N = nullptr;
+  TK_TRY(nccl(&N));
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev != sh->device)
+    return set_error(TK_ERR_INVALID, "the shard lives on device %d, the current device is %d",
+                     sh->device, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t esz = sh->p_dtype == TK_F32 ? 4 : 2;
+  std::vector<tk_muon_leaf> leaves;
+  for (size_t k = 0; k < sh->mine.size(); ++k) {
+    const size_t i = sh->mine[k];
+    if (grads[i] == nullptr) return set_error(TK_ERR_INVALID, "gradient %zu is NULL", i);
+    tk_muon_leaf L;
+    std::memset(&L, 0, sizeof(L));
+    L.p = sh->p + sh->offset[i] * esz;
+    L.g = grads[i];
+    L.momentum = sh->mom + sh->mom_off[k];
+    L.heads = 1;
+    L.rows = sh->rows[i];
+    L.cols = sh->cols[i];
+    L.p_dtype = sh->p_dtype;
+    L.g_dtype = g_dtype;
+    leaves.push_back(L);
+  }
+  const tk_muon_leaf* lp = leaves.empty() ? nullptr : leaves.data();
+  const bool peers = sh->world > 1 && sh->exchange != TK_SHARD_ALLGATHER;
+  if (peers)  // the peers are done reading this step's destination ranges
+    TK_NCCL_TRY(N, N->AllReduce(sh->barrier, sh->barrier, 1, ncclFloat64, ncclSum, sh->comm, s));
+  if (peers && sh->exchange == TK_SHARD_PEERS)
+    TK_TRY(tk_muon_step_peers(lp, leaves.size(), &sh->hp, sh->deltas.data(),
+                              (int)sh->deltas.size(), s));
+  else if (peers)
+    TK_TRY(tk_muon_step_copy(lp, leaves.size(), &sh->hp, sh->deltas.data(),
+                             (int)sh->deltas.size(), s));
+  else
+    TK_TRY(tk_muon_step(lp, leaves.size(), &sh->hp, s));
+  if (peers)
+    TK_NCCL_TRY(N, N->AllReduce(sh->barrier, sh->barrier, 1, ncclFloat64, ncclSum, sh->comm, s));
+  else if (sh->world > 1)
+    TK_NCCL_TRY(N, N->AllGather(sh->p + (uint64_t)sh->rank * sh->extent * esz, sh->p,
+                                sh->extent * esz, ncclUint8, sh->comm, s));
+  return TK_OK;
+}
+
+int tk_muon_shard_destroy(tk_muon_shard* sh, void* stream) {
+  clear_error();
+  if (sh == nullptr) return TK_OK;
+  int st = TK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!sh->peer_ptrs.empty()) {
+    const Nccl* N = nullptr;
+    st = nccl(&N);
+    if (st == TK_OK) {
+      ncclResult_t r = N->AllReduce(sh->barrier, sh->barrier, 1, ncclFloat64, ncclSum, sh->comm, s);
+      if (r != ncclSuccess)
+        st = set_error(TK_ERR_CUDA, "end-of-life barrier failed: %s", N->GetErrorString(r));
+      else if (cudaStreamSynchronize(s) != cudaSuccess)
+        st = set_error(TK_ERR_CUDA, "end-of-life barrier did not complete");
+    }
+  } else {
+    cudaDeviceSynchronize();
+  }
+  muon_shard_free(sh);
+  return st;
+}
+
+}  // extern "C"

@@ -462,3 +462,73 @@ class MuonShard:
         if self.peers is not None:
             self.peers.close()
             self.peers = None
+
+
+class NativeMuonShard:
+    """MuonShard through the C ABI (tk_muon_shard_*): the LPT assignment, the
+    owner-major layout, the momentum, the exchange and its collectives run in
+    the library over the process group's NCCL communicator (or ``comm``)."""
+
+    def __init__(self, shapes, dtype: torch.dtype, device, lr: float, momentum: float = 0.95,
+                 nesterov: bool = True, ns_steps: int = 5, precision: int | None = None,
+                 group=None, exchange: str = "copy", comm: int | None = None):
+        if dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("Muon parameters are f32 or bf16")
+        L = _native.lib()
+        self.shapes = [tuple(s) for s in shapes]
+        self.device = torch.device(device)
+        self.dtype = dtype
+        n = len(self.shapes)
+        world = dist.get_world_size(group)
+        rows = (ctypes.c_int64 * max(n, 1))(*[r for r, _ in self.shapes])
+        cols = (ctypes.c_int64 * max(n, 1))(*[c for _, c in self.shapes])
+        owner = (ctypes.c_int32 * max(n, 1))()
+        offs = (ctypes.c_uint64 * max(n, 1))()
+        extent = ctypes.c_uint64()
+        _native.check(L.tk_muon_layout(n, rows, cols, world, owner, offs, ctypes.byref(extent)))
+        self.owner, self.offs, self.extent = list(owner)[:n], list(offs)[:n], extent.value
+        self.rank = dist.get_rank(group)
+        self.mine = [i for i in range(n) if self.owner[i] == self.rank]
+        self.params = torch.zeros(self.extent * world, dtype=dtype, device=self.device)
+        hp = _native.TkMuonHParams(lr, momentum, 1 if nesterov else 0, ns_steps,
+                                   _native.DEFAULT_NS_PRECISION if precision is None
+                                   else precision)
+        mode = {"allgather": 0, "peers": 1, "copy": 2}[exchange]
+        comm = comm or nccl_comm_ptr(group, self.device)
+        handle = ctypes.c_void_p()
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        pdt = _native.TK_F32 if dtype == torch.float32 else _native.TK_BF16
+        _native.check(L.tk_muon_shard_init(comm, n, rows, cols, self.params.data_ptr(), pdt,
+                                           ctypes.byref(hp), mode, s, ctypes.byref(handle)))
+        self.handle = handle
+        self._n = n
+
+    def param(self, i: int) -> torch.Tensor:
+        r, c = self.shapes[i]
+        return self.params[self.offs[i]:self.offs[i] + r * c].view(r, c)
+
+    def step(self, grads) -> None:
+        """``grads[i]``: contiguous device tensors of one dtype (f32 or bf16)
+        for the rank's own matrices; enqueued on the current stream."""
+        ptrs = (ctypes.c_void_p * max(self._n, 1))()
+        gdt = None
+        for i in self.mine:
+            g = grads[i]
+            r, c = self.shapes[i]
+            if g.numel() != r * c or not g.is_contiguous():
+                raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
+            d = _native.TK_F32 if g.dtype == torch.float32 else _native.TK_BF16
+            if gdt is not None and d != gdt:
+                raise ValueError("all gradients of a step share one dtype")
+            gdt = d
+            ptrs[i] = g.data_ptr()
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        _native.check(_native.lib().tk_muon_shard_step(
+            self.handle, ptrs, _native.TK_F32 if gdt is None else gdt, s))
+
+    def close(self) -> None:
+        """Collective: every rank calls it before the process group goes."""
+        if self.handle:
+            s = torch.cuda.current_stream(self.device).cuda_stream
+            _native.check(_native.lib().tk_muon_shard_destroy(self.handle, s))
+            self.handle = None
