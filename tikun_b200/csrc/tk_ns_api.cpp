@@ -97,6 +97,39 @@ static int peer_copy_streams(PeerCopy* pc) {
   return TK_OK;
 }
 
+// Shape groups of one call run concurrently on side streams: a persistent
+// GEMM launch of one group leaves SMs idle in its first and last waves, and
+// another group's launch fills them.  That pays for calls of modest work (the
+// GPT-2 and 1.3B shapes: 3 % and 10 % per clock) but not for the 8B shapes,
+// whose launches are many waves long (4 % slower per clock), so calls under
+// 50 dense TFLOP use 2 streams and larger ones 1; TIKUN_NS_STREAMS (1..4)
+// overrides.
+struct GroupStreams {
+  std::mutex mu;  // one call at a time uses a device's streams
+  bool ready = false;
+  cudaStream_t st[4] = {};
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join[4] = {};
+};
+
+static int ns_streams(double call_flops) {
+  static const int forced = [] {
+    const char* e = std::getenv("TIKUN_NS_STREAMS");
+    return e ? std::max(1, std::min(std::atoi(e), 4)) : 0;
+  }();
+  if (forced) return forced;
+  return call_flops < 50e12 ? 2 : 1;
+}
+
+static int group_streams(GroupStreams** out) {
+  static GroupStreams devs[64];
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  *out = &devs[dev];
+  return TK_OK;
+}
+
 // Runs NS over matrices that are all m x n or n x m, in waves that fit the
 // scratch budget and the per-launch pointer capacity.  With `copy`, each
 // wave's finished parameters are copied into the peers' copies by the copy
@@ -311,17 +344,42 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
   }
   std::stable_sort(order.begin(), order.end(),
                    [](const auto& a, const auto& b) { return a.first < b.first; });
-  for (auto& ord : order) {
-    auto& kv = *ord.second;
+  double call_flops = 0.0;
+  for (const auto& o : order) call_flops -= o.first * (double)hp->ns_steps;
+  const int ks = std::min<int>(ns_streams(call_flops), (int)order.size());
+  GroupStreams* GS = nullptr;
+  std::unique_lock<std::mutex> gs_lock;
+  if (ks > 1) {
+    TK_TRY(group_streams(&GS));
+    gs_lock = std::unique_lock<std::mutex>(GS->mu);
+    if (!GS->ready) {
+      for (int j = 0; j < 4; ++j) {
+        TK_CUDA_TRY(cudaStreamCreateWithFlags(&GS->st[j], cudaStreamNonBlocking));
+        TK_CUDA_TRY(cudaEventCreateWithFlags(&GS->join[j], cudaEventDisableTiming));
+      }
+      TK_CUDA_TRY(cudaEventCreateWithFlags(&GS->fork, cudaEventDisableTiming));
+      GS->ready = true;
+    }
+    TK_CUDA_TRY(cudaEventRecord(GS->fork, s));
+    for (int j = 0; j < ks; ++j) TK_CUDA_TRY(cudaStreamWaitEvent(GS->st[j], GS->fork, 0));
+  }
+  for (size_t gi = 0; gi < order.size(); ++gi) {
+    auto& kv = *order[gi].second;
+    cudaStream_t gs = ks > 1 ? GS->st[gi % (size_t)ks] : s;
     const int64_t m = std::get<0>(kv.first), n = std::get<1>(kv.first);
     const int pdt = std::get<2>(kv.first), gdt = std::get<3>(kv.first);
     // rows/cols is m/n (<= 1) for a wide matrix and n/m for a tall one
     const float upd_wide = (float)(-hp->lr * std::sqrt(std::max(1.0, (double)m / (double)n)));
     const float upd_tall = (float)(-hp->lr * std::sqrt(std::max(1.0, (double)n / (double)m)));
     TK_TRY(run_batches(m, n, kv.second.g, kv.second.p, &kv.second.mom, kv.second.tall, gdt, pdt,
-                       1, upd_wide, upd_tall, mu, om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, s,
+                       1, upd_wide, upd_tall, mu, om, hp->nesterov ? 1 : 0, hp->ns_steps, fmt, gs,
                        peers, copy));
   }
+  if (ks > 1)  // the caller's stream waits for every group
+    for (int j = 0; j < ks; ++j) {
+      TK_CUDA_TRY(cudaEventRecord(GS->join[j], GS->st[j]));
+      TK_CUDA_TRY(cudaStreamWaitEvent(s, GS->join[j], 0));
+    }
   if (copy != nullptr && copy->join) {
     const int streams = copy->engines ? copy->n : (copy->n > 0 ? 1 : 0);
     for (int j = 0; j < streams; ++j) {  // the caller's stream waits for every copy
