@@ -648,8 +648,10 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     elif world == 1:
         # in-backward (one GPU): layer l's grads are produced on the main stream
         # (a generator kernel standing in for backward), then its Muon and
-        # AdamW steps run on a side stream, in reverse layer order
-        side = torch.cuda.Stream(device=dev)
+        # AdamW steps run on a side stream, in reverse layer order; two side
+        # streams take alternate layers, so one layer's step can overlap the
+        # previous one's
+        sides = [torch.cuda.Stream(device=dev) for _ in range(2)]
         per_layer = len(mats) // wl["layers"]
         layer_mu = [mu_leaves(list(range(l * per_layer, (l + 1) * per_layer)))
                     for l in range(wl["layers"])]
@@ -662,8 +664,9 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         def one_step():
             state["step"] += 1
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(side)
+            e0.record(stream)
             for l in reversed(range(wl["layers"])):
+                side = sides[l % 2]
                 for i in range(l * per_layer, (l + 1) * per_layer):
                     g_mu[i].normal_(0, 1e-3, generator=gen)
                 layer_ev[l].record(stream)
@@ -676,9 +679,10 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
             _native.check(L.tk_apply_pointwise(rest_aw[0], rest_aw[1], _native.TK_ADAMW,
                                                ctypes.byref(hp), state["step"], None,
                                                side.cuda_stream))
-            e1.record(side)
+            for sd in sides:
+                stream.wait_stream(sd)
+            e1.record(stream)
             ns_ev.append((e0, e1))
-            stream.wait_stream(side)
             return -1
 
     uuid = str(torch.cuda.get_device_properties(dev).uuid)

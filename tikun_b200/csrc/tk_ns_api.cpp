@@ -105,11 +105,13 @@ static int peer_copy_streams(PeerCopy* pc) {
 // 50 dense TFLOP use 2 streams and larger ones 1; TIKUN_NS_STREAMS (1..4)
 // overrides.
 struct GroupStreams {
-  std::mutex mu;  // one call at a time uses a device's streams
+  std::mutex mu;  // serialises the enqueueing, not the device work
   bool ready = false;
   cudaStream_t st[4] = {};
   cudaEvent_t fork = nullptr;
   cudaEvent_t join[4] = {};
+  unsigned calls = 0;  // successive calls take successive pairs of streams, so
+                       // calls from different caller streams can overlap too
 };
 
 static int ns_streams(double call_flops) {
@@ -361,11 +363,14 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
       GS->ready = true;
     }
     TK_CUDA_TRY(cudaEventRecord(GS->fork, s));
-    for (int j = 0; j < ks; ++j) TK_CUDA_TRY(cudaStreamWaitEvent(GS->st[j], GS->fork, 0));
   }
+  const int base = ks > 1 ? (int)((GS->calls++ * (unsigned)ks) % 4u) : 0;
+  auto sidx = [&](int j) { return (base + j) % 4; };
+  if (ks > 1)
+    for (int j = 0; j < ks; ++j) TK_CUDA_TRY(cudaStreamWaitEvent(GS->st[sidx(j)], GS->fork, 0));
   for (size_t gi = 0; gi < order.size(); ++gi) {
     auto& kv = *order[gi].second;
-    cudaStream_t gs = ks > 1 ? GS->st[gi % (size_t)ks] : s;
+    cudaStream_t gs = ks > 1 ? GS->st[sidx((int)(gi % (size_t)ks))] : s;
     const int64_t m = std::get<0>(kv.first), n = std::get<1>(kv.first);
     const int pdt = std::get<2>(kv.first), gdt = std::get<3>(kv.first);
     // rows/cols is m/n (<= 1) for a wide matrix and n/m for a tall one
@@ -377,8 +382,8 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
   }
   if (ks > 1)  // the caller's stream waits for every group
     for (int j = 0; j < ks; ++j) {
-      TK_CUDA_TRY(cudaEventRecord(GS->join[j], GS->st[j]));
-      TK_CUDA_TRY(cudaStreamWaitEvent(s, GS->join[j], 0));
+      TK_CUDA_TRY(cudaEventRecord(GS->join[sidx(j)], GS->st[sidx(j)]));
+      TK_CUDA_TRY(cudaStreamWaitEvent(s, GS->join[sidx(j)], 0));
     }
   if (copy != nullptr && copy->join) {
     const int streams = copy->engines ? copy->n : (copy->n > 0 ? 1 : 0);
