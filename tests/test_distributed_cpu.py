@@ -214,3 +214,47 @@ def test_native_muon_layout_matches_python(world):
     assert list(owner) == want_owner
     assert list(offs) == want_offs
     assert extent.value == want_extent
+
+
+def _dying_worker(rank, world, port, result_q):
+    """Rank 1 leaves before the step's first collective; rank 0 runs the step's
+    choreography (f64 norm all-reduce, then the parameter all-gather) and must
+    get an error from its process group's timeout instead of hanging."""
+    import time
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    if rank == 1:
+        result_q.put((rank, "left"))
+        result_q.close()
+        result_q.join_thread()  # the message is out before the process goes
+        os._exit(0)  # no collective, no destroy: the rank is simply gone
+    t0 = time.monotonic()
+    try:
+        sumsq = torch.ones(1, dtype=torch.float64)
+        dist.all_reduce(sumsq)
+        parts = [torch.empty(4) for _ in range(world)]
+        dist.all_gather(parts, torch.ones(4))
+        result_q.put((rank, "completed"))
+    except Exception as e:  # the gloo backend raises on timeout or a lost peer
+        result_q.put((rank, f"error after {time.monotonic() - t0:.1f}s: {type(e).__name__}"))
+
+
+def test_rank_leaving_before_the_exchange_errors_instead_of_hanging():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == "left"
+    assert res[0].startswith("error after"), res[0]
+    assert float(res[0].split()[2].rstrip("s:")) < 60

@@ -412,7 +412,10 @@ static int step_device(const tk_leaf* leaves, size_t n, int kind, const tk_hpara
   Scratch norm_scratch;
   double* partials = nullptr;
   int n_partials = 0;
-  if (max_norm > 0.0f) TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s, comm));
+  if (max_norm > 0.0f) {
+    NvtxRange r("tikun/tier1_norm");
+    TK_TRY(launch_norm(plan, &norm_scratch, &partials, &n_partials, s, comm));
+  }
   if (plan.tables.empty()) {  // a rank holding no elements still reports the global scale
     if (scale_dev != nullptr) {
       TK_TRY(launch_clip_scale(partials, n_partials, max_norm, scale_dev, s));
@@ -420,6 +423,7 @@ static int step_device(const tk_leaf* leaves, size_t n, int kind, const tk_hpara
     }
     return TK_OK;
   }
+  NvtxRange r("tikun/tier2_update");
   if (g_update_start) TK_CUDA_TRY(cudaEventRecord(g_update_start, s));
   for (size_t i = 0; i < plan.tables.size(); ++i)
     TK_TRY(launch_table(plan, i, kind, c, partials, n_partials, max_norm, nullptr,
@@ -496,6 +500,7 @@ static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const 
                                cudaStream_t s, void* comm = nullptr) {
   constexpr uint64_t kChunkElems = 8u << 20;
   constexpr int kMaxPieces = kMaxLeavesPerLaunch;
+  NvtxRange range("tikun/host_pipeline");
   HostPipe* P = nullptr;
   TK_TRY(host_pipe(&P));
   std::lock_guard<std::mutex> serial(P->mu);

@@ -4,6 +4,8 @@
 
 #include <cuda_runtime.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include <cstdint>
 #include <string>
 
@@ -27,6 +29,19 @@ int cuda_error(cudaError_t e, const char* what);
     int _s = (expr);               \
     if (_s != TK_OK) return _s;    \
   } while (0)
+
+// ---------------------------------------------------------------- tracing
+// An NVTX range over the enqueueing of one phase (Tier 1, Tier 2, a
+// Newton-Schulz iteration, an exchange); profilers project it onto the GPU
+// work launched inside.  Costs a function-pointer test when no tool is
+// attached.
+class NvtxRange {
+ public:
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // ---------------------------------------------------------------- scratch
 // Stream-ordered device scratch from a per-device memory pool that keeps its

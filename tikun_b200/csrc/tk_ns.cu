@@ -1086,6 +1086,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   const float inv_pre = std::ldexp(1.0f, -k), inv_pre2 = std::ldexp(1.0f, -2 * k);
   int cur_xt = 0;
   static thread_local GemmArgs g, h;
+  NvtxRange range("tikun/ns_iterations");
   for (int it = 0; it < steps; ++it) {
     std::memset(&g, 0, sizeof(g));
     g.batch = (int)L.batch;

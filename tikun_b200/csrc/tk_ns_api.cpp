@@ -368,6 +368,7 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
   auto sidx = [&](int j) { return (base + j) % 4; };
   if (ks > 1)
     for (int j = 0; j < ks; ++j) TK_CUDA_TRY(cudaStreamWaitEvent(GS->st[sidx(j)], GS->fork, 0));
+  NvtxRange range("tikun/muon_step");
   for (size_t gi = 0; gi < order.size(); ++gi) {
     auto& kv = *order[gi].second;
     cudaStream_t gs = ks > 1 ? GS->st[sidx((int)(gi % (size_t)ks))] : s;

@@ -374,6 +374,7 @@ int tk_shard_step(tk_shard* sh, const tk_hparams* hp, uint64_t step, float max_n
   const bool clip = max_norm > 0.f;
   const bool peers = sh->exchange == TK_SHARD_PEERS && sh->world > 1;
   const bool copy = sh->exchange == TK_SHARD_COPY && sh->world > 1;
+  NvtxRange range("tikun/shard_step");
   if (clip) {
     if (nl > 0) TK_TRY(tk_grad_sumsq(L, nl, sh->sumsq, s));
     else TK_CUDA_TRY(cudaMemsetAsync(sh->sumsq, 0, sizeof(double), s));
@@ -703,6 +704,7 @@ int tk_muon_shard_step(tk_muon_shard* sh, const void* const* grads, int32_t g_dt
   }
   const tk_muon_leaf* lp = leaves.empty() ? nullptr : leaves.data();
   const bool peers = sh->world > 1 && sh->exchange != TK_SHARD_ALLGATHER;
+  NvtxRange range("tikun/muon_shard_step");
   if (peers)  // the peers are done reading this step's destination ranges
     TK_NCCL_TRY(N, N->AllReduce(sh->barrier, sh->barrier, 1, ncclFloat64, ncclSum, sh->comm, s));
   if (peers && sh->exchange == TK_SHARD_PEERS)
