@@ -41,3 +41,32 @@ def test_inspect_report():
     assert "load_p_g" in text and "store_p" in text
     with pytest.raises(_native.TikunValueError):
         emit_inspect([0], [1, 2], "adamw", 0.0, 1e-3, 0.9, 0.999, 1e-8, 0.01)
+
+
+def test_optimizer_state_roundtrip_and_report_on_cpu():
+    """state_dict/load_state_dict keep m1/m2 in parameter order (the step
+    itself needs a GPU and is tested there); to_json gives the plan report."""
+    import numpy as np
+
+    from tikun_b200.universal import UniversalOptimizer, _extract_pointer_and_len
+
+    ps = [np.zeros(10, np.float32), np.zeros(5, np.float32)]
+    opt = UniversalOptimizer(ps, max_norm=1.0)
+    ptr, n = _extract_pointer_and_len(ps[0])
+    opt._state_for(ps[0], ptr, n)
+    opt.m1_state[ptr][:] = 3.0
+    opt.m2_state[ptr][:] = 2.0
+    opt.step_count = 7
+    sd = opt.state_dict()
+    assert sd["step"] == 7 and sd["m1"][1] is None
+    qs = [np.zeros(10, np.float32), np.zeros(5, np.float32)]
+    opt2 = UniversalOptimizer(qs)
+    opt2.load_state_dict(sd)
+    p2, _ = _extract_pointer_and_len(qs[0])
+    assert opt2.step_count == 7
+    assert (opt2.m1_state[p2] == 3.0).all() and (opt2.m2_state[p2] == 2.0).all()
+    with pytest.raises(ValueError):
+        UniversalOptimizer([np.zeros(10, np.float32)]).load_state_dict(sd)
+    assert "Hardware Execution Plan" in opt2.to_json()
+    with pytest.raises(NotImplementedError):
+        opt2.to_mlir()

@@ -196,3 +196,61 @@ class UniversalOptimizer:
         for p in self.params:
             if hasattr(p, "grad") and p.grad is not None:
                 p.grad = None
+
+    # -- checkpoint / resume ---------------------------------------------------
+    # The reference keeps m1/m2 keyed by raw pointers and never serialises them
+    # (python/tikun/universal.py:93-95, 116-121); here they can be saved and
+    # restored in parameter order, so a resumed run continues bit-identically.
+    def state_dict(self) -> dict:
+        """The step counter and copies of m1/m2 in parameter order (None for a
+        parameter not stepped yet)."""
+        m1, m2 = [], []
+        for p in self.params:
+            ptr, _ = _extract_pointer_and_len(p)
+            if ptr in self.m1_state:
+                a, b = self.m1_state[ptr], self.m2_state[ptr]
+                m1.append(a.clone() if hasattr(a, "clone") else a.copy())
+                m2.append(b.clone() if hasattr(b, "clone") else b.copy())
+            else:
+                m1.append(None)
+                m2.append(None)
+        return {"step": self.step_count, "m1": m1, "m2": m2}
+
+    def load_state_dict(self, state: dict) -> None:
+        """Restores state_dict() output onto this optimizer's parameters (same
+        order and sizes)."""
+        if len(state["m1"]) != len(self.params):
+            raise ValueError(f"state holds {len(state['m1'])} parameters, the optimizer "
+                             f"{len(self.params)}")
+        self.step_count = int(state["step"])
+        for p, a, b in zip(self.params, state["m1"], state["m2"]):
+            if a is None:
+                continue
+            ptr, n = _extract_pointer_and_len(p)
+            size = a.numel() if hasattr(a, "numel") else a.size
+            if size != n:
+                raise ValueError("state and parameter sizes differ")
+            self._state_for(p, ptr, n)
+            for dst, src in ((self.m1_state[ptr], a), (self.m2_state[ptr], b)):
+                if hasattr(dst, "copy_"):
+                    dst.copy_(src)
+                else:
+                    dst[...] = np.asarray(src)
+
+    # -- inspection (python/tikun/universal.py:199-225) -------------------------
+    def to_json(self) -> str:
+        """The execution-plan report for these parameters, as the reference's
+        to_json returns its emit_inspect text."""
+        from .inspect import emit_inspect
+
+        ptrs = [_extract_pointer_and_len(p)[0] for p in self.params]
+        lens = [_extract_pointer_and_len(p)[1] for p in self.params]
+        return emit_inspect(ptrs, lens, self.algorithm, self.max_norm, self.lr, self.beta1,
+                            self.beta2, self.eps, self.weight_decay)
+
+    def inspect(self):
+        print(self.to_json())
+
+    def to_mlir(self) -> str:
+        raise NotImplementedError("the MLIR text emitter (crates/tikun-core/src/mlir.rs) is "
+                                  "not part of the B200 lowering; see to_json()")
