@@ -258,3 +258,46 @@ def test_rank_leaving_before_the_exchange_errors_instead_of_hanging():
     assert res[1] == "left"
     assert res[0].startswith("error after"), res[0]
     assert float(res[0].split()[2].rstrip("s:")) < 60
+
+
+def _heartbeat_worker(rank, world, port, result_q):
+    """Three host-side steps with a Liveness check before each; rank 1 leaves
+    after step 1 (between steps, nothing in flight)."""
+    from datetime import timedelta
+
+    from tikun_b200.distributed import Liveness, RankLost
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    live = Liveness(timeout=2.0)
+    out = []
+    try:
+        for k in (1, 2, 3):
+            live.step(k)
+            out.append(k)
+            if rank == 1 and k == 1:
+                result_q.put((rank, out))
+                result_q.close()
+                result_q.join_thread()
+                os._exit(0)
+        result_q.put((rank, out))
+    except RankLost as e:
+        result_q.put((rank, out + [str(e)]))
+
+
+def test_liveness_reports_a_rank_that_left_between_steps():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_heartbeat_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1] == [1]
+    assert res[0][:1] == [1] and "rank(s) [1] did not reach step 2" in res[0][1], res[0]

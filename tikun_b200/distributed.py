@@ -207,6 +207,49 @@ class ZeroPointwise:
         self.launches_per_step = launches
 
 
+class RankLost(RuntimeError):
+    """A rank stopped announcing steps: raised on the host before the next
+    launch, so no collective is left waiting for it on the GPU."""
+
+
+class Liveness:
+    """Host-side heartbeat over the process group's key-value store.  Every
+    rank announces step k (``beat``) and, before launching step k's kernels and
+    collectives, waits at most ``timeout`` seconds for every other rank's
+    announcement (``check``); a rank that left between steps is reported as
+    RankLost instead of a hang inside a collective."""
+
+    def __init__(self, store=None, rank: int | None = None, world: int | None = None,
+                 timeout: float = 10.0, prefix: str = "tikun/alive"):
+        from datetime import timedelta
+
+        self.store = store or dist.distributed_c10d._get_default_store()
+        self.rank = dist.get_rank() if rank is None else rank
+        self.world = dist.get_world_size() if world is None else world
+        self.timeout = timedelta(seconds=timeout)
+        self.prefix = prefix
+
+    def _key(self, rank: int, step: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def beat(self, step: int) -> None:
+        self.store.set(self._key(self.rank, step), "1")
+
+    def check(self, step: int) -> None:
+        keys = [self._key(r, step) for r in range(self.world)]
+        try:
+            self.store.wait(keys, self.timeout)
+        except Exception as e:  # the store raises on timeout
+            missing = [r for r in range(self.world) if not self.store.check([self._key(r, step)])]
+            raise RankLost(f"rank(s) {missing} did not reach step {step} within "
+                           f"{self.timeout.total_seconds():.0f} s") from e
+
+    def step(self, step: int) -> None:
+        """beat + check."""
+        self.beat(step)
+        self.check(step)
+
+
 def nccl_comm_ptr(group=None, device=None) -> int:
     """The ncclComm_t behind a PyTorch NCCL process group (created by a tiny
     all-reduce if the group was initialised lazily)."""
@@ -256,11 +299,16 @@ class ShardedStep:
         _native.check(L.tk_shard_info(handle, ctypes.byref(lo), ctypes.byref(hi), None, None))
         self.lo, self.hi = lo.value, hi.value
         self.hparams = _native.TkHParams(hp.lr, hp.beta1, hp.beta2, hp.eps, hp.weight_decay)
+        self.liveness: Liveness | None = None
 
     def step(self, return_scale: bool = False) -> float | None:
         """One step on the current stream; with ``return_scale`` waits for it
-        and returns the clip scale (step_fast_buffers' return value)."""
+        and returns the clip scale (step_fast_buffers' return value).  With a
+        Liveness (``self.liveness``), a rank that left is reported before any
+        launch."""
         self.step_count += 1
+        if self.liveness is not None:
+            self.liveness.step(self.step_count)
         L = _native.lib()
         s = torch.cuda.current_stream(self.p.device).cuda_stream
         out = ctypes.c_float(1.0)
@@ -363,6 +411,8 @@ class MuonShard:
         self.peers = (PeerArena(self.params, group) if self.exchange in ("peers", "copy")
                       else None)
         self.barrier_buf = torch.zeros(1, dtype=torch.float64, device=self.device)
+        self.liveness: Liveness | None = None  # optional host heartbeat before each step
+        self.step_count = 0
 
     def param(self, i: int) -> torch.Tensor:
         r, c = self.shapes[i]
@@ -373,6 +423,9 @@ class MuonShard:
         rank's own matrices ``self.mine``; others are not read.  Enqueued on
         the current stream.  ``events`` (two CUDA events) are recorded just
         around the Newton-Schulz launches."""
+        self.step_count += 1
+        if self.liveness is not None:
+            self.liveness.step(self.step_count)
         L = _native.lib()
         s = torch.cuda.current_stream(self.device).cuda_stream
         gdt = {torch.float32: _native.TK_F32, torch.bfloat16: _native.TK_BF16}
@@ -423,6 +476,9 @@ class MuonShard:
 
     def step_begin(self, stream=None) -> None:
         """Collective: opens a step issued in parts (step_part)."""
+        self.step_count += 1
+        if self.liveness is not None:
+            self.liveness.step(self.step_count)
         with torch.cuda.stream(stream or torch.cuda.current_stream(self.device)):
             if self.exchange in ("peers", "copy"):
                 dist.all_reduce(self.barrier_buf, group=self.group)
@@ -502,6 +558,8 @@ class NativeMuonShard:
                                            ctypes.byref(hp), mode, s, ctypes.byref(handle)))
         self.handle = handle
         self._n = n
+        self.liveness: Liveness | None = None  # optional host heartbeat before each step
+        self.step_count = 0
 
     def param(self, i: int) -> torch.Tensor:
         r, c = self.shapes[i]
@@ -510,6 +568,9 @@ class NativeMuonShard:
     def step(self, grads) -> None:
         """``grads[i]``: contiguous device tensors of one dtype (f32 or bf16)
         for the rank's own matrices; enqueued on the current stream."""
+        self.step_count += 1
+        if self.liveness is not None:
+            self.liveness.step(self.step_count)
         ptrs = (ctypes.c_void_p * max(self._n, 1))()
         gdt = None
         for i in self.mine:
