@@ -266,3 +266,42 @@ def test_bounded_wait_gives_up_and_leaves_the_device_usable():
     t = torch.from_numpy(x.copy()).cuda()
     _native.newton_schulz_2d_ffi(t.data_ptr(), 64, 96, 5)
     assert relf(to_np(t), oracle.polar_step_np(x, 5)) <= 5e-3
+
+
+def _torch_fp32_ns(G: torch.Tensor, steps: int = 5) -> torch.Tensor:
+    """Newton-Schulz in fp32 on the GPU (TF32 off), the oracle's arithmetic
+    (tensor_engine.rs:12-77): transpose if tall, X / max(||X||, 1e-7), then
+    A = X X^T, B = b A + c A A, X = a X + B X."""
+    a, b, c = 3.4445, -4.7750, 2.0315
+    X = G.float()
+    tall = X.shape[0] > X.shape[1]
+    if tall:
+        X = X.T
+    X = X / torch.clamp(X.norm(), min=1e-7)
+    for _ in range(steps):
+        A = X @ X.T
+        B = b * A + c * (A @ A)
+        X = a * X + B @ X
+    return X.T if tall else X
+
+
+@pytest.mark.parametrize("shape", [(4096, 14336), (14336, 4096), (4096, 4096), (4096, 1024)],
+                         ids=lambda s: f"{s[0]}x{s[1]}")
+def test_ns_full_llama_shapes_against_torch_fp32(shape):
+    """The 8B workload's matrix shapes at full size (the oracle's CPU loops
+    would take minutes): the engine's Newton-Schulz (f16 operands) against an
+    fp32 torch restatement of the same iteration, within the f16 bar."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        g = torch.Generator(device="cuda").manual_seed(shape[0] + shape[1])
+        G = torch.randn(*shape, device="cuda", generator=g) * 1e-3
+        want = _torch_fp32_ns(G)
+        X = G.clone()
+        _native.newton_schulz_2d_ffi(X.data_ptr(), shape[0], shape[1], 5)
+        torch.cuda.synchronize()
+        err = float((X - want).norm() / want.norm())
+        assert err <= NS_TOL[_native.TK_NS_F16], err
+        assert _native.device_status() == 0
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
