@@ -30,13 +30,22 @@ using namespace pw;
 // Tuning knobs (compile time): quads each thread keeps in flight per loop
 // trip, the minimum resident CTAs per SM the register budget must allow, and
 // the cache policy of the streaming accesses (0: default, 1: evict-first).
-// Defaults measured best on the GPT-2-small table among unroll {1,2,4} x
-// occupancy floor {1..8} x cache policy: 4 quads per trip, 2 CTAs per SM.
+// Measured on B200: all-f32 leaves are best at 4 quads per trip with 2 CTAs
+// per SM (unroll {1,2,4,8} x occupancy floor {1..8}); leaves with a bf16 p or
+// g at 2 quads per trip with 3 CTAs per SM (a 100M-element AdamW update
+// 614 -> 487 us for bf16 p and g, 598 -> 482 us for bf16 g), where the
+// f32 setting loses 20 % per element.
 #ifndef TK_PW_UNROLL
 #define TK_PW_UNROLL 4
 #endif
 #ifndef TK_PW_MINBLOCKS
 #define TK_PW_MINBLOCKS 2
+#endif
+#ifndef TK_PW_UNROLL_BF16
+#define TK_PW_UNROLL_BF16 2
+#endif
+#ifndef TK_PW_MINBLOCKS_BF16
+#define TK_PW_MINBLOCKS_BF16 3
 #endif
 #ifndef TK_PW_STREAMING
 #define TK_PW_STREAMING 0
@@ -48,7 +57,13 @@ using namespace pw;
 #define TK_PW_OVERSUB 0
 #endif
 constexpr int kThreads = 256;
-constexpr int kUnroll = TK_PW_UNROLL;
+
+template <int PDT, int GDT>
+struct Tune {
+  static constexpr bool all_f32 = PDT == TK_F32 && GDT == TK_F32;
+  static constexpr int unroll = all_f32 ? TK_PW_UNROLL : TK_PW_UNROLL_BF16;
+  static constexpr int minblocks = all_f32 ? TK_PW_MINBLOCKS : TK_PW_MINBLOCKS_BF16;
+};
 
 template <typename T>
 __device__ __forceinline__ T ld_stream(const T* p) {
@@ -156,7 +171,7 @@ clip_scale_kernel(const double* __restrict__ partials, int n, float max_norm,
 // ------------------------------------------------------------------ Tier 2
 // SCALE: 0 = no clipping, 1 = fold partials in every CTA, 2 = read scale_dev.
 template <int KIND, int PDT, int GDT, int SCALE>
-__global__ void __launch_bounds__(kThreads, TK_PW_MINBLOCKS)
+__global__ void __launch_bounds__(kThreads, (Tune<PDT, GDT>::minblocks))
 pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
                  const double* __restrict__ partials, int n_partials, float max_norm,
                  const float* __restrict__ scale_dev, float* __restrict__ scale_out,
@@ -191,6 +206,7 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
     const uint64_t a = q - L.q_begin, b = seg_end - L.q_begin;
     // quads [a, full_end) are whole and vector-accessible; the rest go scalar
     const uint64_t full_end = L.vec_ok ? min(b, L.n >> 2) : a;
+    constexpr int kUnroll = Tune<PDT, GDT>::unroll;
     for (uint64_t lq = a + threadIdx.x; lq < full_end; lq += kThreads * kUnroll) {
       float P[kUnroll][4], G[kUnroll][4], M[kUnroll][4], V[kUnroll][4];
       bool act[kUnroll];
@@ -217,8 +233,9 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         }
         const uint64_t e = (lq + (uint64_t)u * kThreads) * 4;
         store_quad<PDT>(L.p, e, P[u]);
-        for (int r = 0; r < peers.n; ++r)  // the updated parameters, into each peer's copy
-          store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, P[u]);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r)  // the updated parameters, into each peer's copy
+          if (r < peers.n) store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, P[u]);
         store_quad<TK_F32>(L.m, e, M[u]);
         if constexpr (KIND == TK_ADAMW) store_quad<TK_F32>(L.v, e, V[u]);
       }
@@ -234,7 +251,9 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         if constexpr (KIND == TK_ADAMW) v = L.v[e];
         apply<KIND>(p, g, m, v, k);
         store1<PDT>(L.p, e, p);
-        for (int r = 0; r < peers.n; ++r) store1<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, p);
+#pragma unroll
+        for (int r = 0; r < kMaxPeers; ++r)
+          if (r < peers.n) store1<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, p);
         L.m[e] = m;
         if constexpr (KIND == TK_ADAMW) L.v[e] = v;
       }
@@ -259,6 +278,7 @@ int occupancy_grid(uint64_t total_quads) {
   int sms = 0;
   if (pointwise_sms(&sms) != TK_OK) return 0;
   const int cap = sms * per_sm;
+  constexpr int kUnroll = Tune<PDT, GDT>::unroll;
   const uint64_t want = (total_quads + kThreads * kUnroll - 1) / (kThreads * kUnroll);
   if (TK_PW_OVERSUB) return (int)std::min<uint64_t>(want ? want : 1, 1u << 30);
   return (int)(want < (uint64_t)cap ? (want ? want : 1) : cap);
