@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tikun|reference]
                     [--workload gpt2-small-clip|flat-100m|muon-gpt2-d768|
                                 muon-1.3b-inbackward|muon-llama3-8b]
+                    [--zero auto|fused|copy|allgather]
 
 Default workload (the one the headline metric is quoted on at one GPU):
 clipped AdamW (global-norm clip 1.0) over the GPT-2-small PyTree, 148 fp32
@@ -13,23 +14,30 @@ N(0, 1e-2) (seeded synthetic data).
 One step = one full optimizer step over every leaf.  ``value`` is parameters
 updated per second with all buffers resident in HBM (p, g, m, v: 1.99 GB, well
 above the 126 MB L2, so no flush is needed between steps), timed with CUDA
-events on the launching stream; at N GPUs the step is ZeRO-1 (each rank
-updates its 1/N of the flat parameter space, f64 norm all-reduce, NCCL
-all-gather of the updated fp32 parameters) and the time is the max over ranks.
-``e2e`` is the same step through the C ABI with the leaves in pinned host
-memory (the reference engine's calling convention), copies included.
+events on the launching stream.  At N GPUs the step is ZeRO-1 through the C
+ABI (tk_shard_step): each rank updates its 1/N of the flat parameter space
+after an f64 norm all-reduce, and the updated fp32 parameters reach the other
+ranks by peer stores from the update kernel itself (``--zero fused``, the
+default), copies of finished chunks, or an NCCL all-gather; the time is the
+max over ranks.  ``e2e`` is the same step through the C ABI with the leaves
+in pinned host memory (the reference engine's calling convention), copies
+included: tk_step_buffers at one GPU, tk_step_buffers_sharded over each
+rank's slice at N.
 
 The Muon workloads (bf16 parameters and gradients, f32 momentum and AdamW
 moments; Muon with momentum 0.95, Nesterov, 5 Newton-Schulz steps, lr 0.02 on
 every hidden matrix; AdamW as above on embeddings and norms) report params/s
 and the Newton-Schulz tensor throughput (dense-equivalent FLOPs
 5(4m^2n + 2m^3) per matrix) against the measured bf16 peak.  At N GPUs the
-matrices are spread by FLOP-balanced bin-packing and the AdamW leaves by
-ZeRO-1; one all-gather per buffer reassembles the parameters.
+matrices are spread by FLOP-balanced bin-packing (MuonShard) and the AdamW
+leaves by ZeRO-1; finished matrices reach the other ranks through a copy
+kernel beside the next batch's tensor-core work (``--zero copy``, the default
+for Muon), the last GEMM's epilogue (``fused``) or all-gathers.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's
 restatement of tikun-cpu; the Rust engine cannot be built here) on this host's
-cores on the same workload.
+cores on the same workload; for the Muon workloads one matrix per shape group
+is timed and scaled by the group's count.
 """
 from __future__ import annotations
 
