@@ -1,0 +1,39 @@
+"""bench.py's workload definitions and CPU reference arms, on CPU: the
+configurations are the ones the headline metric and the parity cases name, and
+the reference arms run (on tiny stand-ins) and describe their sample."""
+import os
+import sys
+
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import bench  # noqa: E402
+from tikun_b200.sharding import ns_dense_flops  # noqa: E402
+
+
+def test_workload_shapes():
+    g = bench.WORKLOADS["gpt2-small-clip"]
+    assert len(g["sizes"]) == 148 and sum(g["sizes"]) == 124_439_808 and g["max_norm"] == 1.0
+    assert bench.WORKLOADS["flat-100m"]["sizes"] == [100_000_000]
+    m2 = bench.MUON["muon-gpt2-d768"]
+    assert len(m2["mats"]) == 72 and m2["adamw"][0] == 50257 * 768
+    assert abs(sum(ns_dense_flops(r, c) for r, c in m2["mats"]) / 1e12 - 1.631) < 0.01
+    m3 = bench.MUON["muon-1.3b-inbackward"]
+    assert m3["inbackward"] and m3["layers"] == 24 and len(m3["mats"]) == 24 * 6
+    m4 = bench.MUON["muon-llama3-8b"]
+    assert len(m4["mats"]) == 224 and m4["adamw"][:2] == [128256 * 4096] * 2
+    assert abs(sum(ns_dense_flops(r, c) for r, c in m4["mats"]) / 1e12 - 665.9) < 0.05
+
+
+def test_cpu_reference_arms_run_on_tiny_workloads():
+    tiny = dict(sizes=[1000, 17, 4097], kinds=["w", "b", "w"], max_norm=1.0, g_std=1e-2,
+                desc="tiny")
+    value, ms = bench.cpu_reference_run(tiny, 2, 1, 2)
+    assert value > 0 and ms > 0
+    muon = dict(mats=[(64, 96), (96, 64), (256, 512)], adamw=[300, 64], layers=1,
+                inbackward=False, desc="tiny muon")
+    value, ms, sample = bench.cpu_muon_run(muon, 2)
+    assert value > 0 and ms > 0 and "one matrix per shape group" in sample
+    assert "extrapolated" not in sample
+    # a budget below the largest matrix forces a scaled-down timing
+    value, ms, sample = bench.cpu_muon_run(muon, 2, budget_flops=1e7)
+    assert "timed at" in sample and "extrapolated by FLOP ratio" in sample
