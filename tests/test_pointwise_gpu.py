@@ -417,3 +417,52 @@ def test_checkpoint_resume_is_bit_identical():
     for x, y in zip(a, c):
         assert torch.equal(x, y)
     assert "sm_100a" in opt_c.to_json()
+
+
+def test_framework_agnostic_frontends_match_oracle():
+    """examples/test_framework_agnostic.py:12-84 with assertions: a nested dict
+    of NumPy arrays with grads passed to step (Lion), a bare NumPy array (SGD
+    with momentum) and raw (pointer, length) leaves (AdamW) step through the
+    host-buffer path and match the oracle bit for bit."""
+    import tikun_b200
+
+    def oracle_step(opt, ps, gs, m1, m2):
+        return oracle.step_two_tier(ps, gs, m1, m2, oracle.opt_kind(opt.algorithm), opt.lr,
+                                    opt.beta1, opt.beta2, opt.eps, opt.weight_decay,
+                                    opt.step_count, opt.max_norm)
+
+    rng = np.random.default_rng(9)
+    # nested dict, Lion, grads given to step()
+    params = {"encoder": {"w": np.ones((50, 50), np.float32), "b": np.zeros(50, np.float32)},
+              "decoder": {"w": np.ones((50, 10), np.float32)}}
+    leaves = [params["encoder"]["w"], params["encoder"]["b"], params["decoder"]["w"]]
+    ref = [x.copy() for x in leaves]
+    rm = [np.zeros(x.size, np.float32) for x in leaves]
+    opt = tikun_b200.Lion(params, lr=1e-4)
+    for _ in range(3):
+        grads = {"encoder": {"w": rng.standard_normal((50, 50)).astype(np.float32) * 0.1,
+                             "b": rng.standard_normal(50).astype(np.float32) * 0.05},
+                 "decoder": {"w": rng.standard_normal((50, 10)).astype(np.float32) * 0.2}}
+        opt.step(grads=grads)
+        g = [grads["encoder"]["w"], grads["encoder"]["b"], grads["decoder"]["w"]]
+        oracle_step(opt, [r.reshape(-1) for r in ref], [x.reshape(-1) for x in g], rm, None)
+    for a, b in zip(leaves, ref):
+        assert_bitexact(a, b, "dict/lion")
+    # bare NumPy array, SGD with momentum
+    p = np.ones(1000, np.float32)
+    rp, rm1 = p.copy(), np.zeros(1000, np.float32)
+    opt = tikun_b200.SGD(p, lr=0.01, momentum=0.9)
+    for _ in range(3):
+        g = rng.standard_normal(1000).astype(np.float32) * 0.05
+        opt.step(grads=g)
+        oracle_step(opt, [rp], [g], [rm1], None)
+    assert_bitexact(p, rp, "numpy/sgd")
+    # raw (pointer, length) leaves, AdamW
+    p = np.ones(500, np.float32)
+    rp, rm1, rm2 = p.copy(), np.zeros(500, np.float32), np.zeros(500, np.float32)
+    opt = tikun_b200.AdamW([(p.ctypes.data, 500)], lr=1e-3)
+    for _ in range(3):
+        g = rng.standard_normal(500).astype(np.float32) * 0.1
+        opt.step(grads=[(g.ctypes.data, 500)])
+        oracle_step(opt, [rp], [g], [rm1], [rm2])
+    assert_bitexact(p, rp, "raw/adamw")
