@@ -106,3 +106,27 @@ def test_pytree_flattening_order():
     assert flat[0] is a and flat[1] is b and flat[2] is c and flat[3] == (1234, 7)
     assert _extract_pointer_and_len(flat[3]) == (1234, 7)
     assert _extract_pointer_and_len(b) == (b.ctypes.data, 4)
+
+
+# -- arena: crates/tikun-core/src/arena.rs:120-133 ----------------------------
+def test_arena_leaf_views_alias_the_flat_buffer():
+    import torch
+
+    from tikun_b200.arena import Arena, LayoutPlan, shard_segments
+
+    plan = LayoutPlan([128, 256, 17])
+    a = Arena(plan, device="cpu")
+    a.leaf(0)[0] = 42.0
+    a.leaf(2)[16] = 7.0
+    assert a.leaf(0)[0].item() == 42.0
+    off2, _ = plan.slots[2]
+    assert a.flat[off2 + 16].item() == 7.0
+    # the padding between and after leaves stays zero-filled and belongs to no leaf
+    mask = torch.zeros(plan.total, dtype=torch.bool)
+    for off, n in plan.slots:
+        mask[off:off + n] = True
+    assert torch.count_nonzero(a.flat[~mask]) == 0
+    assert [p - a.flat.data_ptr() for p in a.ptrs()] == [off * 4 for off, _ in plan.slots]
+    assert plan.total % 16 == 0
+    pieces = shard_segments(plan, 0, plan.total)
+    assert pieces == [(i, 0, n) for i, n in enumerate(plan.sizes)]

@@ -6,6 +6,7 @@
   (python/tikun/muon.py:10-32) on seeded matrices.
 * The 4x4 identity polar test (crates/tikun-cpu/src/tensor_engine.rs:198-210).
 * LayoutPlan 64-byte alignment (crates/tikun-core/src/arena.rs:219-228).
+* One AdamW step lowers p and raises m and v (crates/tikun-cpu/src/jit.rs:128-152).
 """
 import os
 
@@ -110,3 +111,19 @@ def test_bf16_roundtrip_rne():
     back = oracle.bf16_to_f32(h)
     assert back[0] == 1.0 and back[1] == 1.0 and back[2] == 1.015625 and back[3] == -3.5
     assert np.isinf(back[5]) and np.signbit(back[6])
+
+
+def test_one_adamw_step_moves_p_down_and_moments_up():
+    # crates/tikun-cpu/src/jit.rs:128-152: 16 ones, grads 0.1, one AdamW step at
+    # lr 1e-3, betas 0.9/0.999, eps 1e-8, decay 0.01 -> p < 1, m > 0, v > 0.
+    p = np.ones(16, np.float32)
+    g = np.full(16, 0.1, np.float32)
+    m = np.zeros(16, np.float32)
+    v = np.zeros(16, np.float32)
+    s = oracle.step_two_tier([p], [g], [m], [v], oracle.ADAMW, 1e-3, 0.9, 0.999, 1e-8, 0.01,
+                             1, 0.0)
+    assert s == 1.0
+    assert np.all(p < 1.0) and np.all(m > 0.0) and np.all(v > 0.0)
+    # first step of bias-corrected AdamW: m_hat = g, v_hat = g^2, so the step is
+    # lr * (g / (|g| + eps) + decay * p) ~= 1e-3 * 1.01
+    assert np.allclose(1.0 - p, 1e-3 * 1.01, rtol=1e-4)
