@@ -130,3 +130,64 @@ def test_arena_leaf_views_alias_the_flat_buffer():
     assert plan.total % 16 == 0
     pieces = shard_segments(plan, 0, plan.total)
     assert pieces == [(i, 0, n) for i, n in enumerate(plan.sizes)]
+
+
+# -- argument checks that return before any CUDA call --------------------------
+def _err(status):
+    return status, _native.lib().tk_last_error().decode()
+
+
+def test_argument_checks_need_no_device():
+    import ctypes
+
+    L = _native.lib()
+    I64 = ctypes.c_int64
+    hp = _native.TkHParams(1e-3, 0.9, 0.999, 1e-8, 0.0)
+    mhp = _native.TkMuonHParams()
+    cases = [
+        (lambda: L.tk_newton_schulz_2d(None, -1, 4, 5, _native.TK_F32, _native.TK_NS_F16, None),
+         _native.TK_ERR_INVALID, "negative size"),
+        (lambda: L.tk_newton_schulz_2d(None, 4, 4, 5, 7, _native.TK_NS_F16, None),
+         _native.TK_ERR_INVALID, "not f32 or bf16"),
+        (lambda: L.tk_newton_schulz_3d(None, 2, 4, 4, 5, _native.TK_F32, 9, None),
+         _native.TK_ERR_INVALID, "unknown Newton-Schulz precision"),
+        (lambda: L.tk_apply_pointwise_peers(None, 0, _native.TK_ADAMW, ctypes.byref(hp), 1, None,
+                                            None, 8, None),
+         _native.TK_ERR_INVALID, "n_peers must be 0..7"),
+        (lambda: L.tk_apply_pointwise_peers(None, 0, _native.TK_ADAMW, ctypes.byref(hp), 1, None,
+                                            (I64 * 1)(8), 1, None),
+         _native.TK_ERR_INVALID, "not a multiple of 16 bytes"),
+        (lambda: L.tk_muon_step_peers(None, 0, ctypes.byref(mhp), (I64 * 1)(24), 1, None),
+         _native.TK_ERR_INVALID, "not a multiple of 16 bytes"),
+        (lambda: L.tk_muon_step_copy(None, 0, ctypes.byref(mhp), None, 2, None),
+         _native.TK_ERR_INVALID, "with a delta for each"),
+        (lambda: L.tk_set_reserved_sms(-1), _native.TK_ERR_INVALID, "out of range"),
+        (lambda: L.tk_set_update_events(ctypes.c_void_p(16), None),
+         _native.TK_ERR_INVALID, "set both events or neither"),
+        (lambda: L.tk_ipc_close(ctypes.c_void_p(4096)),
+         _native.TK_ERR_INVALID, "was not returned by tk_ipc_import"),
+        (lambda: L.tk_shard_init(None, None, None, 16, None, None, 0, _native.TK_ADAMW, 0, None,
+                                 ctypes.byref(ctypes.c_void_p())),
+         _native.TK_ERR_INVALID, "null communicator or arena"),
+        (lambda: L.tk_muon_shard_init(None, 0, None, None, None, _native.TK_BF16,
+                                      ctypes.byref(mhp), 0, None,
+                                      ctypes.byref(ctypes.c_void_p())),
+         _native.TK_ERR_INVALID, "null communicator"),
+        (lambda: L.tk_shard_step(None, ctypes.byref(hp), 1, 0.0, None, None),
+         _native.TK_ERR_INVALID, "null shard"),
+        (lambda: L.tk_nccl_comm_init(ctypes.c_void_p(16), 2, 2, ctypes.byref(ctypes.c_void_p())),
+         _native.TK_ERR_INVALID, "rank 2 of world 2"),
+        (lambda: L.tk_muon_layout(0, None, None, 0, None, None, None),
+         _native.TK_ERR_INVALID, "world 0"),
+    ]
+    for call, code, text in cases:
+        status, msg = _err(call())
+        assert status == code and text in msg, (status, msg, text)
+        # the next successful call clears the message
+        assert _err(L.tk_newton_schulz_2d(None, 0, 0, 5, _native.TK_F32, _native.TK_NS_F16,
+                                          None)) == (0, "")
+    # releasing nothing succeeds
+    assert L.tk_shard_destroy(None, None) == 0
+    assert L.tk_muon_shard_destroy(None, None) == 0
+    assert L.tk_nccl_comm_destroy(None) == 0
+    assert L.tk_set_reserved_sms(0) == 0

@@ -557,6 +557,19 @@ static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const 
   const size_t slot_bytes = arr_bytes * arrays;
   Scratch sc;
   TK_TRY(sc.alloc(256 + gbytes + slot_bytes * HostPipe::kSlots, s));
+  // On an early return the scratch goes back to the pool in s's order while
+  // copies on the side streams may still use it: s first waits for both.
+  // (Destroyed before sc; disarmed once s has joined them on the normal path.)
+  struct JoinSideStreams {
+    HostPipe* P;
+    cudaStream_t s;
+    bool armed = true;
+    ~JoinSideStreams() {
+      if (!armed) return;
+      if (cudaEventRecord(P->g_ready, P->h2d) == cudaSuccess) cudaStreamWaitEvent(s, P->g_ready, 0);
+      if (cudaEventRecord(P->end, P->d2h) == cudaSuccess) cudaStreamWaitEvent(s, P->end, 0);
+    }
+  } join_guard{P, s};
   char* base = static_cast<char*>(sc.get());
   float* scale_dev = reinterpret_cast<float*>(base);
   char* gdev = base + 256;
@@ -643,6 +656,7 @@ static int step_host_pipelined(const tk_leaf* leaves, size_t n, int kind, const 
   // the caller's stream (and the scratch it frees) waits for the last copies
   TK_CUDA_TRY(cudaEventRecord(P->end, P->d2h));
   TK_CUDA_TRY(cudaStreamWaitEvent(s, P->end, 0));
+  join_guard.armed = false;
   float scale = 1.0f;
   if (clip) TK_CUDA_TRY(cudaMemcpyAsync(&scale, scale_dev, 4, cudaMemcpyDeviceToHost, s));
   TK_CUDA_TRY(cudaStreamSynchronize(s));

@@ -17,8 +17,9 @@ namespace ns {
 constexpr int kMaxBatch = 256;
 
 // Scratch layout of one batch of matrices that are all m x n or n x m
-// (m <= n): X is m x n, X^T is n x m, A and B are m x m, all half precision
-// with rows padded to a multiple of 64 elements.
+// (m <= n): X is m x n, two X^T buffers (ping-pong) are n x m, and A, A' and
+// B are m x m, all half precision with rows padded to a multiple of 64
+// elements.
 struct GroupLayout {
   int64_t m, n, batch;
   int64_t ldx, ldm;

@@ -257,6 +257,7 @@ extern "C" {
 
 int tk_newton_schulz_2d(void* matrix, int64_t rows, int64_t cols, int32_t steps, int32_t dtype,
                         int32_t precision, void* stream) {
+  clear_error();
   return ns_entry(matrix, 1, rows, cols, steps, dtype, precision,
                   static_cast<cudaStream_t>(stream));
 }
@@ -264,6 +265,7 @@ int tk_newton_schulz_2d(void* matrix, int64_t rows, int64_t cols, int32_t steps,
 int tk_newton_schulz_3d(void* tensor, int64_t num_heads, int64_t head_dim_out,
                         int64_t head_dim_in, int32_t steps, int32_t dtype, int32_t precision,
                         void* stream) {
+  clear_error();
   return ns_entry(tensor, num_heads, head_dim_out, head_dim_in, steps, dtype, precision,
                   static_cast<cudaStream_t>(stream));
 }
@@ -398,11 +400,13 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
 
 int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
                  void* stream) {
+  clear_error();
   return muon_step(leaves, n_leaves, hp, nullptr, nullptr, stream);
 }
 
 int tk_muon_step_peers(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
                        const int64_t* peer_deltas, int n_peers, void* stream) {
+  clear_error();
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
     return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
   for (int i = 0; i < n_peers; ++i)  // vector stores into the peers keep their alignment
@@ -418,6 +422,7 @@ int tk_muon_step_peers(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muo
 
 static int muon_step_copy(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_hparams* hp,
                           const int64_t* peer_deltas, int n_peers, bool join, void* stream) {
+  clear_error();
   if (n_peers < 0 || n_peers > kMaxPeers || (n_peers > 0 && peer_deltas == nullptr))
     return set_error(TK_ERR_INVALID, "n_peers must be 0..%d with a delta for each", kMaxPeers);
   for (int i = 0; i < n_peers; ++i)  // vector stores into the peers keep their alignment
@@ -452,6 +457,7 @@ int tk_muon_step_copy_deferred(const tk_muon_leaf* leaves, size_t n_leaves,
 }
 
 int tk_muon_copy_join(void* stream) {
+  clear_error();
   PeerCopy copy;
   TK_TRY(peer_copy_streams(&copy));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -463,6 +469,7 @@ int tk_muon_copy_join(void* stream) {
 }
 
 int tk_device_status(int* status_out) {
+  clear_error();
   if (status_out == nullptr) return set_error(TK_ERR_INVALID, "status_out is NULL");
   int* status = nullptr;
   TK_TRY(device_status_word(&status));
@@ -474,6 +481,7 @@ int tk_device_status(int* status_out) {
 
 int tk_testing_gemm_tn(const void* P, const void* Q, void* D, int batch, int M, int N, int K,
                        int64_t ldp, int64_t ldq, int64_t ldd, float alpha, int fmt, void* stream) {
+  clear_error();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = nullptr;
   TK_TRY(device_status_word(&status));
@@ -484,6 +492,7 @@ int tk_testing_gemm_tn(const void* P, const void* Q, void* D, int batch, int M, 
 }
 
 int tk_testing_bounded_wait(int limit_ms, void* stream) {
+  clear_error();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* status = nullptr;
   TK_TRY(device_status_word(&status));

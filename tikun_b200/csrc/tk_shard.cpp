@@ -25,6 +25,7 @@
 #include <algorithm>
 #include <cstring>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "tk_internal.h"
@@ -167,7 +168,10 @@ int tk_nccl_comm_destroy(void* comm) {
   return TK_OK;
 }
 
+// Both free functions keep the thread's error message: they run on failure
+// paths, and closing a peer mapping through the public entry point clears it.
 static void shard_free(tk_shard* sh) {
+  const std::string err = tk_last_error();
   for (cudaEvent_t e : sh->chunk_done) cudaEventDestroy(e);
   for (cudaEvent_t e : sh->peer_done) cudaEventDestroy(e);
   for (cudaStream_t q : sh->peer_streams) cudaStreamDestroy(q);
@@ -176,6 +180,7 @@ static void shard_free(tk_shard* sh) {
   if (sh->v) cudaFree(sh->v);
   if (sh->sumsq) cudaFree(sh->sumsq);
   delete sh;
+  if (!err.empty()) set_error(TK_OK, "%s", err.c_str());
 }
 
 int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_t n_elems,
@@ -543,10 +548,12 @@ int tk_muon_layout(size_t n_mats, const int64_t* rows, const int64_t* cols, int 
 }
 
 static void muon_shard_free(tk_muon_shard* sh) {
+  const std::string err = tk_last_error();
   for (void* p : sh->peer_ptrs) tk_ipc_close(p);
   if (sh->mom) cudaFree(sh->mom);
   if (sh->barrier) cudaFree(sh->barrier);
   delete sh;
+  if (!err.empty()) set_error(TK_OK, "%s", err.c_str());
 }
 
 int tk_muon_shard_init(void* nccl_comm, size_t n_mats, const int64_t* rows, const int64_t* cols,
