@@ -55,6 +55,15 @@ def pieces_to_segments(plan: LayoutPlan, lo: int, hi: int) -> list[tuple[int, in
     return out
 
 
+def _close_mappings(ptrs: list[int]) -> None:
+    """Unmaps what a failed set-up had already mapped (best effort: the
+    set-up's own error is the one raised)."""
+    L = _native.lib()
+    for p in ptrs:
+        L.tk_ipc_close(ctypes.c_void_p(p))
+    ptrs.clear()
+
+
 @dataclass
 class ZeroHParams:
     lr: float = 1e-3
@@ -125,16 +134,20 @@ class ZeroPointwise:
         everyone = [None] * self.world
         dist.all_gather_object(everyone, mine, group=self.group)
         deltas = []
-        for r, (h, o, total) in enumerate(everyone):
-            if total != self.plan.total:
-                raise ValueError(f"rank {r} has an arena of {total} elements, "
-                                 f"this rank {self.plan.total}")
-            if r == self.rank:
-                continue
-            ptr = ctypes.c_void_p()
-            _native.check(L.tk_ipc_import(h, o, ctypes.byref(ptr)))
-            self.peer_ptrs.append(ptr.value)
-            deltas.append(ptr.value - self.p.data_ptr())
+        try:
+            for r, (h, o, total) in enumerate(everyone):
+                if total != self.plan.total:
+                    raise ValueError(f"rank {r} has an arena of {total} elements, "
+                                     f"this rank {self.plan.total}")
+                if r == self.rank:
+                    continue
+                ptr = ctypes.c_void_p()
+                _native.check(L.tk_ipc_import(h, o, ctypes.byref(ptr)))
+                self.peer_ptrs.append(ptr.value)
+                deltas.append(ptr.value - self.p.data_ptr())
+        except Exception:
+            _close_mappings(self.peer_ptrs)
+            raise
         self.peer_deltas = (ctypes.c_int64 * max(len(deltas), 1))(*deltas)
         self.barrier_buf = torch.zeros(1, dtype=torch.float64, device=self.p.device)
 
@@ -344,15 +357,19 @@ class PeerArena:
         everyone = [None] * world
         dist.all_gather_object(everyone, mine, group=group)
         deltas = []
-        for r, (h, o, nbytes) in enumerate(everyone):
-            if nbytes != mine[2]:
-                raise ValueError(f"rank {r} shares {nbytes} bytes, this rank {mine[2]}")
-            if r == rank:
-                continue
-            ptr = ctypes.c_void_p()
-            _native.check(L.tk_ipc_import(h, o, ctypes.byref(ptr)))
-            self.ptrs.append(ptr.value)
-            deltas.append(ptr.value - t.data_ptr())
+        try:
+            for r, (h, o, nbytes) in enumerate(everyone):
+                if nbytes != mine[2]:
+                    raise ValueError(f"rank {r} shares {nbytes} bytes, this rank {mine[2]}")
+                if r == rank:
+                    continue
+                ptr = ctypes.c_void_p()
+                _native.check(L.tk_ipc_import(h, o, ctypes.byref(ptr)))
+                self.ptrs.append(ptr.value)
+                deltas.append(ptr.value - t.data_ptr())
+        except Exception:
+            _close_mappings(self.ptrs)
+            raise
         self.n = len(deltas)
         self.deltas = (ctypes.c_int64 * max(self.n, 1))(*deltas)
 
