@@ -301,3 +301,31 @@ def test_liveness_reports_a_rank_that_left_between_steps():
             p.kill()
     assert res[1] == [1]
     assert res[0][:1] == [1] and "rank(s) [1] did not reach step 2" in res[0][1], res[0]
+
+
+def test_muon_shard_checks_gradients_before_announcing_the_step():
+    # world 1 without a process group: the shard's host side runs on the CPU
+    # and every check fires before the (CUDA) step would be enqueued
+    from tikun_b200.distributed import MuonShard
+
+    class Beats:
+        def __init__(self):
+            self.steps = []
+
+        def step(self, k):
+            self.steps.append(k)
+
+    sh = MuonShard([(8, 16), (16, 8)], torch.float32, "cpu", lr=0.02)
+    sh.liveness = Beats()
+    good = [torch.zeros(8, 16), torch.zeros(16, 8)]
+    bad_dtype = [torch.zeros(8, 16, dtype=torch.float16), good[1]]
+    bad_shape = [torch.zeros(8, 15), good[1]]
+    strided = [torch.zeros(16, 8).t(), good[1]]
+    for grads, text in ((bad_dtype, "float32 or bfloat16"), (bad_shape, "contiguous 8x16"),
+                        (strided, "contiguous 8x16")):
+        with pytest.raises(ValueError, match=text):
+            sh.step(grads)
+        with pytest.raises(ValueError, match=text):
+            sh.step_part([0, 1], grads)
+    assert sh.step_count == 0 and sh.liveness.steps == []
+    assert sh._leaves(sh.mine, good)[0].rows == 8

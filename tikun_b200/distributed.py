@@ -384,6 +384,18 @@ class PeerArena:
             self.ptrs = []
 
 
+_MUON_DTYPES = {torch.float32: _native.TK_F32, torch.bfloat16: _native.TK_BF16}
+
+
+def _check_grad(grads, i: int, r: int, c: int) -> torch.Tensor:
+    g = grads[i]
+    if g.numel() != r * c or not g.is_contiguous():
+        raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
+    if g.dtype not in _MUON_DTYPES:
+        raise ValueError(f"gradient {i} is {g.dtype}; Muon gradients are float32 or bfloat16")
+    return g
+
+
 class MuonShard:
     """Muon over matrices split across ranks (one process per GPU).
 
@@ -439,22 +451,15 @@ class MuonShard:
         """``grads[i]`` (device tensors, any of f32/bf16, contiguous) for the
         rank's own matrices ``self.mine``; others are not read.  Enqueued on
         the current stream.  ``events`` (two CUDA events) are recorded just
-        around the Newton-Schulz launches."""
+        around the Newton-Schulz launches.  The gradients are checked before
+        the step is announced, so a bad argument surfaces on the other ranks as
+        a missing heartbeat, not as a collective left waiting."""
+        arr = self._leaves(self.mine, grads)
         self.step_count += 1
         if self.liveness is not None:
             self.liveness.step(self.step_count)
         L = _native.lib()
         s = torch.cuda.current_stream(self.device).cuda_stream
-        gdt = {torch.float32: _native.TK_F32, torch.bfloat16: _native.TK_BF16}
-        pdt = gdt[self.dtype]
-        arr = (_native.TkMuonLeaf * max(len(self.mine), 1))()
-        for k, i in enumerate(self.mine):
-            r, c = self.shapes[i]
-            g = grads[i]
-            if g.numel() != r * c or not g.is_contiguous():
-                raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
-            arr[k] = _native.TkMuonLeaf(self.param(i).data_ptr(), g.data_ptr(),
-                                        self.momentum[i].data_ptr(), 1, r, c, pdt, gdt[g.dtype])
         if self.exchange in ("peers", "copy"):
             # the peers are done reading this step's destination ranges
             dist.all_reduce(self.barrier_buf, group=self.group)
@@ -479,16 +484,14 @@ class MuonShard:
 
     # -- a step issued in parts (e.g. a layer at a time during backward) --
     def _leaves(self, idx, grads):
-        gdt = {torch.float32: _native.TK_F32, torch.bfloat16: _native.TK_BF16}
-        pdt = gdt[self.dtype]
+        pdt = _MUON_DTYPES[self.dtype]
         arr = (_native.TkMuonLeaf * max(len(idx), 1))()
         for k, i in enumerate(idx):
             r, c = self.shapes[i]
-            g = grads[i]
-            if g.numel() != r * c or not g.is_contiguous():
-                raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
+            g = _check_grad(grads, i, r, c)
             arr[k] = _native.TkMuonLeaf(self.param(i).data_ptr(), g.data_ptr(),
-                                        self.momentum[i].data_ptr(), 1, r, c, pdt, gdt[g.dtype])
+                                        self.momentum[i].data_ptr(), 1, r, c, pdt,
+                                        _MUON_DTYPES[g.dtype])
         return arr
 
     def step_begin(self, stream=None) -> None:
@@ -506,9 +509,9 @@ class MuonShard:
         mine = [i for i in idx if self.owner[i] == self.rank]
         if not mine:
             return
+        arr = self._leaves(mine, grads)
         L = _native.lib()
         s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
-        arr = self._leaves(mine, grads)
         if self.exchange == "peers":
             _native.check(L.tk_muon_step_peers(arr, len(mine), ctypes.byref(self.hp),
                                                self.peers.deltas, self.peers.n, s))
@@ -584,22 +587,21 @@ class NativeMuonShard:
 
     def step(self, grads) -> None:
         """``grads[i]``: contiguous device tensors of one dtype (f32 or bf16)
-        for the rank's own matrices; enqueued on the current stream."""
-        self.step_count += 1
-        if self.liveness is not None:
-            self.liveness.step(self.step_count)
+        for the rank's own matrices; enqueued on the current stream.  Checked
+        before the step is announced (see MuonShard.step)."""
         ptrs = (ctypes.c_void_p * max(self._n, 1))()
         gdt = None
         for i in self.mine:
-            g = grads[i]
             r, c = self.shapes[i]
-            if g.numel() != r * c or not g.is_contiguous():
-                raise ValueError(f"gradient {i} must be a contiguous {r}x{c} tensor")
-            d = _native.TK_F32 if g.dtype == torch.float32 else _native.TK_BF16
+            g = _check_grad(grads, i, r, c)
+            d = _MUON_DTYPES[g.dtype]
             if gdt is not None and d != gdt:
                 raise ValueError("all gradients of a step share one dtype")
             gdt = d
             ptrs[i] = g.data_ptr()
+        self.step_count += 1
+        if self.liveness is not None:
+            self.liveness.step(self.step_count)
         s = torch.cuda.current_stream(self.device).cuda_stream
         _native.check(_native.lib().tk_muon_shard_step(
             self.handle, ptrs, _native.TK_F32 if gdt is None else gdt, s))
