@@ -163,7 +163,8 @@ TK_API int tk_step_buffers_noalloc(const tk_leaf* leaves, size_t n_leaves, int32
 
 /* The pieces of the step, for callers that shard it (ZeRO-1 over ranks):
  *   tk_grad_sumsq       sum over the leaves of g*g in f64 -> *sumsq_dev
- *   tk_clip_scale       *scale_dev = clip scale of *sumsq_dev (lib.rs:117-122)
+ *   tk_clip_scale       *scale_dev = clip scale of *sumsq_dev
+ *                       (crates/tikun-cpu/src/lib.rs:117-122)
  *   tk_apply_pointwise  Tier 2 over the leaves with the scale at scale_dev
  *                       (NULL: no clipping)
  * The caller may all-reduce *sumsq_dev between the first two. */

@@ -125,7 +125,7 @@ void tko_pointwise_leaf(const tko_leaf* leaf, int32_t kind, const tko_hparams* h
     }
     return;
   }
-  /* AdamW: lib.rs:152-154 then :258-270 */
+  /* AdamW: crates/tikun-cpu/src/lib.rs:152-154 then :258-270 */
   const float lr = hp->lr, b1 = hp->beta1, b2 = hp->beta2, eps = hp->eps, decay = hp->decay;
   int32_t step_val = (int32_t)(step < 1 ? 1 : step);
   float bias_corr1 = 1.0f - tko_powi(b1, step_val);

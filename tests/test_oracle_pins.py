@@ -5,7 +5,7 @@
 * Newton-Schulz against the reference's torch restatement
   (python/tikun/muon.py:10-32) on seeded matrices.
 * The 4x4 identity polar test (crates/tikun-cpu/src/tensor_engine.rs:198-210).
-* LayoutPlan 64-byte alignment (crates/tikun-core/src/arena.rs:219-228).
+* LayoutPlan 64-byte alignment (crates/tikun-core/src/arena.rs:109-118).
 * One AdamW step lowers p and raises m and v (crates/tikun-cpu/src/jit.rs:128-152).
 """
 import os
@@ -97,7 +97,7 @@ def test_layout_alignment():
 
 
 def test_clip_scale_rule():
-    # lib.rs:117-122: scale only when the norm exceeds max_norm > 0
+    # crates/tikun-cpu/src/lib.rs:117-122: scale only when the norm exceeds max_norm > 0
     assert oracle.clip_scale(4.0, 1.0) == np.float32(1.0) / (np.float32(2.0) + np.float32(1e-6))
     assert oracle.clip_scale(0.25, 1.0) == 1.0
     assert oracle.clip_scale(4.0, 0.0) == 1.0

@@ -21,7 +21,7 @@ _SMS = 148
 _LEAVES_PER_LAUNCH = 224  # kMaxLeavesPerLaunch: leaf table in kernel parameters
 _UPDATE_CTAS_PER_SM = 2   # pointwise_kernel: 256 threads, 2 resident CTAs per SM
 
-# the reference's fast-path schedule (tikun-py/src/lib.rs:47-49)
+# the reference's fast-path schedule (tikun-py/src/lib.rs:48-51)
 _NODES = [("Load", "load_p_g", 16), ("Compute", "fma_update", 16), ("Store", "store_p", 16)]
 
 # algorithmic bytes per parameter of one Tier-2 pass, f32 p and g
@@ -30,7 +30,7 @@ _FLOPS = {"AdamW": 14, "Lion": 8, "SGD": 5}
 
 
 def _algorithm(name: str) -> str:
-    # build_spec (tikun-py/src/lib.rs:51-55): "lion", "sgd", anything else AdamW
+    # build_spec (tikun-py/src/lib.rs:56-60): "lion", "sgd", anything else AdamW
     return {"lion": "Lion", "sgd": "SGD"}.get(name.lower(), "AdamW")
 
 

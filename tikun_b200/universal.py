@@ -1,6 +1,6 @@
 """Framework-agnostic pointwise optimizer front-end on the B200 engine.
 
-Mirrors the reference's ``UniversalOptimizer`` (python/tikun/universal.py:87-223):
+Mirrors the reference's ``UniversalOptimizer`` (python/tikun/universal.py:61-225):
 same constructor arguments, PyTree flattening (dict values in insertion order,
 lists, tuples, iterables, ``(ptr, len)`` pairs), per-parameter first/second
 moment state keyed by the parameter's address, a step counter incremented at
@@ -26,7 +26,7 @@ from . import _native
 
 
 def _extract_pointer_and_len(tensor) -> tuple[int, int]:
-    """universal.py:48-61."""
+    """universal.py:22-35."""
     if hasattr(tensor, "data_ptr") and hasattr(tensor, "numel"):
         return tensor.data_ptr(), tensor.numel()
     if isinstance(tensor, np.ndarray):
@@ -40,7 +40,7 @@ def _extract_pointer_and_len(tensor) -> tuple[int, int]:
 
 
 def _flatten_pytree(container) -> list:
-    """universal.py:63-85."""
+    """universal.py:37-59."""
     if isinstance(container, dict):
         items = []
         for v in container.values():
@@ -79,7 +79,7 @@ def _is_cuda(t) -> bool:
 
 
 class UniversalOptimizer:
-    """See the module docstring; arguments as python/tikun/universal.py:93-104."""
+    """See the module docstring; arguments as python/tikun/universal.py:67-78."""
 
     def __init__(self, params, algorithm: str = "adamw", lr: float = 1e-3, beta1: float = 0.9,
                  beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.01,
@@ -147,7 +147,7 @@ class UniversalOptimizer:
         return _hook
 
     def _step_single_tensor(self, p):
-        """universal.py:138-163: one leaf, with step max(1, step_count) —
+        """universal.py:112-137: one leaf, with step max(1, step_count) —
         the count is read before step() increments it, so the first two
         backward passes both use step 1, exactly as the reference does."""
         p_ptr, length = _extract_pointer_and_len(p)
@@ -158,7 +158,7 @@ class UniversalOptimizer:
 
     # -- step ----------------------------------------------------------------
     def step(self, grads=None):
-        """universal.py:165-218."""
+        """universal.py:139-192."""
         self.step_count += 1
         if self.in_backward:
             return
