@@ -179,6 +179,8 @@ def test_argument_checks_need_no_device():
          _native.TK_ERR_INVALID, "rank 2 of world 2"),
         (lambda: L.tk_muon_layout(0, None, None, 0, None, None, None),
          _native.TK_ERR_INVALID, "world 0"),
+        (lambda: L.tk_step_buffers_noalloc(None, 0, _native.TK_ADAMW, None, 1, 0.0, None, None),
+         _native.TK_ERR_INVALID, "hparams is NULL"),
     ]
     for call, code, text in cases:
         status, msg = _err(call())

@@ -140,6 +140,7 @@ using namespace tk;
 extern "C" int tk_step_buffers_noalloc(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
                                        const tk_hparams* hp, uint64_t step, float max_norm,
                                        float* clip_scale_out, void* stream) {
+  clear_error();
   if (hp == nullptr) return set_error(TK_ERR_INVALID, "hparams is NULL");
   TK_TRY(validate(leaves, n_leaves, kind));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
