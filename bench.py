@@ -36,8 +36,9 @@ for Muon), the last GEMM's epilogue (``fused``) or all-gathers.
 
 ``--impl reference`` times the reference's CPU algorithm (the oracle's
 restatement of tikun-cpu; the Rust engine cannot be built here) on this host's
-cores on the same workload; for the Muon workloads one matrix per shape group
-is timed and scaled by the group's count.
+cores on the same workload: the requested --steps after --warmup, cut only
+where they would run past two minutes each; for the Muon workloads one matrix
+per shape group is timed and scaled by the group's count.
 """
 from __future__ import annotations
 
@@ -170,35 +171,53 @@ def make_host_state(wl, seed=1234):
     return p, g
 
 
-def cpu_reference_run(wl, steps, warmup, nthreads):
+def cpu_reference_run(wl, steps, warmup, nthreads, budget_s=None):
     """The oracle (tikun-cpu's algorithm, restated) on host cores, threads over
-    leaves as tikun-cpu's rayon par_iter over leaves."""
+    leaves as tikun-cpu's rayon par_iter over leaves.
+
+    Returns (params/s, ms/step, warm-up steps run, steps timed).  With
+    ``budget_s`` the warm-up stops and the timed steps are cut once the
+    measured step time says they would run past that many seconds each."""
     import oracle
 
     p, g = make_host_state(wl)
     m = [np.zeros_like(x) for x in p]
     v = [np.zeros_like(x) for x in p]
-    for s in range(warmup):
+
+    def one(s):
         oracle.step_two_tier(p, g, m, v, oracle.ADAMW, HP["lr"], HP["b1"], HP["b2"], HP["eps"],
-                             HP["decay"], s + 1, wl["max_norm"], nthreads)
+                             HP["decay"], s, wl["max_norm"], nthreads)
+
+    warm, t_step = 0, 0.0
+    for s in range(max(1, warmup)):
+        t0 = time.perf_counter()
+        one(s + 1)
+        t_step = time.perf_counter() - t0
+        warm += 1
+        if budget_s is not None and t_step * (s + 2) > budget_s:
+            break
+    if budget_s is not None:
+        steps = max(1, min(steps, int(budget_s / max(t_step, 1e-9))))
     t0 = time.perf_counter()
     for s in range(steps):
-        oracle.step_two_tier(p, g, m, v, oracle.ADAMW, HP["lr"], HP["b1"], HP["b2"], HP["eps"],
-                             HP["decay"], warmup + s + 1, wl["max_norm"], nthreads)
+        one(warm + s + 1)
     dt = time.perf_counter() - t0
-    return sum(wl["sizes"]) * steps / dt, dt / steps * 1e3
+    return sum(wl["sizes"]) * steps / dt, dt / steps * 1e3, warm, steps
 
 
 def run_reference(args, wl, rank):
     if rank != 0:
         return
     nthreads = os.cpu_count() or 1
-    # bounded: at most 10 timed steps of the full workload (about 1 s each)
-    steps = max(1, min(args.steps, 10))
-    warm = max(1, min(args.warmup, 3))
-    value, ms = cpu_reference_run(wl, steps, warm, nthreads)
+    # the requested --steps K after --warmup W; bounded so that each phase
+    # stays within two minutes on a slow host (the step is about 0.15 s on a
+    # B200 box's host cores)
+    value, ms, warm, steps = cpu_reference_run(wl, args.steps, args.warmup, nthreads,
+                                               budget_s=120.0)
     sample = (f"full workload ({sum(wl['sizes']):,} params), {steps} timed steps after {warm} "
               f"warm-up, {nthreads} threads over leaves")
+    if (steps, warm) != (args.steps, args.warmup):
+        sample += f" (cut from {args.steps} / {args.warmup} to stay within the time bound)"
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "params/s",
         "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": ms,
@@ -472,7 +491,7 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
     cpu = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
         nthreads = os.cpu_count() or 1
-        cval, cms = cpu_reference_run(wl, 2, 1, nthreads)
+        cval, cms, _, _ = cpu_reference_run(wl, 2, 1, nthreads)
         cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
                "sample": f"full workload, 2 timed steps after 1 warm-up, {nthreads} threads over "
                          f"leaves ({cms:.0f} ms/step)"}

@@ -27,8 +27,11 @@ def test_workload_shapes():
 def test_cpu_reference_arms_run_on_tiny_workloads():
     tiny = dict(sizes=[1000, 17, 4097], kinds=["w", "b", "w"], max_norm=1.0, g_std=1e-2,
                 desc="tiny")
-    value, ms = bench.cpu_reference_run(tiny, 2, 1, 2)
-    assert value > 0 and ms > 0
+    value, ms, warm, steps = bench.cpu_reference_run(tiny, 2, 1, 2)
+    assert value > 0 and ms > 0 and (warm, steps) == (1, 2)
+    # a time budget far below one step cuts both phases to one step
+    value, ms, warm, steps = bench.cpu_reference_run(tiny, 50, 5, 2, budget_s=1e-9)
+    assert (warm, steps) == (1, 1)
     muon = dict(mats=[(64, 96), (96, 64), (256, 512)], adamw=[300, 64], layers=1,
                 inbackward=False, desc="tiny muon")
     value, ms, sample = bench.cpu_muon_run(muon, 2)
