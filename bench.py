@@ -491,10 +491,11 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
     cpu = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
         nthreads = os.cpu_count() or 1
-        cval, cms, _, _ = cpu_reference_run(wl, 2, 1, nthreads)
+        # a bounded sample: as many full steps as fit in about 10 s of host time
+        cval, cms, cwarm, csteps = cpu_reference_run(wl, 100, 3, nthreads, budget_s=10.0)
         cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
-               "sample": f"full workload, 2 timed steps after 1 warm-up, {nthreads} threads over "
-                         f"leaves ({cms:.0f} ms/step)"}
+               "sample": f"full workload, {csteps} timed steps after {cwarm} warm-up (about "
+                         f"10 s), {nthreads} threads over leaves ({cms:.0f} ms/step)"}
     res = {
         "value": value, "ms_per_step": ms_step, "dtype": "f32", "scaling": "strong",
         "data": "synthetic (seeded N(0,0.02) params, N(0,%g) grads held fixed across steps)"
