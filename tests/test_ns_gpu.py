@@ -59,8 +59,15 @@ def test_gemm_tn_matches_torch(B, M, N, K, fmt, dt):
 
 
 # -- Newton-Schulz ---------------------------------------------------------
+# vectors (one row or one column) and 1 x 1 included: a 2-D parameter may have
+# either extent 1.  For them X X^T is one scalar and every iteration scales X by
+# a + B, a difference of two numbers near 3.4 and 2.7: the 16-bit rounding of B
+# moves all elements alike instead of averaging out over m^2 entries, so they
+# are held to the Newton-Schulz bar of 2e-2 (an emulation of the kernel's
+# rounding points gives up to 3.6e-3 with f16 operands and 1.7e-2 with bf16).
+VECTOR_NS_TOL = 2e-2
 SHAPES = [(64, 96), (96, 64), (128, 128), (17, 45), (200, 32), (768, 768), (768, 3072),
-          (3072, 768), (1000, 1500)]
+          (3072, 768), (1000, 1500), (1, 300), (300, 1), (1, 1)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
@@ -72,7 +79,9 @@ def test_ns_2d_matches_oracle(shape, prec):
     ref = oracle.polar_step_np(x, 5)
     t = torch.from_numpy(x.copy()).cuda()
     _native.newton_schulz_2d_ffi(t.data_ptr(), r, c, 5, precision=prec)
-    assert relf(to_np(t), ref) <= NS_TOL[prec]
+    err = relf(to_np(t), ref)
+    print(f"{r}x{c} relative Frobenius error {err:.3e}")
+    assert err <= (NS_TOL[prec] if min(r, c) > 1 else VECTOR_NS_TOL)
 
 
 @pytest.mark.parametrize("prec", PRECISIONS)
@@ -169,7 +178,7 @@ def _muon_oracle_step(p, buf, g, lr, mu, rows, cols, heads, p_bf16):
 
 
 @pytest.mark.parametrize("rows,cols,heads", [(768, 768, 1), (768, 3072, 1), (3072, 768, 1),
-                                             (96, 40, 1), (16, 24, 3)])
+                                             (96, 40, 1), (16, 24, 3), (1, 512, 1)])
 @pytest.mark.parametrize("p_bf16", [False, True], ids=["p_f32", "p_bf16"])
 def test_muon_step_ten_steps(rows, cols, heads, p_bf16):
     shape = (heads, rows, cols) if heads > 1 else (rows, cols)
@@ -197,7 +206,9 @@ def test_muon_step_ten_steps(rows, cols, heads, p_bf16):
             alpha = -lr * oracle.muon_update_scale(rows, cols)
             upd = ((p.float() - prev) / alpha).cpu().numpy()
             if not p_bf16:
-                assert relf(upd, o_ref) <= 5e-3
+                err0 = relf(upd, o_ref)
+                print(f"first update relative Frobenius error {err0:.3e}")
+                assert err0 <= (5e-3 if min(rows, cols) > 1 else VECTOR_NS_TOL)
     assert_bitexact(to_np(mom), buf_ref, "momentum after 10 steps")
     assert _native.device_status() == 0
     got = p.float().cpu().numpy()
