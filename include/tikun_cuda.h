@@ -375,6 +375,25 @@ TK_API int tk_nccl_unique_id(void* id_out);
 TK_API int tk_nccl_comm_init(const void* id, int world, int rank, void** comm_out);
 TK_API int tk_nccl_comm_destroy(void* comm);
 
+/* Failure detection for a communicator (no reference counterpart: the
+ * reference is single-process).
+ *   tk_nccl_comm_async_error  *result_out = the communicator's asynchronous
+ *                             error (an ncclResult_t; 0 = none)
+ *   tk_nccl_comm_abort        ncclCommAbort: ends its collectives, including
+ *                             kernels waiting for a peer that is gone, and
+ *                             releases it (use instead of _destroy)
+ *   tk_stream_wait_deadline   waits on the host for the work on `stream`,
+ *                             at most timeout_ms, polling the communicator's
+ *                             asynchronous error when `comm` is given; on an
+ *                             error or at the deadline it aborts `comm` (if
+ *                             given) and returns TK_ERR_DEVICE.  Results of
+ *                             that step are then not valid.  Give only a
+ *                             communicator this caller owns (PyTorch aborts
+ *                             its own through its watchdog). */
+TK_API int tk_nccl_comm_async_error(void* comm, int32_t* result_out);
+TK_API int tk_nccl_comm_abort(void* comm);
+TK_API int tk_stream_wait_deadline(void* stream, int32_t timeout_ms, void* comm);
+
 /* Leaves `sms` SMs of every device free of pointwise (Tier 1 / Tier 2) CTAs,
  * so that kernels launched concurrently on other streams -- NCCL all-gathers
  * overlapping a sharded update -- can run at the same time.  Process-wide;

@@ -181,6 +181,10 @@ def test_argument_checks_need_no_device():
          _native.TK_ERR_INVALID, "world 0"),
         (lambda: L.tk_step_buffers_noalloc(None, 0, _native.TK_ADAMW, None, 1, 0.0, None, None),
          _native.TK_ERR_INVALID, "hparams is NULL"),
+        (lambda: L.tk_nccl_comm_async_error(None, ctypes.byref(ctypes.c_int32())),
+         _native.TK_ERR_INVALID, "null argument"),
+        (lambda: L.tk_stream_wait_deadline(None, -1, None),
+         _native.TK_ERR_INVALID, "negative timeout"),
     ]
     for call, code, text in cases:
         status, msg = _err(call())
@@ -192,4 +196,5 @@ def test_argument_checks_need_no_device():
     assert L.tk_shard_destroy(None, None) == 0
     assert L.tk_muon_shard_destroy(None, None) == 0
     assert L.tk_nccl_comm_destroy(None) == 0
+    assert L.tk_nccl_comm_abort(None) == 0
     assert L.tk_set_reserved_sms(0) == 0

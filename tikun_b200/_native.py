@@ -158,6 +158,9 @@ _SIGNATURES = {
     "tk_nccl_unique_id": [_P],
     "tk_nccl_comm_init": [_P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)],
     "tk_nccl_comm_destroy": [_P],
+    "tk_nccl_comm_async_error": [_P, ctypes.POINTER(_I32)],
+    "tk_nccl_comm_abort": [_P],
+    "tk_stream_wait_deadline": [_P, _I32, _P],
     "tk_step_buffers_noalloc": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams),
                                 _U64, _F, ctypes.POINTER(_F), _P],
     "tk_newton_schulz_2d": [_P, _I64, _I64, _I32, _I32, _I32, _P],

@@ -23,9 +23,11 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "tk_internal.h"
@@ -44,6 +46,8 @@ struct Nccl {
   ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
   ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 
@@ -71,6 +75,8 @@ int nccl(const Nccl** out) {
       sym(fns.GetUniqueId, "ncclGetUniqueId");
       sym(fns.CommInitRank, "ncclCommInitRank");
       sym(fns.CommDestroy, "ncclCommDestroy");
+      sym(fns.CommAbort, "ncclCommAbort");
+      sym(fns.CommGetAsyncError, "ncclCommGetAsyncError");
       sym(fns.GetErrorString, "ncclGetErrorString");
       if (ok) status = 0;
     }
@@ -166,6 +172,65 @@ int tk_nccl_comm_destroy(void* comm) {
   TK_TRY(nccl(&N));
   TK_NCCL_TRY(N, N->CommDestroy(static_cast<ncclComm_t>(comm)));
   return TK_OK;
+}
+
+int tk_nccl_comm_async_error(void* comm, int32_t* result_out) {
+  clear_error();
+  if (comm == nullptr || result_out == nullptr) return set_error(TK_ERR_INVALID, "null argument");
+  const Nccl* N = nullptr;
+  TK_TRY(nccl(&N));
+  ncclResult_t r = ncclSuccess;
+  TK_NCCL_TRY(N, N->CommGetAsyncError(static_cast<ncclComm_t>(comm), &r));
+  *result_out = (int32_t)r;
+  return TK_OK;
+}
+
+int tk_nccl_comm_abort(void* comm) {
+  clear_error();
+  if (comm == nullptr) return TK_OK;
+  const Nccl* N = nullptr;
+  TK_TRY(nccl(&N));
+  TK_NCCL_TRY(N, N->CommAbort(static_cast<ncclComm_t>(comm)));
+  return TK_OK;
+}
+
+int tk_stream_wait_deadline(void* stream, int32_t timeout_ms, void* comm) {
+  clear_error();
+  if (timeout_ms < 0) return set_error(TK_ERR_INVALID, "negative timeout %d ms", timeout_ms);
+  const Nccl* N = nullptr;
+  if (comm != nullptr) TK_TRY(nccl(&N));
+  ncclComm_t c = static_cast<ncclComm_t>(comm);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaStreamQuery(s);
+    if (e == cudaSuccess) return TK_OK;
+    if (e != cudaErrorNotReady) return cuda_error(e, "cudaStreamQuery");
+    if (N != nullptr) {
+      ncclResult_t r = ncclSuccess;
+      const ncclResult_t q = N->CommGetAsyncError(c, &r);
+      if (q != ncclSuccess || (r != ncclSuccess && r != ncclInProgress)) {
+        const char* why = N->GetErrorString(q != ncclSuccess ? q : r);
+        N->CommAbort(c);
+        return set_error(TK_ERR_DEVICE, "the communicator reported an error (%s) and was aborted",
+                         why);
+      }
+    }
+    const auto waited = std::chrono::duration_cast<std::chrono::milliseconds>(
+        std::chrono::steady_clock::now() - t0);
+    if (waited.count() > timeout_ms) {
+      if (N != nullptr) {
+        N->CommAbort(c);
+        return set_error(TK_ERR_DEVICE,
+                         "the stream's work did not finish within %d ms; the communicator was "
+                         "aborted",
+                         timeout_ms);
+      }
+      return set_error(TK_ERR_DEVICE, "the stream's work did not finish within %d ms",
+                       timeout_ms);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
 }
 
 // Both free functions keep the thread's error message: they run on failure

@@ -280,6 +280,18 @@ def nccl_comm_ptr(group=None, device=None) -> int:
     return int(ptr)
 
 
+def wait_step(stream, deadline_s: float, own_comm: int | None = None) -> None:
+    """Waits on the host for the work enqueued on ``stream`` at most
+    ``deadline_s`` seconds (tk_stream_wait_deadline).  On a communicator error
+    or at the deadline it raises TikunError; with ``own_comm`` (a communicator
+    from tk_nccl_comm_init, never PyTorch's, which PyTorch's watchdog aborts)
+    that communicator is aborted first, which ends collectives waiting for a
+    rank that is gone.  Results of that step are not valid."""
+    _native.check(_native.lib().tk_stream_wait_deadline(
+        ctypes.c_void_p(stream.cuda_stream), int(deadline_s * 1000),
+        ctypes.c_void_p(own_comm) if own_comm else None))
+
+
 class ShardedStep:
     """ZeRO-1 clipped AdamW/Lion/SGD through the C ABI (tk_shard_*): the
     native multi-GPU step over a flat f32 parameter/gradient arena laid out by
@@ -287,7 +299,9 @@ class ShardedStep:
     update kernel stores into every rank's arena over NVLink), "copy" (the
     copy engines copy each updated chunk into every rank's arena) or
     "allgather" (an in-place ncclAllGather after the update).  ``comm`` is an ncclComm_t
-    to use instead of the process group's (e.g. from tk_nccl_comm_init)."""
+    to use instead of the process group's (e.g. from tk_nccl_comm_init).  With
+    ``deadline_s`` set, every step waits for its work at most that long
+    (``wait_step``), aborting ``comm`` when one was given."""
 
     def __init__(self, plan: LayoutPlan, p_flat: torch.Tensor, g_flat: torch.Tensor,
                  hp: ZeroHParams, group=None, exchange: str = "peers", comm: int | None = None):
@@ -301,6 +315,8 @@ class ShardedStep:
         L = _native.lib()
         offs = (ctypes.c_uint64 * len(plan))(*[o for o, _ in plan.slots])
         lens = (ctypes.c_uint64 * len(plan))(*[n for _, n in plan.slots])
+        self.own_comm = comm
+        self.deadline_s: float | None = None
         comm = comm or nccl_comm_ptr(group, p_flat.device)
         handle = ctypes.c_void_p()
         s = torch.cuda.current_stream(p_flat.device).cuda_stream
@@ -323,11 +339,13 @@ class ShardedStep:
         if self.liveness is not None:
             self.liveness.step(self.step_count)
         L = _native.lib()
-        s = torch.cuda.current_stream(self.p.device).cuda_stream
+        st = torch.cuda.current_stream(self.p.device)
         out = ctypes.c_float(1.0)
         _native.check(L.tk_shard_step(self.handle, ctypes.byref(self.hparams), self.step_count,
                                       self.hp.max_norm, ctypes.byref(out) if return_scale else None,
-                                      s))
+                                      st.cuda_stream))
+        if self.deadline_s is not None:
+            wait_step(st, self.deadline_s, self.own_comm)
         return out.value if return_scale else None
 
     def close(self) -> None:
@@ -543,7 +561,8 @@ class MuonShard:
 class NativeMuonShard:
     """MuonShard through the C ABI (tk_muon_shard_*): the LPT assignment, the
     owner-major layout, the momentum, the exchange and its collectives run in
-    the library over the process group's NCCL communicator (or ``comm``)."""
+    the library over the process group's NCCL communicator (or ``comm``).
+    ``deadline_s`` works as in ShardedStep."""
 
     def __init__(self, shapes, dtype: torch.dtype, device, lr: float, momentum: float = 0.95,
                  nesterov: bool = True, ns_steps: int = 5, precision: int | None = None,
@@ -570,6 +589,8 @@ class NativeMuonShard:
                                    _native.DEFAULT_NS_PRECISION if precision is None
                                    else precision)
         mode = {"allgather": 0, "peers": 1, "copy": 2}[exchange]
+        self.own_comm = comm
+        self.deadline_s: float | None = None
         comm = comm or nccl_comm_ptr(group, self.device)
         handle = ctypes.c_void_p()
         s = torch.cuda.current_stream(self.device).cuda_stream
@@ -602,9 +623,11 @@ class NativeMuonShard:
         self.step_count += 1
         if self.liveness is not None:
             self.liveness.step(self.step_count)
-        s = torch.cuda.current_stream(self.device).cuda_stream
+        st = torch.cuda.current_stream(self.device)
         _native.check(_native.lib().tk_muon_shard_step(
-            self.handle, ptrs, _native.TK_F32 if gdt is None else gdt, s))
+            self.handle, ptrs, _native.TK_F32 if gdt is None else gdt, st.cuda_stream))
+        if self.deadline_s is not None:
+            wait_step(st, self.deadline_s, self.own_comm)
 
     def close(self) -> None:
         """Collective: every rank calls it before the process group goes."""
