@@ -1,21 +1,33 @@
 """A CPU model of where the Newton-Schulz kernels round, checked against the
 errors the B200 produced on the same inputs.
 
-For m < 256 (or bf16 operands) one iteration of tikun_b200's Newton-Schulz is
-three tensor-core GEMMs with 16-bit operands and f32 accumulation:
+One iteration of tikun_b200's Newton-Schulz is three tensor-core GEMMs with
+16-bit operands and f32 accumulation.  For m < 256 (or bf16 operands):
 
     A = round16(X X^T)
     B = round16(c (A A) + b A)          (the epilogue adds b A in f32)
     X = round16(B X + a X)              (the epilogue adds a X in f32)
 
-with X = round16(x / ||x||) first (the f16 power-of-two pre-scale is exact
-and changes nothing at these sizes) and the last iteration's f32 result as
-the output.  The figures below are the relative Frobenius errors against the
-oracle's f32 Newton-Schulz (crates/tikun-cpu/src/tensor_engine.rs:12-77) that
+and from 256 rows up with f16 operands (the folded form):
+
+    A = round16(X X^T),  A' = round16(c X X^T + b I)   (one product)
+    B' = round16(A A' + a I)                           (upper tiles, mirrored)
+    X = round16(B' X)
+
+with X = round16(2^k x / ||x||) first, the pre-scale 2^k undone exactly in
+the first iteration's epilogues, and the last iteration's f32 result as the
+output.  The symmetric GEMMs compute the upper tiles only and mirror them; for
+B' that matters, because A and A' are rounded separately and A A' is not
+exactly symmetric: the mirror adds about 3.5 % to the folded form's error.
+
+The figures below are the relative Frobenius errors against the oracle's f32
+Newton-Schulz (crates/tikun-cpu/src/tensor_engine.rs:12-77) that
 test_ns_gpu.py::test_ns_2d_matches_oracle measured on a B200 for these seeded
-inputs; the model reproduces them to within 1 %, so a change of rounding
+inputs.  The model reproduces them to within 1 %, so a change of rounding
 points can be judged on the CPU before it is built.
 """
+import math
+
 import numpy as np
 import pytest
 
@@ -29,6 +41,36 @@ def round16(x, fmt):
     if fmt == "bf16":
         return oracle.bf16_to_f32(oracle.f32_to_bf16(x))
     return x.astype(np.float16).astype(np.float32)
+
+
+def upper_mirror(a):
+    return np.triu(a) + np.triu(a, 1).T
+
+
+def prescale_k(m, n):
+    r = math.sqrt(m * n) / 16.0
+    return max(0, min(int(math.floor(math.log2(max(r, 1.0)))), 60))
+
+
+def ns_model_folded(x, steps=5):
+    tall = x.shape[0] > x.shape[1]
+    X = np.ascontiguousarray(x.T if tall else x).astype(np.float32)
+    m, n = X.shape
+    k = prescale_k(m, n)
+    norm = max(math.sqrt(float(np.sum(X.astype(np.float64) ** 2))), 1e-7)
+    X = round16(X * np.float32(1.0 / norm) * np.float32(2.0 ** k), "f16")
+    eye = np.eye(m, dtype=np.float32)
+    out = X
+    for it in range(steps):
+        alpha = np.float32(2.0 ** (-2 * k)) if it == 0 else np.float32(1)
+        post = np.float32(2.0 ** (-k)) if it == 0 else np.float32(1)
+        acc = upper_mirror(X @ X.T)
+        A = round16(alpha * acc, "f16")
+        Ap = round16((np.float32(NS_C) * alpha) * acc + np.float32(NS_B) * eye, "f16")
+        Bp = round16(upper_mirror(A @ Ap) + np.float32(NS_A) * eye, "f16")
+        out = (post * (Bp @ X)).astype(np.float32)
+        X = round16(out, "f16")
+    return out.T if tall else out
 
 
 def ns_model(x, fmt, steps=5):
@@ -61,3 +103,17 @@ def test_model_reproduces_the_measured_error(rows, cols, fmt):
     got = ns_model(x, fmt).astype(np.float64)
     err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
     assert abs(err - MEASURED[(rows, cols, fmt)]) <= 0.01 * MEASURED[(rows, cols, fmt)], err
+
+
+# the folded form (f16, m >= 256), measured on a B200 with the same inputs
+MEASURED_FOLDED = {(768, 768): 1.7556e-3, (768, 3072): 2.1105e-3}
+
+
+@pytest.mark.parametrize("rows,cols", sorted(MEASURED_FOLDED), ids=lambda v: str(v))
+def test_folded_model_reproduces_the_measured_error(rows, cols):
+    x = (np.random.default_rng(rows * 7 + cols).standard_normal((rows, cols)) * 0.01
+         ).astype(np.float32)
+    ref = oracle.polar_step_np(x, 5).astype(np.float64)
+    got = ns_model_folded(x).astype(np.float64)
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert abs(err - MEASURED_FOLDED[(rows, cols)]) <= 0.01 * MEASURED_FOLDED[(rows, cols)], err
