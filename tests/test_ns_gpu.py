@@ -8,7 +8,6 @@ Bars (stated here, used below):
   parameters (f16 operands).
 * The momentum buffer is element-wise f32 arithmetic: bit-identical.
 """
-import ctypes
 import os
 
 import numpy as np

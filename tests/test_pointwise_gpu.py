@@ -14,7 +14,7 @@ import torch
 
 import oracle
 from helpers import (POINTWISE_RTOL, Leaves, assert_bitexact, gpt2_small_init, gpt2_small_sizes,
-                     max_rel_err, tk_dtype, to_np)
+                     max_rel_err, to_np)
 from tikun_b200 import _native
 
 pytestmark = pytest.mark.gpu

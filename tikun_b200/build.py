@@ -31,20 +31,6 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found: the tikun_b200 CUDA library cannot be built")
 
 
-def cutlass_include() -> str | None:
-    """CuTe/CUTLASS header tree vendored with flashinfer (headers only)."""
-    try:
-        import flashinfer  # noqa: F401
-        import importlib.util
-
-        spec = importlib.util.find_spec("flashinfer")
-        root = os.path.dirname(spec.origin)
-        inc = os.path.join(root, "data", "cutlass", "include")
-        return inc if os.path.isdir(inc) else None
-    except Exception:
-        return None
-
-
 def _sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
@@ -68,9 +54,6 @@ def _compile(src: str) -> str:
            "-I", os.path.join(REPO, "include"), "-I", CSRC,
            "-Xcompiler", "-fPIC,-fvisibility=hidden,-ffp-contract=off",
            "-Xptxas", "-warn-spills"]
-    inc = cutlass_include()
-    if inc and src.endswith(".cu"):
-        cmd += ["-I", inc]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
