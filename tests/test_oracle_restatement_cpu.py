@@ -96,7 +96,7 @@ def test_two_restatements_agree_bit_for_bit(kind, scale):
 
 
 def test_step_zero_is_step_one():
-    # lib.rs:152: step_count.max(1)
+    # crates/tikun-cpu/src/lib.rs:152: step_count.max(1)
     p, g = inputs(257, 9)
     m, v = np.zeros(257, F), np.zeros(257, F)
     p0, m0, v0 = p.copy(), m.copy(), v.copy()
