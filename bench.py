@@ -170,18 +170,25 @@ def make_host_state(wl, seed=1234):
     return p, g
 
 
-def cpu_reference_run(wl, steps, warmup, nthreads, budget_s=None):
+def cpu_reference_run(wl, steps, warmup, nthreads, budget_s=None, chunk=None):
     """The oracle (tikun-cpu's algorithm, restated) on host cores, threads over
     leaves as tikun-cpu's rayon par_iter over leaves.
 
     Returns (params/s, ms/step, warm-up steps run, steps timed).  With
     ``budget_s`` the warm-up stops and the timed steps are cut once the
-    measured step time says they would run past that many seconds each."""
+    measured step time says they would run past that many seconds each.
+    With ``chunk`` every leaf is cut into contiguous pieces of at most that
+    many elements, so that all threads share the large leaves: a faster CPU
+    schedule than tikun-cpu's, reported beside it and labelled as such."""
     import oracle
 
     p, g = make_host_state(wl)
     m = [np.zeros_like(x) for x in p]
     v = [np.zeros_like(x) for x in p]
+    if chunk:
+        def pieces(arrs):
+            return [a[i:i + chunk] for a in arrs for i in range(0, a.size, chunk)]
+        p, g, m, v = pieces(p), pieces(g), pieces(m), pieces(v)
 
     def one(s):
         oracle.step_two_tier(p, g, m, v, oracle.ADAMW, HP["lr"], HP["b1"], HP["b2"], HP["eps"],
@@ -495,6 +502,14 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
                "sample": f"full workload, {csteps} timed steps after {cwarm} warm-up (about "
                          f"10 s), {nthreads} threads over leaves ({cms:.0f} ms/step)"}
+        # not the reference's schedule: the same arithmetic with every leaf cut
+        # into 1M-element pieces shared by all threads
+        hval, hms, hwarm, hsteps = cpu_reference_run(wl, 100, 3, nthreads, budget_s=5.0,
+                                                     chunk=1 << 20)
+        cpu["all_cores_chunked"] = {
+            "value": hval, "unit": "params/s", "cores": nthreads, "kind": "port, non-reference",
+            "sample": f"full workload, leaves cut into 1M-element pieces over {nthreads} "
+                      f"threads, {hsteps} timed steps after {hwarm} warm-up ({hms:.0f} ms/step)"}
     res = {
         "value": value, "ms_per_step": ms_step, "dtype": "f32", "scaling": "strong",
         "data": "synthetic (seeded N(0,0.02) params, N(0,%g) grads held fixed across steps)"

@@ -29,6 +29,9 @@ def test_cpu_reference_arms_run_on_tiny_workloads():
                 desc="tiny")
     value, ms, warm, steps = bench.cpu_reference_run(tiny, 2, 1, 2)
     assert value > 0 and ms > 0 and (warm, steps) == (1, 2)
+    # the chunked (non-reference) schedule processes the same elements
+    cval, cms, _, _ = bench.cpu_reference_run(tiny, 2, 1, 2, chunk=1000)
+    assert cval > 0 and cms > 0
     # a time budget far below one step cuts both phases to one step
     value, ms, warm, steps = bench.cpu_reference_run(tiny, 50, 5, 2, budget_s=1e-9)
     assert (warm, steps) == (1, 1)
