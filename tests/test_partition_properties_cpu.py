@@ -1,0 +1,83 @@
+"""Property tests (random inputs) for the host-side partitioning that every path
+depends on: the LayoutPlan offsets (crates/tikun-core/src/arena.rs:34-57), the
+ZeRO-1 and chunk-major ownership of the flat arena, and the LPT assignment and
+owner-major layout of Muon matrices, in Python and through the C ABI."""
+import ctypes
+
+import numpy as np
+from hypothesis import given, settings
+from hypothesis import strategies as st
+
+import oracle
+from tikun_b200 import _native
+from tikun_b200.arena import LayoutPlan, shard_bounds, shard_segments
+from tikun_b200.distributed import chunk_major_pieces, pieces_to_segments
+from tikun_b200.sharding import lpt_assign, ns_dense_flops, owner_major_layout
+
+leaf_sizes = st.lists(st.integers(min_value=1, max_value=70_000), min_size=1, max_size=40)
+worlds = st.integers(min_value=1, max_value=8)
+shapes = st.lists(st.tuples(st.integers(1, 600), st.integers(1, 600)), min_size=1, max_size=60)
+
+
+@settings(max_examples=150, deadline=None)
+@given(leaf_sizes)
+def test_native_layout_equals_the_oracle_and_is_aligned(sizes):
+    offs, total = _native.layout_from_shapes(sizes)
+    assert (offs, total) == oracle.layout_from_shapes(sizes)
+    assert all(o % 64 == 0 for o in offs)
+    ends = [o + 4 * n for o, n in zip(offs, sizes)]
+    assert all(e <= o for e, o in zip(ends, offs[1:])) and total == ends[-1]
+
+
+@settings(max_examples=150, deadline=None)
+@given(leaf_sizes, worlds)
+def test_zero1_shards_cover_every_element_once(sizes, world):
+    plan = LayoutPlan(sizes, pad_to=16 * world)
+    seen = [np.zeros(n, np.int8) for n in sizes]
+    for r in range(world):
+        lo, hi = shard_bounds(plan.total, world, r)
+        assert lo % 16 == 0 and hi % 16 == 0 and hi - lo == plan.total // world
+        for i, a, c in shard_segments(plan, lo, hi):
+            seen[i][a:a + c] += 1
+    assert all((s == 1).all() for s in seen)
+
+
+@settings(max_examples=100, deadline=None)
+@given(leaf_sizes, worlds, st.integers(min_value=1, max_value=6))
+def test_chunk_major_pieces_cover_every_element_once(sizes, world, chunks):
+    plan = LayoutPlan(sizes, pad_to=16 * world * chunks)
+    seen = [np.zeros(n, np.int8) for n in sizes]
+    for r in range(world):
+        for lo, hi in chunk_major_pieces(plan.total, world, r, chunks):
+            assert lo % 16 == 0
+            for i, a, c in pieces_to_segments(plan, lo, hi):
+                seen[i][a:a + c] += 1
+    assert all((s == 1).all() for s in seen)
+
+
+@settings(max_examples=150, deadline=None)
+@given(shapes, worlds)
+def test_lpt_and_owner_major_layout_native_equals_python(mats, world):
+    costs = [ns_dense_flops(r, c) for r, c in mats]
+    owner = lpt_assign(costs, world)
+    load = [0] * world
+    for i, w in enumerate(owner):
+        load[w] += costs[i]
+    # greedy onto the least-loaded rank keeps the spread within one matrix
+    assert max(load) - min(load) <= max(costs)
+    sizes = [r * c for r, c in mats]
+    offs, extent = owner_major_layout(sizes, owner, world)
+    assert extent % 64 == 0
+    for i, (o, n) in enumerate(zip(offs, sizes)):
+        assert o % 64 == 0 and owner[i] * extent <= o and o + n <= (owner[i] + 1) * extent
+    spans = sorted(zip(offs, sizes))
+    assert all(a + n <= b for (a, n), (b, _) in zip(spans, spans[1:]))
+
+    n = len(mats)
+    rows = (ctypes.c_int64 * n)(*[r for r, _ in mats])
+    cols = (ctypes.c_int64 * n)(*[c for _, c in mats])
+    own = (ctypes.c_int32 * n)()
+    off = (ctypes.c_uint64 * n)()
+    ext = ctypes.c_uint64()
+    _native.check(_native.lib().tk_muon_layout(n, rows, cols, world, own, off, ctypes.byref(ext)))
+    assert list(own) == owner and list(off) == offs and ext.value == extent
