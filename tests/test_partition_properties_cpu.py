@@ -81,3 +81,49 @@ def test_lpt_and_owner_major_layout_native_equals_python(mats, world):
     ext = ctypes.c_uint64()
     _native.check(_native.lib().tk_muon_layout(n, rows, cols, world, own, off, ctypes.byref(ext)))
     assert list(own) == owner and list(off) == offs and ext.value == extent
+
+
+# -- verifier text: crates/tikun-core/src/verifier.rs:14-45 with Rust's {:?} --
+def _rust_debug(s):
+    out = '"'
+    for ch in s:
+        code = ord(ch)
+        if ch in "\t\r\n\\\"":
+            out += {"\t": "\\t", "\r": "\\r", "\n": "\\n", "\\": "\\\\", '"': '\\"'}[ch]
+        elif code < 0x20 or code == 0x7f:
+            out += "\\u{%x}" % code
+        else:
+            out += ch
+    return out + '"'
+
+
+def _expected(nodes):
+    if not nodes:
+        return "Static verification failed: [EmptyPipeline]"
+    errs = []
+    for name, _, tile, _, width, _ in nodes:
+        if tile % 64 != 0:
+            errs.append(f"MisalignedCacheLine {{ node_name: {_rust_debug(name)}, tile_size: {tile} }}")
+        if width < 4 or width & (width - 1):
+            errs.append(f"InvalidVectorWidth {{ node_name: {_rust_debug(name)}, width: {width} }}")
+    return "Static verification failed: [" + ", ".join(errs) + "]" if errs else None
+
+
+ascii_names = st.text(alphabet=st.characters(min_codepoint=1, max_codepoint=127), max_size=10)
+nodes = st.lists(st.tuples(ascii_names, st.integers(0, 2), st.integers(0, 1 << 20),
+                           st.integers(0, 8),
+                           st.one_of(st.sampled_from([0, 1, 2, 3, 4, 6, 8, 16, 64, 1 << 40]),
+                                     st.integers(0, 1 << 16)),
+                           st.integers(0, 256)), max_size=6)
+
+
+@settings(max_examples=300, deadline=None)
+@given(nodes)
+def test_verifier_text_matches_rust_debug_formatting(nodes):
+    want = _expected(nodes)
+    try:
+        _native.verify(nodes)
+        got = None
+    except _native.TikunError as e:
+        got = str(e)
+    assert got == want

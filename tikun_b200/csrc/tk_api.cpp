@@ -129,11 +129,28 @@ int Scratch::alloc(size_t bytes, cudaStream_t s) {
 // (crates/tikun-cpu/src/lib.rs:74).
 static bool is_pow2(uint64_t x) { return x != 0 && (x & (x - 1)) == 0; }
 
+// Rust's Debug text of a string (str::escape_debug) for the characters a C
+// string can hold: \t \r \n \\ \" escaped by name, other ASCII control
+// characters as \u{hex}, everything else (UTF-8 bytes included) as is.
 static std::string rust_debug_str(const char* s) {
   std::string out = "\"";
   for (const char* c = s ? s : ""; *c; ++c) {
-    if (*c == '"' || *c == '\\') out += '\\';
-    out += *c;
+    const unsigned char u = static_cast<unsigned char>(*c);
+    switch (u) {
+      case '\t': out += "\\t"; break;
+      case '\r': out += "\\r"; break;
+      case '\n': out += "\\n"; break;
+      case '\\': out += "\\\\"; break;
+      case '"': out += "\\\""; break;
+      default:
+        if (u < 0x20 || u == 0x7f) {
+          char buf[16];
+          std::snprintf(buf, sizeof(buf), "\\u{%x}", u);
+          out += buf;
+        } else {
+          out += *c;
+        }
+    }
   }
   return out + "\"";
 }
