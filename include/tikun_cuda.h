@@ -41,7 +41,8 @@ enum {
   TK_ERR_CUDA = 3,        /* a CUDA runtime call failed */
   TK_ERR_ALLOC = 4,       /* device or pinned memory could not be obtained */
   TK_ERR_UNSUPPORTED = 5, /* combination not implemented */
-  TK_ERR_DEVICE = 6       /* a kernel reported an error status (bounded wait expired) */
+  TK_ERR_DEVICE = 6       /* a kernel reported an error status (bounded wait expired),
+                             or a step missed its deadline (tk_stream_wait_deadline) */
 };
 
 /* element types */
