@@ -43,3 +43,31 @@ def test_cpu_reference_arms_run_on_tiny_workloads():
     # a budget below the largest matrix forces a scaled-down timing
     value, ms, sample = bench.cpu_muon_run(muon, 2, budget_flops=1e7)
     assert "timed at" in sample and "extrapolated by FLOP ratio" in sample
+
+
+def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
+    import json
+
+    tiny = dict(sizes=[1000, 17, 4097], kinds=["w", "b", "w"], max_norm=1.0, g_std=1e-2,
+                desc="tiny")
+    monkeypatch.setitem(bench.WORKLOADS, "gpt2-small-clip", tiny)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--steps", "4",
+                                      "--warmup", "3"])
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    bench.main()
+    lines = [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["steps"] == 4 and d["warmup"] == 3
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
+    # another rank under torchrun prints nothing and does no work
+    monkeypatch.setenv("RANK", "1")
+    bench.main()
+    assert not [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
