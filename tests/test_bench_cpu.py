@@ -24,6 +24,15 @@ def test_workload_shapes():
     assert abs(sum(ns_dense_flops(r, c) for r, c in m4["mats"]) / 1e12 - 665.9) < 0.05
 
 
+def test_ns_scratch_bytes_follow_the_library_layout():
+    # 2(3mn + 3m^2) bytes for 64-multiple shapes, plus 256 f64 norm partials,
+    # the scale and the 256-byte tail
+    m, n = 4096, 14336
+    assert bench.ns_scratch_bytes(m, n) == 2 * (3 * m * n + 3 * m * m) + 8 * 256 + 256 + 256
+    # padding: a 17 x 45 matrix uses 64-element rows
+    assert bench.ns_scratch_bytes(17, 45) >= 2 * (17 * 64 + 2 * 45 * 64 + 3 * 17 * 64)
+
+
 def test_cpu_reference_arms_run_on_tiny_workloads():
     tiny = dict(sizes=[1000, 17, 4097], kinds=["w", "b", "w"], max_norm=1.0, g_std=1e-2,
                 desc="tiny")
