@@ -105,6 +105,15 @@ def test_pytree_flattening_order():
     flat = _flatten_pytree(tree)
     assert flat[0] is a and flat[1] is b and flat[2] is c and flat[3] == (1234, 7)
     assert _extract_pointer_and_len(flat[3]) == (1234, 7)
+    # strided views would be stepped as if contiguous: rejected
+    import torch
+
+    with pytest.raises(ValueError, match="strided"):
+        _extract_pointer_and_len(torch.zeros(4, 6).t())
+    with pytest.raises(ValueError, match="strided"):
+        _extract_pointer_and_len(np.zeros(10, np.float32)[::2])
+    t = torch.zeros(4, 6)
+    assert _extract_pointer_and_len(t[1:3]) == (t[1:3].data_ptr(), 12)
     assert _extract_pointer_and_len(b) == (b.ctypes.data, 4)
 
 
@@ -198,3 +207,15 @@ def test_argument_checks_need_no_device():
     assert L.tk_nccl_comm_destroy(None) == 0
     assert L.tk_nccl_comm_abort(None) == 0
     assert L.tk_set_reserved_sms(0) == 0
+
+
+def test_muon_frontend_rejects_strided_parameters_before_any_launch():
+    import torch
+
+    from tikun_b200.muon import Muon
+
+    p = torch.nn.Parameter(torch.zeros(6, 4).t())  # a transposed (strided) weight
+    p.grad = torch.zeros_like(p)
+    opt = Muon([p], lr=0.02)
+    with pytest.raises(ValueError, match="contiguous"):
+        opt.step()

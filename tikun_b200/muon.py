@@ -62,6 +62,9 @@ class Muon(torch.optim.Optimizer):
         for i, p in enumerate(self.param_groups[0]["params"]):
             if p.grad is None:
                 continue
+            if not (p.is_contiguous() and p.grad.is_contiguous()):
+                raise ValueError("Muon parameters and gradients must be contiguous (the kernels "
+                                 "take their first address and shape)")
             mom = self.state_momentum[i]
             leaves.append((p.data_ptr(), p.grad.data_ptr(), mom.data_ptr(), 1, p.shape[0],
                            p.shape[1], _tk_dtype(p), _tk_dtype(p.grad)))

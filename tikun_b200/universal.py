@@ -26,10 +26,18 @@ from . import _native
 
 
 def _extract_pointer_and_len(tensor) -> tuple[int, int]:
-    """universal.py:22-35."""
+    """universal.py:22-35.  A strided view (a transposed weight, a slice with a
+    step) is rejected: its first address and element count do not describe
+    its elements, and the step would update the memory between them."""
     if hasattr(tensor, "data_ptr") and hasattr(tensor, "numel"):
+        if hasattr(tensor, "is_contiguous") and not tensor.is_contiguous():
+            raise ValueError("tikun_b200 steps contiguous tensors only; got a strided view of "
+                             f"shape {tuple(tensor.shape)}")
         return tensor.data_ptr(), tensor.numel()
     if isinstance(tensor, np.ndarray):
+        if not tensor.flags.c_contiguous:
+            raise ValueError("tikun_b200 steps contiguous arrays only; got a strided view of "
+                             f"shape {tensor.shape}")
         return tensor.ctypes.data, tensor.size
     if hasattr(tensor, "__array__"):
         arr = np.asarray(tensor)
