@@ -154,6 +154,20 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ workload
+def cpu_model() -> str:
+    """The host CPU's model name (recorded beside every CPU baseline)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or platform.machine()
+
+
 def make_host_state(wl, seed=1234):
     """Seeded synthetic leaves: params N(0, 0.02) (biases 0, LayerNorm weights 1),
     grads N(0, g_std)."""
@@ -229,7 +243,7 @@ def run_reference(args, wl, rank):
         "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": args.workload, "desc": wl["desc"]},
-        "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads, "kind": "port",
+        "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -499,7 +513,7 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         nthreads = os.cpu_count() or 1
         # a bounded sample: as many full steps as fit in about 10 s of host time
         cval, cms, cwarm, csteps = cpu_reference_run(wl, 100, 3, nthreads, budget_s=10.0)
-        cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
+        cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(), "kind": "port",
                "sample": f"full workload, {csteps} timed steps after {cwarm} warm-up (about "
                          f"10 s), {nthreads} threads over leaves ({cms:.0f} ms/step)"}
         # not the reference's schedule: the same arithmetic with every leaf cut
@@ -507,7 +521,7 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         hval, hms, hwarm, hsteps = cpu_reference_run(wl, 100, 3, nthreads, budget_s=5.0,
                                                      chunk=1 << 20)
         cpu["all_cores_chunked"] = {
-            "value": hval, "unit": "params/s", "cores": nthreads, "kind": "port, non-reference",
+            "value": hval, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(), "kind": "port, non-reference",
             "sample": f"full workload, leaves cut into 1M-element pieces over {nthreads} "
                       f"threads, {hsteps} timed steps after {hwarm} warm-up ({hms:.0f} ms/step)"}
     res = {
@@ -786,7 +800,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     if not args.no_cpu_baseline and world == 1 and rank == 0:
         nthreads = os.cpu_count() or 1
         cval, cms, csample = cpu_muon_run(wl, nthreads)
-        cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "kind": "port",
+        cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(), "kind": "port",
                "sample": f"{csample} ({cms:.0f} ms/step)"}
     return {
         "value": value, "ms_per_step": ms_step, "dtype": "bf16 params, f16 tensor-core operands",
@@ -847,7 +861,7 @@ def main():
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f32 Newton-Schulz, bf16 params", "data": "synthetic",
                 "config": {"workload": args.workload, "desc": MUON[args.workload]["desc"]},
-                "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads,
+                "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(),
                                  "kind": "port", "sample": sample},
                 "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}), flush=True)

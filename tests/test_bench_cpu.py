@@ -74,6 +74,7 @@ def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
         assert key in d, key
     assert d["impl"] == "reference" and d["steps"] == 4 and d["warmup"] == 3
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["cpu_baseline"]["cores"] >= 1 and d["cpu_baseline"]["cpu_model"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
     # another rank under torchrun prints nothing and does no work
