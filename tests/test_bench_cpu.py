@@ -81,3 +81,21 @@ def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
     monkeypatch.setenv("RANK", "1")
     bench.main()
     assert not [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+
+
+def test_muon_reference_arm_prints_the_contract_line(monkeypatch, capsys):
+    import json
+
+    tiny = dict(mats=[(64, 96), (96, 64), (128, 128)], adamw=[300, 64], layers=1,
+                inbackward=False, desc="tiny muon")
+    monkeypatch.setitem(bench.MUON, "muon-gpt2-d768", tiny)
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--workload",
+                                      "muon-gpt2-d768"])
+    monkeypatch.setenv("RANK", "0")
+    monkeypatch.setenv("WORLD_SIZE", "1")
+    bench.main()
+    lines = [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["value"] > 0 and d["cpu_baseline"]["cpu_model"]
+    assert d["config"]["workload"] == "muon-gpt2-d768" and d["e2e"]["h2d_bytes_per_step"] == 0
