@@ -127,3 +127,44 @@ def test_verifier_text_matches_rust_debug_formatting(nodes):
     except _native.TikunError as e:
         got = str(e)
     assert got == want
+
+
+# -- the Muon exchange's copy kernel (peer_copy_kernel in tikun_b200/csrc/tk_ns.cu) --
+def _peer_copy_units(entry_bytes, grid, threads=512, unroll=4):
+    """The kernel's work split restated: 16-byte units numbered across the
+    entries (unit0 prefix sums), an equal contiguous range per CTA, each thread
+    walking its units in order with a cursor over the entries.  Returns
+    per-entry byte coverage counts."""
+    unit0 = [0]
+    for b in entry_bytes:
+        unit0.append(unit0[-1] + (b + 15) // 16)
+    total, n = unit0[-1], len(entry_bytes)
+    cover = [np.zeros(b, np.int32) for b in entry_bytes]
+    per = (total + grid - 1) // grid
+    for blk in range(grid):
+        u0, u1 = blk * per, min(blk * per + per, total)
+        for t in range(threads):
+            e = 0
+            base = u0
+            while base < u1:
+                for k in range(unroll):
+                    u = base + k * threads + t
+                    if u >= u1:
+                        continue
+                    while e + 1 < n and unit0[e + 1] <= u:
+                        e += 1
+                    off = (u - unit0[e]) * 16
+                    rem = entry_bytes[e] - off
+                    ln = 16 if rem >= 16 else rem
+                    assert 0 < ln <= 16 and off + ln <= entry_bytes[e]
+                    cover[e][off:off + ln] += 1
+                base += threads * unroll
+    return cover
+
+
+@settings(max_examples=40, deadline=None)
+@given(st.lists(st.integers(min_value=0, max_value=40_000), min_size=1, max_size=6),
+       st.integers(min_value=1, max_value=12))
+def test_peer_copy_split_copies_every_byte_once(entry_bytes, grid):
+    cover = _peer_copy_units(entry_bytes, grid, threads=64, unroll=4)
+    assert all((c == 1).all() for c in cover)
