@@ -168,3 +168,56 @@ def _peer_copy_units(entry_bytes, grid, threads=512, unroll=4):
 def test_peer_copy_split_copies_every_byte_once(entry_bytes, grid):
     cover = _peer_copy_units(entry_bytes, grid, threads=64, unroll=4)
     assert all((c == 1).all() for c in cover)
+
+
+# -- the pointwise update's work split (pointwise_kernel in tk_pointwise.cu) --
+def _pointwise_cover(sizes, vec_ok, grid, threads=256, unroll=4):
+    """The kernel's split restated: the leaves' 4-element groups ("quads") in
+    one index space, an equal contiguous quad range per CTA, the leaf found by
+    binary search on q_begin, whole quads of aligned leaves through the
+    unrolled vector loop and the rest element by element.  Returns per-leaf
+    element coverage, and whether any vector access ran past a leaf's end."""
+    q_begin, total = [], 0
+    for n in sizes:
+        q_begin.append(total)
+        total += (n + 3) // 4
+    cover = [np.zeros(n, np.int32) for n in sizes]
+    past_end = False
+    for blk in range(grid):
+        q0, q1 = total * blk // grid, total * (blk + 1) // grid
+        if q0 >= q1:
+            continue
+        lo, hi = 0, len(sizes) - 1  # last leaf with q_begin <= q0
+        while lo < hi:
+            mid = (lo + hi + 1) >> 1
+            lo, hi = (mid, hi) if q_begin[mid] <= q0 else (lo, mid - 1)
+        li, q = lo, q0
+        while q < q1:
+            n = sizes[li]
+            seg_end = min(q1, q_begin[li] + (n + 3) // 4)
+            a, b = q - q_begin[li], seg_end - q_begin[li]
+            full_end = min(b, n >> 2) if vec_ok[li] else a
+            for t in range(threads):
+                lq = np.arange(a + t, full_end, threads * unroll)
+                qq = (lq[:, None] + np.arange(unroll)[None, :] * threads).ravel()
+                qq = qq[qq < full_end]
+                past_end |= bool((qq * 4 + 4 > n).any())
+                for j in range(4):
+                    np.add.at(cover[li], qq * 4 + j, 1)
+                for tq in range(max(a, full_end) + t, b, threads):
+                    cover[li][tq * 4:min(tq * 4 + 4, n)] += 1
+            q = seg_end
+            li += 1
+    return cover, past_end
+
+
+@settings(max_examples=60, deadline=None)
+@given(st.lists(st.tuples(st.integers(min_value=1, max_value=6000), st.booleans()),
+                min_size=1, max_size=6),
+       st.integers(min_value=1, max_value=9), st.sampled_from([(32, 4), (64, 2), (16, 1)]))
+def test_pointwise_split_updates_every_element_once(leaves, grid, shape):
+    sizes = [n for n, _ in leaves]
+    vec_ok = [v for _, v in leaves]
+    cover, past_end = _pointwise_cover(sizes, vec_ok, grid, threads=shape[0], unroll=shape[1])
+    assert not past_end
+    assert all((c == 1).all() for c in cover)
