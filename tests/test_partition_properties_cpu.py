@@ -5,7 +5,7 @@ owner-major layout of Muon matrices, in Python and through the C ABI."""
 import ctypes
 
 import numpy as np
-from hypothesis import given, settings
+from hypothesis import example, given, settings
 from hypothesis import strategies as st
 
 import oracle
@@ -221,3 +221,49 @@ def test_pointwise_split_updates_every_element_once(leaves, grid, shape):
     cover, past_end = _pointwise_cover(sizes, vec_ok, grid, threads=shape[0], unroll=shape[1])
     assert not past_end
     assert all((c == 1).all() for c in cover)
+
+
+# -- symmetric GEMM tiles (decode_tile / sym_store in tikun_b200/csrc/tk_ns.cu) --
+def _sym_writes(m, bm=128, bn=256):
+    """The symmetric products' tile plan restated: row block i computes the
+    128 x 256 column blocks floor(i/2) .. tiles_n-1, and the epilogue writes
+    each entry (r, c) with c >= r of its tile plus the mirror (c, r) for
+    c > r.  Returns how often each entry of the m x m output is written."""
+    tiles_m, tiles_n = -(-m // bm), -(-m // bn)
+    n_tiles = sum(tiles_n - (i >> 1) for i in range(tiles_m))
+    writes = np.zeros((m, m), np.int32)
+    for t in range(n_tiles):
+        r = t
+        for i in range(tiles_m):
+            cnt = tiles_n - (i >> 1)
+            assert cnt >= 1
+            if r < cnt:
+                tm, tn = i, (i >> 1) + r
+                break
+            r -= cnt
+        rows = np.arange(tm * bm, min(tm * bm + bm, m))
+        cols = np.arange(tn * bn, min(tn * bn + bn, m))
+        R, C = np.meshgrid(rows, cols, indexing="ij")
+        up = C >= R
+        np.add.at(writes, (R[up], C[up]), 1)
+        lo = C > R
+        np.add.at(writes, (C[lo], R[lo]), 1)
+    return writes
+
+
+@settings(max_examples=40, deadline=None)
+@given(st.integers(min_value=1, max_value=1100))
+@example(1)
+@example(127)
+@example(128)
+@example(129)
+@example(255)
+@example(256)
+@example(257)
+@example(383)
+@example(384)
+@example(385)
+@example(768)
+@example(1024)
+def test_symmetric_tiles_write_every_entry_once(m):
+    assert (_sym_writes(m) == 1).all()
