@@ -184,6 +184,20 @@ def make_host_state(wl, seed=1234):
     return p, g
 
 
+def pointwise_config(workload, wl):
+    """The workload as both arms report it (``config``)."""
+    return {"workload": workload, "desc": wl["desc"], "params": sum(wl["sizes"]),
+            "leaves": len(wl["sizes"]), "l2": "inputs (p,g,m,v) larger than L2; no flush"}
+
+
+def muon_config(workload, wl):
+    """The Muon workload as both arms report it (``config``)."""
+    return {"workload": workload, "desc": wl["desc"],
+            "params": sum(r * c for r, c in wl["mats"]) + sum(wl["adamw"]),
+            "muon_matrices": len(wl["mats"]), "adamw_leaves": len(wl["adamw"]),
+            "l2": "inputs larger than L2; no flush"}
+
+
 def cpu_reference_run(wl, steps, warmup, nthreads, budget_s=None, chunk=None):
     """The oracle (tikun-cpu's algorithm, restated) on host cores, threads over
     leaves as tikun-cpu's rayon par_iter over leaves.
@@ -225,6 +239,27 @@ def cpu_reference_run(wl, steps, warmup, nthreads, budget_s=None, chunk=None):
     return sum(wl["sizes"]) * steps / dt, dt / steps * 1e3, warm, steps
 
 
+def run_reference_muon(args, wl, rank):
+    """The reference arm for a Muon workload: --warmup untimed and --steps
+    timed bounded samples of the step (cpu_muon_sample) on host cores."""
+    if rank != 0:
+        return
+    nthreads = os.cpu_count() or 1
+    value, ms, sample = cpu_muon_run(wl, nthreads, args.steps, args.warmup)
+    sample = f"{args.steps} timed samples after {args.warmup} warm-up; each: {sample}"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "params/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 Newton-Schulz, bf16 params", "data": "synthetic",
+        "config": muon_config(args.workload, wl),
+        "parallelism": "host cores (the oracle's restatement of tikun-cpu)",
+        "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads,
+                         "cpu_model": cpu_model(), "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def run_reference(args, wl, rank):
     if rank != 0:
         return
@@ -242,7 +277,8 @@ def run_reference(args, wl, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "params/s",
         "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": args.workload, "desc": wl["desc"]},
+        "data": "synthetic", "config": pointwise_config(args.workload, wl),
+        "parallelism": "host cores (the oracle's restatement of tikun-cpu)",
         "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
@@ -250,24 +286,29 @@ def run_reference(args, wl, rank):
     }), flush=True)
 
 
-def cpu_muon_run(wl, nthreads, budget_flops=1.5e11):
-    """The oracle on host cores for a Muon workload, as a bounded sample: per
-    shape group, the momentum/Nesterov update and the f32 Newton-Schulz of one
-    matrix (tensor_engine.rs:12-77, GEMM rows over `nthreads`) are timed and
-    multiplied by the group's count; a matrix whose Newton-Schulz exceeds
-    `budget_flops` is timed at a scaled-down size of the same aspect ratio and
-    extrapolated by FLOP ratio.  The AdamW leaves (bf16 parameters) run in
-    full through the oracle's two-tier step, threads over leaves.  Returns
-    (params/s, ms per step, sample description)."""
+def cpu_muon_sample(wl, nthreads, budget_flops=4e10, aw_cap=1 << 22, seed=7):
+    """One bounded sample of a Muon workload's step on host cores through the
+    oracle, extrapolated to the whole step.
+
+    * Per shape group, the momentum/Nesterov update and the f32 Newton-Schulz
+      (tensor_engine.rs:12-77, GEMM rows over ``nthreads`` as rayon does) of
+      one matrix, timed at a scaled-down size of the same aspect ratio when its
+      Newton-Schulz exceeds ``budget_flops``, times the FLOP ratio and the
+      group's count.
+    * The AdamW leaves (bf16 p and g, f32 m and v) through the oracle's
+      two-tier step, threads over leaves as tikun-cpu's rayon: each leaf cut to
+      its first ``aw_cap`` elements, times the element ratio.
+
+    Returns (extrapolated seconds per full step, sample description)."""
     import oracle
 
     from tikun_b200.sharding import ns_dense_flops
 
-    rng = np.random.default_rng(7)
+    rng = np.random.default_rng(seed)
     groups = {}
     for rc in wl["mats"]:
         groups[rc] = groups.get(rc, 0) + 1
-    total_s, notes, extrapolated = 0.0, [], False
+    total_s, notes = 0.0, []
     for (r, c), cnt in groups.items():
         f = 1
         while ns_dense_flops(r // f, c // f) > budget_flops and min(r, c) // f >= 64:
@@ -280,25 +321,39 @@ def cpu_muon_run(wl, nthreads, budget_flops=1.5e11):
         x = np.ascontiguousarray(u, dtype=np.float32)
         oracle.polar_step(x, 5, nthreads)
         dt = time.perf_counter() - t0
-        scale = ns_dense_flops(r, c) / ns_dense_flops(rr, cc)
-        extrapolated |= f > 1
-        total_s += dt * scale * cnt
-        notes.append(f"{cnt}x{r}x{c}" + (f" (timed at {rr}x{cc})" if f > 1 else ""))
-    # AdamW leaves in full: bf16 p and g as uint16, f32 m and v
+        total_s += dt * (ns_dense_flops(r, c) / ns_dense_flops(rr, cc)) * cnt
+        notes.append(f"{cnt}x{r}x{c}" + (f" timed at {rr}x{cc}" if f > 1 else ""))
     sizes = wl["adamw"]
-    p = [oracle.f32_to_bf16((rng.standard_normal(n) * 0.02).astype(np.float32)) for n in sizes]
-    gr = [oracle.f32_to_bf16((rng.standard_normal(n) * 1e-3).astype(np.float32)) for n in sizes]
-    m = [np.zeros(n, np.float32) for n in sizes]
-    v = [np.zeros(n, np.float32) for n in sizes]
+    cut = [min(n, aw_cap) for n in sizes]
+    p = [oracle.f32_to_bf16((rng.standard_normal(n) * 0.02).astype(np.float32)) for n in cut]
+    gr = [oracle.f32_to_bf16((rng.standard_normal(n) * 1e-3).astype(np.float32)) for n in cut]
+    m = [np.zeros(n, np.float32) for n in cut]
+    v = [np.zeros(n, np.float32) for n in cut]
     t0 = time.perf_counter()
     oracle.step_two_tier(p, gr, m, v, oracle.ADAMW, HP["lr"], HP["b1"], HP["b2"], HP["eps"],
-                         HP["decay"], 1, 0.0, nthreads)
-    total_s += time.perf_counter() - t0
-    n_params = sum(r * c for r, c in wl["mats"]) + sum(sizes)
-    sample = ("Newton-Schulz of one matrix per shape group, times the group's count: " +
-              ", ".join(notes) + f"; AdamW leaves ({sum(sizes):,} params) in full; "
-              f"{nthreads} threads" + ("; extrapolated by FLOP ratio" if extrapolated else ""))
-    return n_params / total_s, total_s * 1e3, sample
+                         HP["decay"], 1, 0.0, min(nthreads, len(cut)))
+    # threads over leaves: the step takes as long as its largest leaf
+    total_s += (time.perf_counter() - t0) * max(sizes) / max(cut)
+    desc = ("Newton-Schulz of one matrix per shape group (" + ", ".join(notes) +
+            "), times the FLOP ratio and the group's count; AdamW leaves cut to their first "
+            f"{aw_cap:,} elements, times the element ratio; {nthreads} threads; extrapolated")
+    return total_s, desc
+
+
+def cpu_muon_run(wl, nthreads, steps, warmup):
+    """``warmup`` untimed and ``steps`` timed bounded samples (cpu_muon_sample)
+    of a Muon workload on host cores; returns (params/s, ms per full step
+    extrapolated, sample description)."""
+    for k in range(warmup):
+        cpu_muon_sample(wl, nthreads, seed=100 + k)
+    per = []
+    desc = ""
+    for k in range(steps):
+        t, desc = cpu_muon_sample(wl, nthreads, seed=k)
+        per.append(t)
+    step_s = sum(per) / len(per)
+    n_params = sum(r * c for r, c in wl["mats"]) + sum(wl["adamw"])
+    return n_params / step_s, step_s * 1e3, desc
 
 
 def muon_workloads():
@@ -528,14 +583,12 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
         "value": value, "ms_per_step": ms_step, "dtype": "f32", "scaling": "strong",
         "data": "synthetic (seeded N(0,0.02) params, N(0,%g) grads held fixed across steps)"
                 % wl["g_std"],
-        "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
-                   "leaves": len(wl["sizes"]),
-                   "parallelism": "single GPU" if world == 1 else
-                   f"zero1-dp{world} via tk_shard_step (" + {
-                       "fused": "update kernel stores into peer arenas over NVLink",
-                       "copy": "copy engines copy each updated chunk into peer arenas",
-                       "allgather": "ncclAllGather after the update"}[args.zero] + ")",
-                   "l2": "inputs (p,g,m,v) larger than L2; no flush"},
+        "config": pointwise_config(args.workload, wl),
+        "parallelism": "single GPU" if world == 1 else
+        f"zero1-dp{world} via tk_shard_step (" + {
+            "fused": "update kernel stores into peer arenas over NVLink",
+            "copy": "copy engines copy each updated chunk into peer arenas",
+            "allgather": "ncclAllGather after the update"}[args.zero] + ")",
         "roofline": {"bound": "hbm", "kernel": "pointwise_kernel (AdamW update)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
@@ -568,6 +621,104 @@ def ns_scratch_bytes(m, n):
     nblk = max(1, min(256, (m * n + 16383) // 16384))
     return (a256(m * ldx * 2) + 2 * a256(n * ldm * 2) + 3 * a256(m * ldm * 2) + a256(8 * nblk)
             + a256(4) + 256)
+
+
+def muon_host_e2e(args, wl, world, dev, torch, dist, stream, mine, mats, hp, mhp, p_of, g_of,
+                  p_aw, g_aw, plan, segs):
+    """The Muon step end to end through the C ABI with host buffers, the
+    reference's calling convention (MuonND hands NumPy buffers to the engine,
+    python/tikun/muon_nd.py:96-126): this rank's matrices (bf16 p and g, f32
+    momentum) and its AdamW slice (bf16 p and g, f32 m and v) live in host
+    memory, page-locked with cudaHostRegister; each step is tk_muon_step over
+    the host matrices (g, momentum and p stream in, p and momentum stream back,
+    overlapped with the tensor-core work) and tk_step_buffers over the host
+    AdamW leaves.  Both calls return when their results are back in host
+    memory.  Returns the ``e2e`` record (params/s over all ranks, max-over-ranks
+    time)."""
+    from tikun_b200 import _native
+
+    L = _native.lib()
+    bf = torch.bfloat16
+    s_handle = stream.cuda_stream
+    sizes = {i: mats[i][0] * mats[i][1] for i in mine}
+    n_mu = sum(sizes.values())
+    n_aw = sum(c for _, _, c in segs)
+    host = {"p": np.empty(max(n_mu, 1), np.int16), "g": np.empty(max(n_mu, 1), np.int16),
+            "mom": np.zeros(max(n_mu, 1), np.float32),
+            "ap": np.empty(max(n_aw, 1), np.int16), "ag": np.empty(max(n_aw, 1), np.int16),
+            "am": np.zeros(max(n_aw, 1), np.float32), "av": np.zeros(max(n_aw, 1), np.float32)}
+    cudart = torch.cuda.cudart()
+    registered = []
+    try:
+        for a in host.values():
+            torch.cuda.check_error(cudart.cudaHostRegister(a.ctypes.data, a.nbytes, 0))
+            registered.append(a)
+        t = {k: torch.from_numpy(a) for k, a in host.items()}
+        hoff, at = {}, 0
+        for i in mine:
+            hoff[i] = at
+            t["p"][at:at + sizes[i]].view(bf).copy_(p_of(i).view(-1))
+            g = g_of(i)
+            if g is not None:
+                t["g"][at:at + sizes[i]].view(bf).copy_(g.view(-1))
+            else:
+                t["g"][at:at + sizes[i]].view(bf).normal_(0, 1e-3)
+            at += sizes[i]
+        at = 0
+        for i, a, c in segs:
+            o = plan.slots[i][0] + a
+            t["ap"][at:at + c].view(bf).copy_(p_aw[o:o + c])
+            t["ag"][at:at + c].view(bf).copy_(g_aw[o:o + c])
+            at += c
+        base = {k: a.ctypes.data for k, a in host.items()}
+        arr = (_native.TkMuonLeaf * max(len(mine), 1))()
+        for k, i in enumerate(mine):
+            r, c = mats[i]
+            arr[k] = _native.TkMuonLeaf(base["p"] + hoff[i] * 2, base["g"] + hoff[i] * 2,
+                                        base["mom"] + hoff[i] * 4, 1, r, c, _native.TK_BF16,
+                                        _native.TK_BF16)
+        offs_aw = np.cumsum([0] + [c for _, _, c in segs])[:-1]
+        aw = _native.make_leaves([base["ap"] + int(o) * 2 for o in offs_aw],
+                                 [base["ag"] + int(o) * 2 for o in offs_aw],
+                                 [base["am"] + int(o) * 4 for o in offs_aw],
+                                 [base["av"] + int(o) * 4 for o in offs_aw],
+                                 [c for _, _, c in segs], [_native.TK_BF16] * len(segs),
+                                 [_native.TK_BF16] * len(segs))
+
+        def host_step(k):
+            _native.check(L.tk_muon_step(arr, len(mine), ctypes.byref(mhp), s_handle))
+            _native.check(L.tk_step_buffers(aw[0], aw[1], _native.TK_ADAMW, ctypes.byref(hp), k,
+                                            0.0, None, s_handle))
+
+        host_step(1)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        steps = max(2, min(args.steps, 5))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for k in range(steps):
+            host_step(k + 2)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            tt = torch.tensor([e_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e_ms = float(tt.item())
+    finally:
+        for a in registered:
+            cudart.cudaHostUnregister(a.ctypes.data)
+    n_all = sum(r * c for r, c in mats) + sum(wl["adamw"])
+    return {"value": n_all / (e_ms / 1e3), "unit": "params/s", "ms_per_step": e_ms,
+            # per Muon parameter 8 B in (g 2, momentum 4, p 2) and 6 B out (p, momentum);
+            # per AdamW parameter 12 B in (p, g, m, v) and 10 B out (p, m, v); whole job
+            "h2d_bytes_per_step": 8 * sum(r * c for r, c in mats) + 12 * sum(wl["adamw"]),
+            "d2h_bytes_per_step": 6 * sum(r * c for r, c in mats) + 10 * sum(wl["adamw"]),
+            "steps": steps, "host_memory": "page-locked (cudaHostRegister)",
+            "api": "tk_muon_step over host matrices + tk_step_buffers over host AdamW leaves" +
+                   ("" if world == 1 else f", each of {world} ranks over its own matrices and "
+                                          "ZeRO-1 slice")}
 
 
 def run_muon(args, wl, world, rank, dev, torch, dist):
@@ -625,7 +776,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         return arr, len(idx)
 
     state = {"step": 0, "ns_ms": []}
-    ns_ev = []
+    ns_ev, aw_ev = [], []
     exchange = {"fused": "peers", "copy": "copy", "auto": "copy"}.get(args.zero, "allgather")
     if world > 1:
         # Muon matrices LPT-assigned to ranks (MuonShard); AdamW leaves ZeRO-1;
@@ -705,13 +856,15 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
 
         def one_step():
             state["step"] += 1
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
             e0.record(stream)
             _native.check(L.tk_muon_step(all_mu[0], all_mu[1], ctypes.byref(mhp), s_handle))
             e1.record(stream)
             ns_ev.append((e0, e1))
             _native.check(L.tk_apply_pointwise(all_aw[0], all_aw[1], _native.TK_ADAMW,
                                                ctypes.byref(hp), state["step"], None, s_handle))
+            e2.record(stream)
+            aw_ev.append((e1, e2))
             return -1  # counted below from the tile plan
     elif world == 1:
         # in-backward (one GPU): layer l's grads are produced on the main stream
@@ -796,26 +949,40 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     else:
         launches = ns_launches(mine) + 1
     launches *= args.steps
+    aw_params = sum(c for _, _, c in segs)
+    aw_GBps = None
+    if aw_ev:  # AdamW over bf16 p and g, f32 m and v: 22 B per parameter
+        aw_ms = sum(a.elapsed_time(b) for a, b in aw_ev[-args.steps:]) / args.steps
+        aw_GBps = 22 * aw_params / (aw_ms / 1e3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = muon_host_e2e(args, wl, world, dev, torch, dist, stream, mine, mats, hp, mhp,
+                            lambda i: (p_mu[offs[i]:offs[i] + sizes[i]] if world == 1
+                                       else ms.params[ms.offs[i]:ms.offs[i] + sizes[i]]),
+                            lambda i: g_mu[i] if i in g_mu else None,
+                            p_aw, g_aw, plan, segs)
+
     cpu = None
     if not args.no_cpu_baseline and world == 1 and rank == 0:
         nthreads = os.cpu_count() or 1
-        cval, cms, csample = cpu_muon_run(wl, nthreads)
-        cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(), "kind": "port",
-               "sample": f"{csample} ({cms:.0f} ms/step)"}
+        cval, cms, csample = cpu_muon_run(wl, nthreads, steps=3, warmup=1)
+        cpu = {"value": cval, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(),
+               "kind": "port",
+               "sample": f"3 timed samples after 1 warm-up, each: {csample} "
+                         f"({cms:.0f} ms per full step, extrapolated)"}
     return {
         "value": value, "ms_per_step": ms_step, "dtype": "bf16 params, f16 tensor-core operands",
         "scaling": "strong",
         "data": "synthetic (seeded N(0,0.02) bf16 params, N(0,1e-3) bf16 grads)",
-        "config": {"workload": args.workload, "desc": wl["desc"], "params": n_params,
-                   "muon_matrices": len(mats), "adamw_leaves": len(wl["adamw"]),
-                   "parallelism": "single GPU" if world == 1 else
-                   f"muon-lpt{world}+zero1-dp{world}, " + (
-                       {"peers": "update kernels store into peer arenas over NVLink",
-                        "copy": "a copy kernel on 16 reserved SMs stores each finished Muon "
-                                "batch into peer arenas during the next batch; the AdamW update "
-                                "kernel stores into them",
-                        "allgather": "all-gathers after the updates"}[exchange]),
-                   "l2": "inputs larger than L2; no flush"},
+        "config": muon_config(args.workload, wl),
+        "parallelism": "single GPU" if world == 1 else
+        f"muon-lpt{world}+zero1-dp{world}, " + (
+            {"peers": "update kernels store into peer arenas over NVLink",
+             "copy": "a copy kernel on 16 reserved SMs stores each finished Muon "
+                     "batch into peer arenas during the next batch; the AdamW update "
+                     "kernel stores into them",
+             "allgather": "all-gathers after the updates"}[exchange]),
         "roofline": {"bound": "tensor", "kernel": "gemm_tn_kernel (Newton-Schulz GEMMs)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
@@ -823,8 +990,10 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
                      "ns_ms_per_step": ns_ms,
                      "issued_tflops": my_issued / (ns_ms / 1e3) / 1e12,
                      "issued_frac": my_issued / (ns_ms / 1e3) / 1e12 / peak,
-                     "ns_dense_tflop_per_step_this_rank": my_dense / 1e12},
-        "gpu_launches": launches, "clocks": clocks, "e2e": None, "cpu_baseline": cpu,
+                     "ns_dense_tflop_per_step_this_rank": my_dense / 1e12,
+                     "adamw_GBps": aw_GBps,
+                     "adamw_frac_of_hbm": None if aw_GBps is None else aw_GBps / load_peaks()[0]},
+        "gpu_launches": launches, "clocks": clocks, "e2e": e2e, "cpu_baseline": cpu,
     }
 
 
@@ -834,7 +1003,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="tikun", choices=["tikun", "reference"])
-    ap.add_argument("--workload", default="gpt2-small-clip", choices=sorted(WORKLOADS) + sorted(MUON))
+    ap.add_argument("--workload", default="muon-llama3-8b", choices=sorted(WORKLOADS) + sorted(MUON))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--zero", default="auto", choices=["auto", "fused", "copy", "allgather"],
@@ -852,19 +1021,8 @@ def main():
     if args.impl == "reference":
         if args.workload in WORKLOADS:
             run_reference(args, WORKLOADS[args.workload], rank)
-        elif rank == 0:
-            nthreads = os.cpu_count() or 1
-            value, ms, sample = cpu_muon_run(MUON[args.workload], nthreads)
-            print(json.dumps({
-                "impl": "reference", "metric": METRIC, "value": value, "unit": "params/s",
-                "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": ms,
-                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "f32 Newton-Schulz, bf16 params", "data": "synthetic",
-                "config": {"workload": args.workload, "desc": MUON[args.workload]["desc"]},
-                "cpu_baseline": {"value": value, "unit": "params/s", "cores": nthreads, "cpu_model": cpu_model(),
-                                 "kind": "port", "sample": sample},
-                "e2e": {"value": value, "unit": "params/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}), flush=True)
+        else:
+            run_reference_muon(args, MUON[args.workload], rank)
         return
 
     import torch
@@ -885,6 +1043,7 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
                 "higher_is_better": True, "scaling": res["scaling"], "vs_baseline": None,
                 "dtype": res["dtype"], "data": res["data"], "config": res["config"],
+                "parallelism": res["parallelism"],
                 "roofline": res["roofline"], "gpu_launches": res["gpu_launches"],
                 "clocks": res["clocks"], "e2e": res["e2e"], "cpu_baseline": res["cpu_baseline"]}
         print(json.dumps(line), flush=True)

@@ -199,7 +199,8 @@ TK_API int tk_newton_schulz_3d(void* tensor, int64_t num_heads, int64_t head_dim
                                int32_t precision, void* stream);
 
 /* One Muon leaf: heads (0 or 1 for a matrix) contiguous rows x cols matrices
- * of parameters p, gradients g and f32 momentum, all device memory. */
+ * of parameters p, gradients g and f32 momentum: device memory, or (for
+ * tk_muon_step only) host memory. */
 typedef struct {
   void* p;
   const void* g;
@@ -225,8 +226,15 @@ typedef struct {
  *   U = NS(U);  p = p - lr*sqrt(max(1, rows/cols))*U
  * fused into one prologue kernel pass, the tensor-core iteration, and the
  * parameter update in the last GEMM's epilogue.  Same-shape matrices are
- * batched.  Stream-ordered; does not wait.  A kernel that gives up on a
- * bounded wait sets the device status word (tk_device_status). */
+ * batched.  Device leaves: stream-ordered, does not wait; a kernel that gives
+ * up on a bounded wait sets the device status word (tk_device_status).
+ * Host leaves (all leaves of one call on one side; pinned memory overlaps
+ * best), the reference's calling convention (muon_nd.py keeps momentum in
+ * NumPy arrays): whole matrices stream through three device slots of
+ * TIKUN_MUON_STAGE_MB (default 2048) -- g, momentum and p in, p and momentum
+ * out -- overlapping both copy directions with the tensor-core work, and the
+ * call returns when the results are back in host memory (TK_ERR_DEVICE if a
+ * kernel gave up on a bounded wait). */
 TK_API int tk_muon_step(const tk_muon_leaf* leaves, size_t n_leaves,
                         const tk_muon_hparams* hp, void* stream);
 

@@ -46,12 +46,13 @@ def test_cpu_reference_arms_run_on_tiny_workloads():
     assert (warm, steps) == (1, 1)
     muon = dict(mats=[(64, 96), (96, 64), (256, 512)], adamw=[300, 64], layers=1,
                 inbackward=False, desc="tiny muon")
-    value, ms, sample = bench.cpu_muon_run(muon, 2)
+    value, ms, sample = bench.cpu_muon_run(muon, 2, steps=2, warmup=1)
     assert value > 0 and ms > 0 and "one matrix per shape group" in sample
-    assert "extrapolated" not in sample
-    # a budget below the largest matrix forces a scaled-down timing
-    value, ms, sample = bench.cpu_muon_run(muon, 2, budget_flops=1e7)
-    assert "timed at" in sample and "extrapolated by FLOP ratio" in sample
+    assert "timed at" not in sample
+    # a budget below the largest matrix forces a scaled-down timing, and long
+    # AdamW leaves are cut and scaled by the element ratio
+    secs, sample = bench.cpu_muon_sample(muon, 2, budget_flops=1e7, aw_cap=100)
+    assert secs > 0 and "timed at" in sample and "first 100 elements" in sample
 
 
 def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
@@ -60,8 +61,8 @@ def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
     tiny = dict(sizes=[1000, 17, 4097], kinds=["w", "b", "w"], max_norm=1.0, g_std=1e-2,
                 desc="tiny")
     monkeypatch.setitem(bench.WORKLOADS, "gpt2-small-clip", tiny)
-    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--steps", "4",
-                                      "--warmup", "3"])
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--workload",
+                                      "gpt2-small-clip", "--steps", "4", "--warmup", "3"])
     monkeypatch.setenv("RANK", "0")
     monkeypatch.setenv("WORLD_SIZE", "1")
     bench.main()
@@ -73,6 +74,8 @@ def test_reference_arm_prints_the_contract_line(monkeypatch, capsys):
                 "cpu_baseline", "e2e"):
         assert key in d, key
     assert d["impl"] == "reference" and d["steps"] == 4 and d["warmup"] == 3
+    # the same config dict the GPU arm prints for this workload
+    assert d["config"] == bench.pointwise_config("gpt2-small-clip", tiny)
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["cpu_baseline"]["cores"] >= 1 and d["cpu_baseline"]["cpu_model"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,
@@ -90,7 +93,7 @@ def test_muon_reference_arm_prints_the_contract_line(monkeypatch, capsys):
                 inbackward=False, desc="tiny muon")
     monkeypatch.setitem(bench.MUON, "muon-gpt2-d768", tiny)
     monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--workload",
-                                      "muon-gpt2-d768"])
+                                      "muon-gpt2-d768", "--steps", "2", "--warmup", "3"])
     monkeypatch.setenv("RANK", "0")
     monkeypatch.setenv("WORLD_SIZE", "1")
     bench.main()
@@ -98,4 +101,28 @@ def test_muon_reference_arm_prints_the_contract_line(monkeypatch, capsys):
     assert len(lines) == 1
     d = json.loads(lines[0])
     assert d["impl"] == "reference" and d["value"] > 0 and d["cpu_baseline"]["cpu_model"]
-    assert d["config"]["workload"] == "muon-gpt2-d768" and d["e2e"]["h2d_bytes_per_step"] == 0
+    # the requested steps and warm-up, and the config dict the GPU arm prints
+    assert d["steps"] == 2 and d["warmup"] == 3
+    assert d["config"] == bench.muon_config("muon-gpt2-d768", tiny)
+    assert d["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_default_workload_is_the_largest_single_gpu_config(monkeypatch):
+    """With no --workload the bench runs the Llama-3-8B-shaped Muon+AdamW step."""
+    import argparse
+
+    seen = {}
+
+    def fake_parse(self, args=None, namespace=None):
+        ns = real_parse(self, [] if args is None else args, namespace)
+        seen["workload"] = ns.workload
+        raise SystemExit(0)
+
+    real_parse = argparse.ArgumentParser.parse_args
+    monkeypatch.setattr(argparse.ArgumentParser, "parse_args", fake_parse)
+    monkeypatch.setattr(sys, "argv", ["bench.py"])
+    try:
+        bench.main()
+    except SystemExit:
+        pass
+    assert seen["workload"] == "muon-llama3-8b"

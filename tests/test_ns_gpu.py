@@ -217,6 +217,57 @@ def test_muon_step_ten_steps(rows, cols, heads, p_bf16):
     assert err <= (1e-3 if not p_bf16 else 3e-3), err
 
 
+@pytest.mark.parametrize("pinned", [True, False], ids=["pinned", "pageable"])
+def test_muon_step_host_buffers_match_device_buffers(pinned, monkeypatch):
+    """tk_muon_step with host leaves (the reference's calling convention: MuonND
+    keeps momentum in NumPy arrays, python/tikun/muon_nd.py:96-126) streams the
+    matrices through device slots and gives the same bytes as the same step on
+    device leaves.  A 1 MB slot budget forces several chunks per shape group
+    and reuse of every slot."""
+    monkeypatch.setenv("TIKUN_MUON_STAGE_MB", "1")
+    rng = np.random.default_rng(11)
+    shapes = [(256, 384), (384, 256), (256, 384), (96, 40), (300, 500), (256, 384)]
+    dt = [torch.bfloat16, torch.float32, torch.bfloat16, torch.float32, torch.bfloat16,
+          torch.float32]
+    hp_, hg, hm, dp, dg, dm = [], [], [], [], [], []
+    for (r, c), d in zip(shapes, dt):
+        p = (torch.from_numpy(rng.standard_normal((r, c)).astype(np.float32)) * 0.02).to(d)
+        hp_.append(p.pin_memory() if pinned else p.clone())
+        dp.append(p.cuda())
+        hm.append(torch.zeros(r, c).pin_memory() if pinned else torch.zeros(r, c))
+        dm.append(torch.zeros(r, c, device="cuda"))
+        hg.append(None)
+        dg.append(None)
+    for step in range(2):
+        for i, ((r, c), d) in enumerate(zip(shapes, dt)):
+            g = (torch.from_numpy(rng.standard_normal((r, c)).astype(np.float32)) * 1e-3).to(d)
+            hg[i] = g.pin_memory() if pinned else g.clone()
+            dg[i] = g.cuda()
+
+        def leaves(P, G, M):
+            return [(P[i].data_ptr(), G[i].data_ptr(), M[i].data_ptr(), 1, r, c,
+                     _native.TK_BF16 if d == torch.bfloat16 else _native.TK_F32,
+                     _native.TK_BF16 if d == torch.bfloat16 else _native.TK_F32)
+                    for i, ((r, c), d) in enumerate(zip(shapes, dt))]
+
+        _native.muon_step(leaves(dp, dg, dm), 0.02, 0.95)
+        _native.muon_step(leaves(hp_, hg, hm), 0.02, 0.95)  # returns when done
+        torch.cuda.synchronize()
+    for i in range(len(shapes)):
+        assert_bitexact(to_np(hp_[i]), to_np(dp[i]), f"p {i}")
+        assert_bitexact(to_np(hm[i]), to_np(dm[i]), f"momentum {i}")
+    assert _native.device_status() == 0
+
+
+def test_muon_step_rejects_mixed_host_and_device_leaves():
+    p = torch.zeros(64, 64, device="cuda")
+    g = torch.zeros(64, 64)
+    m = torch.zeros(64, 64, device="cuda")
+    with pytest.raises(ValueError, match="mixed"):
+        _native.muon_step([(p.data_ptr(), g.data_ptr(), m.data_ptr(), 1, 64, 64, _native.TK_F32,
+                            _native.TK_F32)], 0.02, 0.95)
+
+
 def test_muon_nd_frontend_matches_reference_frontend(golden_dir):
     """tikun_b200.MuonND against the reference's MuonND (python/tikun/muon_nd.py)
     run over the oracle: 1-D AdamW leaves bit-identical, 2-D/3-D leaves within
@@ -295,12 +346,15 @@ def _torch_fp32_ns(G: torch.Tensor, steps: int = 5) -> torch.Tensor:
     return X.T if tall else X
 
 
-@pytest.mark.parametrize("shape", [(4096, 14336), (14336, 4096), (4096, 4096), (4096, 1024)],
+@pytest.mark.parametrize("shape", [(4096, 14336), (14336, 4096), (4096, 4096), (4096, 1024),
+                                   (2048, 2048), (2048, 8192), (8192, 2048)],
                          ids=lambda s: f"{s[0]}x{s[1]}")
-def test_ns_full_llama_shapes_against_torch_fp32(shape):
-    """The 8B workload's matrix shapes at full size (the oracle's CPU loops
-    would take minutes): the engine's Newton-Schulz (f16 operands) against an
-    fp32 torch restatement of the same iteration, within the f16 bar."""
+def test_ns_full_model_shapes_against_torch_fp32(shape):
+    """The matrix shapes of the 8B workload (4096^2, 4096x1024, 4096x14336 and
+    its transpose) and of the 1.3B workload (2048^2, 2048x8192, 8192x2048) at
+    full size, where the oracle's CPU loops would take minutes: the engine's
+    Newton-Schulz (f16 operands) against an fp32 torch restatement of the same
+    iteration, within the f16 bar."""
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:

@@ -20,11 +20,12 @@ from tikun_b200 import _native
 pytestmark = pytest.mark.gpu
 
 
-def test_flat_adamw_ten_steps_no_clip():
+@pytest.mark.parametrize("n", [1_000_003, 100_000_000], ids=["1e6+3", "flat-1e8-full"])
+def test_flat_adamw_ten_steps_no_clip(n):
     """Flat-buffer AdamW, fresh N(0, 1e-3) grads each step, lr 1e-3, betas
-    (0.9, 0.999), eps 1e-8, decay 0.01, no clip: the flat-leaf workload at 1e6+3
-    elements (ragged tail)."""
-    L = Leaves([1_000_003])
+    (0.9, 0.999), eps 1e-8, decay 0.01, no clip, 10 steps: the flat-leaf
+    workload at its full 100,000,000 elements and at 1e6+3 (ragged tail)."""
+    L = Leaves([n])
     for step in range(1, 11):
         L.new_grads(1e-3)
         s_gpu = L.gpu_step(step, 0.0)
@@ -37,9 +38,10 @@ def test_flat_adamw_ten_steps_no_clip():
 @pytest.mark.parametrize("scale_down", [True, False], ids=["d128", "gpt2-small-full"])
 def test_gpt2_clipped_adamw(scale_down):
     """Clipped AdamW (global norm 1.0) over the GPT-2-small leaf table: 148
-    leaves; grads N(0, 1e-2) so the clip triggers.  Full size is the
-    124,439,808-parameter table (3 steps there to bound the oracle's time)."""
-    d, vocab, ctx, steps = (128, 1000, 256, 10) if scale_down else (768, 50257, 1024, 3)
+    leaves; grads N(0, 1e-2) so the clip triggers; 10 steps.  Full size is the
+    124,439,808-parameter table."""
+    d, vocab, ctx = (128, 1000, 256) if scale_down else (768, 50257, 1024)
+    steps = 10
     sizes = gpt2_small_sizes(d=d, vocab=vocab, ctx=ctx)
     assert len(sizes) == 148
     if not scale_down:

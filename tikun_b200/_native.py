@@ -290,7 +290,9 @@ def newton_schulz_3d_ffi(tensor_ptr: int, num_heads: int, head_dim_out: int, hea
 def muon_step(leaves: Sequence[tuple], lr: float, momentum: float, nesterov: bool = True,
               ns_steps: int = 5, precision: int | None = None, stream: int | None = None) -> None:
     """Fused Muon update over (p_ptr, g_ptr, mom_ptr, heads, rows, cols, p_dtype,
-    g_dtype) leaves (device memory).  Does not wait."""
+    g_dtype) leaves.  Device leaves: enqueued on the stream, does not wait.
+    Host leaves (all of them; the reference's convention): streamed through
+    device memory, returns when the results are back in host memory."""
     arr = (TkMuonLeaf * max(len(leaves), 1))()
     for i, L in enumerate(leaves):
         arr[i] = TkMuonLeaf(*L)

@@ -249,6 +249,154 @@ static int ns_entry(void* base, int64_t heads, int64_t rows, int64_t cols, int32
   return check_status(s);
 }
 
+// Host Muon leaves (the reference's calling convention: MuonND keeps its
+// momentum in NumPy arrays and hands host buffers to the engine,
+// python/tikun/muon_nd.py:96-126).  Every shape group is cut into chunks of
+// whole matrices that fit one device slot (TIKUN_MUON_STAGE_MB, default
+// 2048 MB, at least one matrix); chunk c moves through a ring of three slots:
+// the H2D stream copies its g, momentum and p into slot c % 3, the caller's
+// stream runs the fused Muon step on them (momentum, Nesterov, Newton-Schulz,
+// update), and the D2H stream copies p and momentum back, so both copy
+// directions overlap the tensor-core work.  Synchronous, like the reference.
+struct HostGroup {
+  int64_t m = 0, n = 0;
+  int p_dtype = TK_F32, g_dtype = TK_F32;
+  std::vector<const void*> g;
+  std::vector<void*> p;
+  std::vector<float*> mom;
+  std::vector<uint8_t> tall;
+};
+
+struct MuonHostPipe {
+  std::mutex mu;  // one host-buffer Muon step at a time per device
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  static constexpr int kSlots = 3;
+  cudaEvent_t start = nullptr, end = nullptr;
+  cudaEvent_t in_ready[kSlots] = {}, done[kSlots] = {}, out_done[kSlots] = {};
+};
+
+static int muon_host_pipe(MuonHostPipe** out) {
+  static MuonHostPipe pipes[64];
+  static bool ready[64] = {};
+  static std::mutex init_mu;
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(init_mu);
+  if (!ready[dev]) {
+    MuonHostPipe& P = pipes[dev];
+    TK_CUDA_TRY(cudaStreamCreateWithFlags(&P.h2d, cudaStreamNonBlocking));
+    TK_CUDA_TRY(cudaStreamCreateWithFlags(&P.d2h, cudaStreamNonBlocking));
+    for (cudaEvent_t* e : {&P.start, &P.end})
+      TK_CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    for (int k = 0; k < MuonHostPipe::kSlots; ++k)
+      for (cudaEvent_t* e : {&P.in_ready[k], &P.done[k], &P.out_done[k]})
+        TK_CUDA_TRY(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+    ready[dev] = true;
+  }
+  *out = &pipes[dev];
+  return TK_OK;
+}
+
+static size_t muon_stage_budget() {
+  const char* e = std::getenv("TIKUN_MUON_STAGE_MB");
+  double mb = e ? std::atof(e) : 2048.0;
+  if (!(mb > 0.0)) mb = 2048.0;
+  return (size_t)(mb * (1ull << 20));
+}
+
+static int muon_step_host(const std::vector<HostGroup>& groups, const tk_muon_hparams& hp,
+                          float mu, float om, int fmt, cudaStream_t s) {
+  NvtxRange range("tikun/muon_host_pipeline");
+  MuonHostPipe* P = nullptr;
+  TK_TRY(muon_host_pipe(&P));
+  std::lock_guard<std::mutex> serial(P->mu);
+  struct Chunk {
+    size_t group;
+    size_t first, count;
+  };
+  const size_t budget = muon_stage_budget();
+  auto a256 = [](size_t b) { return (b + 255) / 256 * 256; };
+  std::vector<Chunk> chunks;
+  size_t slot_bytes = 0;
+  for (size_t gi = 0; gi < groups.size(); ++gi) {
+    const HostGroup& G = groups[gi];
+    const size_t mat = (size_t)G.m * (size_t)G.n;
+    const size_t per = a256(mat * dt_size(G.p_dtype)) + a256(mat * dt_size(G.g_dtype)) + a256(mat * 4);
+    const size_t fit = std::max<size_t>(1, budget / per);
+    for (size_t first = 0; first < G.g.size(); first += fit) {
+      const size_t cnt = std::min(fit, G.g.size() - first);
+      chunks.push_back({gi, first, cnt});
+      slot_bytes = std::max(slot_bytes, cnt * per);
+    }
+  }
+  if (chunks.empty()) return TK_OK;
+  Scratch sc;
+  TK_TRY(sc.alloc(slot_bytes * MuonHostPipe::kSlots, s));
+  // On an early return the slots go back to the pool in s's order while copies
+  // on the side streams may still use them: s first waits for both.
+  struct JoinSideStreams {
+    MuonHostPipe* P;
+    cudaStream_t s;
+    bool armed = true;
+    ~JoinSideStreams() {
+      if (!armed) return;
+      if (cudaEventRecord(P->start, P->h2d) == cudaSuccess) cudaStreamWaitEvent(s, P->start, 0);
+      if (cudaEventRecord(P->end, P->d2h) == cudaSuccess) cudaStreamWaitEvent(s, P->end, 0);
+    }
+  } join_guard{P, s};
+  char* slots = static_cast<char*>(sc.get());
+  // everything starts after the caller's earlier work on s
+  TK_CUDA_TRY(cudaEventRecord(P->start, s));
+  TK_CUDA_TRY(cudaStreamWaitEvent(P->h2d, P->start, 0));
+  TK_CUDA_TRY(cudaStreamWaitEvent(P->d2h, P->start, 0));
+  for (size_t ci = 0; ci < chunks.size(); ++ci) {
+    const Chunk& C = chunks[ci];
+    const HostGroup& G = groups[C.group];
+    const int k = (int)(ci % MuonHostPipe::kSlots);
+    char* at = slots + (size_t)k * slot_bytes;
+    if (ci >= (size_t)MuonHostPipe::kSlots)
+      TK_CUDA_TRY(cudaStreamWaitEvent(P->h2d, P->out_done[k], 0));
+    const size_t mat = (size_t)G.m * (size_t)G.n;
+    const size_t pb = mat * dt_size(G.p_dtype), gb = mat * dt_size(G.g_dtype), mb = mat * 4;
+    std::vector<const void*> dg(C.count);
+    std::vector<void*> dp(C.count);
+    std::vector<float*> dm(C.count);
+    std::vector<uint8_t> tall(G.tall.begin() + C.first, G.tall.begin() + C.first + C.count);
+    for (size_t j = 0; j < C.count; ++j) {
+      const size_t i = C.first + j;
+      dp[j] = at;
+      at += a256(pb);
+      dg[j] = at;
+      at += a256(gb);
+      dm[j] = reinterpret_cast<float*>(at);
+      at += a256(mb);
+      TK_CUDA_TRY(cudaMemcpyAsync(const_cast<void*>(dg[j]), G.g[i], gb, cudaMemcpyHostToDevice, P->h2d));
+      TK_CUDA_TRY(cudaMemcpyAsync(dm[j], G.mom[i], mb, cudaMemcpyHostToDevice, P->h2d));
+      TK_CUDA_TRY(cudaMemcpyAsync(dp[j], G.p[i], pb, cudaMemcpyHostToDevice, P->h2d));
+    }
+    TK_CUDA_TRY(cudaEventRecord(P->in_ready[k], P->h2d));
+    TK_CUDA_TRY(cudaStreamWaitEvent(s, P->in_ready[k], 0));
+    const float upd_wide = (float)(-hp.lr * std::sqrt(std::max(1.0, (double)G.m / (double)G.n)));
+    const float upd_tall = (float)(-hp.lr * std::sqrt(std::max(1.0, (double)G.n / (double)G.m)));
+    TK_TRY(run_batches(G.m, G.n, dg, dp, &dm, tall, G.g_dtype, G.p_dtype, 1, upd_wide, upd_tall,
+                       mu, om, hp.nesterov ? 1 : 0, hp.ns_steps, fmt, s));
+    TK_CUDA_TRY(cudaEventRecord(P->done[k], s));
+    TK_CUDA_TRY(cudaStreamWaitEvent(P->d2h, P->done[k], 0));
+    for (size_t j = 0; j < C.count; ++j) {
+      const size_t i = C.first + j;
+      TK_CUDA_TRY(cudaMemcpyAsync(G.p[i], dp[j], pb, cudaMemcpyDeviceToHost, P->d2h));
+      TK_CUDA_TRY(cudaMemcpyAsync(G.mom[i], dm[j], mb, cudaMemcpyDeviceToHost, P->d2h));
+    }
+    TK_CUDA_TRY(cudaEventRecord(P->out_done[k], P->d2h));
+  }
+  // the caller's stream (and the slots it frees) waits for the last copies
+  TK_CUDA_TRY(cudaEventRecord(P->end, P->d2h));
+  TK_CUDA_TRY(cudaStreamWaitEvent(s, P->end, 0));
+  join_guard.armed = false;
+  return check_status(s);
+}
+
 }  // namespace tk
 
 using namespace tk;
@@ -295,6 +443,7 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
     std::vector<uint8_t> tall;
   };
   std::map<std::tuple<int64_t, int64_t, int, int>, Batch> groups;
+  Residency where = Residency::kNone;
   for (size_t i = 0; i < n_leaves; ++i) {
     const tk_muon_leaf& L = leaves[i];
     if (L.heads < 0 || L.rows < 0 || L.cols < 0)
@@ -312,8 +461,13 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
     for (const void* ptr : {(const void*)L.p, L.g, (const void*)L.momentum}) {
       Residency r;
       TK_TRY(classify_pointer(ptr, &r, dev));
-      if (r != Residency::kDevice)
-        return set_error(TK_ERR_INVALID, "leaf %zu: tk_muon_step takes device buffers", i);
+      if (where == Residency::kNone) where = r;
+      if (r != where)
+        return set_error(TK_ERR_INVALID,
+                         "leaf %zu: host and device buffers are mixed in one Muon call", i);
+      if (r == Residency::kHost && (peers != nullptr || copy != nullptr))
+        return set_error(TK_ERR_INVALID,
+                         "leaf %zu: the multi-GPU Muon steps take device buffers", i);
     }
     // an m x n and an n x m matrix share one batch (m = min, n = max)
     Batch& b = groups[std::make_tuple(std::min(L.rows, L.cols), std::max(L.rows, L.cols),
@@ -348,6 +502,24 @@ static int muon_step(const tk_muon_leaf* leaves, size_t n_leaves, const tk_muon_
   }
   std::stable_sort(order.begin(), order.end(),
                    [](const auto& a, const auto& b) { return a.first < b.first; });
+  if (where == Residency::kHost) {
+    std::vector<HostGroup> hg;
+    for (const auto& o : order) {
+      const auto& key = o.second->first;
+      const Batch& b = o.second->second;
+      HostGroup h;
+      h.m = std::get<0>(key);
+      h.n = std::get<1>(key);
+      h.p_dtype = std::get<2>(key);
+      h.g_dtype = std::get<3>(key);
+      h.g = b.g;
+      h.p = b.p;
+      h.mom = b.mom;
+      h.tall = b.tall;
+      hg.push_back(std::move(h));
+    }
+    return muon_step_host(hg, *hp, mu, om, fmt, s);
+  }
   double call_flops = 0.0;
   for (const auto& o : order) call_flops -= o.first * (double)hp->ns_steps;
   const int ks = std::min<int>(ns_streams(call_flops), (int)order.size());
