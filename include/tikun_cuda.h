@@ -155,10 +155,12 @@ TK_API int tk_step_buffers_async(const tk_leaf* leaves, size_t n_leaves, int32_t
  * pool memory; no cudaMalloc, cudaFree or other allocating routine is called.
  * Device leaves only, at most 224 leaves and 8192 norm blocks per call, else
  * TK_ERR_INVALID.  All calls on a device share the array: calls that overlap
- * on the GPU race.  The first call on each device looks up the array's address
- * (do it before any stream capture).  With clip_scale_out non-NULL the call
- * waits for the stream and returns the scale.  Its leaf tables and overlap
- * check live on the calling thread's stack: about 72 KB. */
+ * on the GPU race.  The first call on each device, and the first after a
+ * cudaDeviceReset, looks up the array's address (do it before any stream
+ * capture).  With clip_scale_out non-NULL the call waits for the stream and
+ * returns the scale; with NULL it returns once its kernels are enqueued (a
+ * kernel error then surfaces at the caller's next synchronisation).  Its leaf
+ * tables and overlap check live on the calling thread's stack: about 72 KB. */
 TK_API int tk_step_buffers_noalloc(const tk_leaf* leaves, size_t n_leaves, int32_t kind,
                                    const tk_hparams* hp, uint64_t step, float max_norm,
                                    float* clip_scale_out, void* stream);

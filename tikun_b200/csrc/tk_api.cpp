@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "tk_internal.h"
+#include "tk_testing.h"
 
 namespace tk {
 
@@ -197,10 +198,22 @@ int classify_pointer(const void* ptr, Residency* r, int dev) {
   return TK_OK;
 }
 
-struct Range {
-  uintptr_t lo, hi;
-  bool writable;
-};
+int check_overlaps(ByteRange* ranges, size_t n) {
+  std::sort(ranges, ranges + n,
+            [](const ByteRange& a, const ByteRange& b) { return a.lo < b.lo; });
+  uintptr_t max_any = 0, max_w = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const ByteRange& r = ranges[i];
+    if ((r.writable && max_any > r.lo) || max_w > r.lo)
+      return set_error(TK_ERR_INVALID,
+                       "leaf buffers overlap at %p: a buffer the step writes (p, m or v) "
+                       "shares memory with another buffer",
+                       (void*)r.lo);
+    max_any = std::max(max_any, r.hi);
+    if (r.writable) max_w = std::max(max_w, r.hi);
+  }
+  return TK_OK;
+}
 
 // Rejects null or mismatched fields, bad dtypes, any overlap between a range
 // the step writes (p, m, v) and any other range, and a mix of host and device
@@ -213,7 +226,7 @@ static int validate_leaves(const tk_leaf* leaves, size_t n, int kind, Residency*
     return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));
-  std::vector<Range> ranges;
+  std::vector<ByteRange> ranges;
   ranges.reserve(n * 4);
   for (size_t i = 0; i < n; ++i) {
     const tk_leaf& L = leaves[i];
@@ -242,19 +255,7 @@ static int validate_leaves(const tk_leaf* leaves, size_t n, int kind, Residency*
                          "leaf %zu: host and device buffers are mixed in one call", i);
     }
   }
-  std::sort(ranges.begin(), ranges.end(),
-            [](const Range& a, const Range& b) { return a.lo < b.lo; });
-  uintptr_t max_any = 0, max_w = 0;
-  for (const Range& r : ranges) {
-    if ((r.writable && max_any > r.lo) || max_w > r.lo)
-      return set_error(TK_ERR_INVALID,
-                       "leaf buffers overlap at %p: a buffer the step writes (p, m or v) "
-                       "shares memory with another buffer",
-                       (void*)r.lo);
-    max_any = std::max(max_any, r.hi);
-    if (r.writable) max_w = std::max(max_w, r.hi);
-  }
-  return TK_OK;
+  return check_overlaps(ranges.data(), ranges.size());
 }
 
 static bool aligned(const void* p, size_t a) { return ((uintptr_t)p % a) == 0; }
@@ -305,7 +306,7 @@ static float powi_f32(float a, int32_t b) {
   return recip ? 1.0f / r : r;
 }
 
-static PointwiseConsts make_consts(int kind, const tk_hparams& hp, uint64_t step) {
+PointwiseConsts make_consts(int kind, const tk_hparams& hp, uint64_t step) {
   PointwiseConsts c;
   c.lr = hp.lr;
   c.b1 = hp.beta1;
@@ -873,6 +874,24 @@ extern "C" {
 const char* tk_last_error(void) { return g_last_error.c_str(); }
 
 int tk_abi_version(void) { return TK_ABI_VERSION; }
+
+int tk_testing_library_device_bytes(uint64_t* bytes_out) {
+  g_last_error.clear();
+  if (bytes_out == nullptr) return set_error(TK_ERR_INVALID, "bytes_out is NULL");
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_pool_mu);
+  uint64_t bytes = 0;
+  if (g_pools[dev] != nullptr) {
+    cuuint64_t reserved = 0;
+    TK_CUDA_TRY(cudaMemPoolGetAttribute(g_pools[dev], cudaMemPoolAttrReservedMemCurrent, &reserved));
+    bytes += reserved;
+  }
+  if (g_status[dev] != nullptr) bytes += 256;
+  *bytes_out = bytes;
+  return TK_OK;
+}
 
 int tk_verify(const tk_pipeline* pipeline) {
   g_last_error.clear();

@@ -119,6 +119,21 @@ struct PointwiseConsts {
   float bc1, bc2;    // AdamW bias corrections
 };
 
+// The update's constants for optimizer `kind` at `step`, formed in f32 as the
+// reference does (crates/tikun-cpu/src/lib.rs:152-154): every entry point
+// builds them here, so all give the same bits.
+PointwiseConsts make_consts(int kind, const tk_hparams& hp, uint64_t step);
+
+// A byte range of one leaf buffer; writable for p, m and v.
+struct ByteRange {
+  uintptr_t lo, hi;
+  bool writable;
+};
+
+// Sorts `ranges` in place and fails with TK_ERR_INVALID if a range the step
+// writes shares memory with any other range.  Allocates nothing.
+int check_overlaps(ByteRange* ranges, size_t n);
+
 // Launchers (tk_pointwise.cu).  Tables hold leaves of one (p, g) dtype pair.
 int launch_sumsq_partials(const LeafTable& t, int g_dtype, double* partials, int n_blocks,
                           cudaStream_t s);

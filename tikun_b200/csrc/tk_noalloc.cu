@@ -20,8 +20,15 @@
 //     (different streams, no ordering between them) race on it;
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress) with that device current; make that first call
-//     before any stream capture.
+//     before any stream capture.  The address is kept per device together
+//     with the id of the CUDA context it was looked up in; after
+//     cudaDeviceReset the next call sees a new context id and looks it up
+//     again (do that call outside a stream capture too).
+//   * with clip_scale_out NULL the call returns once its kernels are
+//     enqueued: a kernel error then surfaces at the caller's next
+//     synchronisation, not from this call.
 // No cudaMalloc, cudaFree or other allocating routine is called.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -42,29 +49,62 @@ static __device__ __align__(256) double g_noalloc_scratch[kNoallocSlots];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mu;
-double* g_scratch_addr[kMaxDevices] = {};
+struct CachedAddress {
+  double* addr = nullptr;
+  unsigned long long ctx_id = 0;  // the CUDA context the address belongs to
+};
+CachedAddress g_scratch_addr[kMaxDevices];
+
+// The id of the current CUDA context (cuCtxGetCurrent + cuCtxGetId, from the
+// driver through the runtime's entry-point query; no link to libcuda).
+int current_context_id(unsigned long long* id) {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  if (get_current == nullptr || get_id == nullptr) {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaDriverEntryPointQueryResult qa, qb;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &a, 12000, cudaEnableDefault, &qa) !=
+            cudaSuccess ||
+        qa != cudaDriverEntryPointSuccess ||
+        cudaGetDriverEntryPointByVersion("cuCtxGetId", &b, 12000, cudaEnableDefault, &qb) !=
+            cudaSuccess ||
+        qb != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return set_error(TK_ERR_CUDA, "cuCtxGetCurrent / cuCtxGetId are not available from the driver");
+    }
+    get_current = reinterpret_cast<GetCurrentFn>(a);
+    get_id = reinterpret_cast<GetIdFn>(b);
+  }
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, id) != CUDA_SUCCESS)
+    return set_error(TK_ERR_CUDA, "could not identify the current CUDA context");
+  return TK_OK;
+}
 
 int scratch_for_current_device(double** out) {
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  TK_CUDA_TRY(cudaSetDevice(dev));  // binds the device's primary context to this thread
+  unsigned long long ctx = 0;
+  TK_TRY(current_context_id(&ctx));
   std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (g_scratch_addr[dev] == nullptr) {
+  CachedAddress& c = g_scratch_addr[dev];
+  if (c.addr == nullptr || c.ctx_id != ctx) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)
       return set_error(TK_ERR_CUDA, "cudaGetSymbolAddress of the fixed scratch failed: %s",
                        cudaGetErrorString(e));
-    g_scratch_addr[dev] = static_cast<double*>(p);
+    c.addr = static_cast<double*>(p);
+    c.ctx_id = ctx;
   }
-  *out = g_scratch_addr[dev];
+  *out = c.addr;
   return TK_OK;
 }
-
-struct NaRange {
-  uintptr_t lo, hi;
-  bool writable;
-};
 
 size_t na_esize(int dt) { return dt == TK_F32 ? 4 : 2; }
 
@@ -80,7 +120,7 @@ int validate(const tk_leaf* leaves, size_t n, int kind) {
     return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));
-  NaRange ranges[4 * kNoallocMaxLeaves];
+  ByteRange ranges[4 * kNoallocMaxLeaves];
   size_t nr = 0;
   for (size_t i = 0; i < n; ++i) {
     const tk_leaf& L = leaves[i];
@@ -107,29 +147,7 @@ int validate(const tk_leaf* leaves, size_t n, int kind) {
                          i);
     }
   }
-  std::sort(ranges, ranges + nr, [](const NaRange& a, const NaRange& b) { return a.lo < b.lo; });
-  uintptr_t max_any = 0, max_w = 0;
-  for (size_t i = 0; i < nr; ++i) {
-    const NaRange& r = ranges[i];
-    if ((r.writable && max_any > r.lo) || max_w > r.lo)
-      return set_error(TK_ERR_INVALID, "leaf buffers overlap at %p", (void*)r.lo);
-    max_any = std::max(max_any, r.hi);
-    if (r.writable) max_w = std::max(max_w, r.hi);
-  }
-  return TK_OK;
-}
-
-float na_powi(float a, int32_t b) {
-  const bool recip = b < 0;
-  uint32_t e = recip ? (uint32_t)(-(int64_t)b) : (uint32_t)b;
-  float r = 1.0f;
-  for (;;) {
-    if (e & 1u) r *= a;
-    e >>= 1;
-    if (e == 0) break;
-    a *= a;
-  }
-  return recip ? 1.0f / r : r;
+  return check_overlaps(ranges, nr);
 }
 
 }  // namespace
@@ -178,20 +196,7 @@ extern "C" int tk_step_buffers_noalloc(const tk_leaf* leaves, size_t n_leaves, i
       }
     }
 
-  PointwiseConsts c;
-  c.lr = hp->lr;
-  c.b1 = hp->beta1;
-  c.b2 = hp->beta2;
-  c.eps = hp->eps;
-  c.decay = hp->decay;
-  c.omb1 = 1.0f - hp->beta1;
-  c.omb2 = 1.0f - hp->beta2;
-  c.bc1 = c.bc2 = 1.0f;
-  if (kind == TK_ADAMW) {
-    const int32_t sv = (int32_t)(step < 1 ? 1 : (step > INT32_MAX ? INT32_MAX : step));
-    c.bc1 = 1.0f - na_powi(hp->beta1, sv);
-    c.bc2 = 1.0f - na_powi(hp->beta2, sv);
-  }
+  const PointwiseConsts c = make_consts(kind, *hp, step);
 
   const bool clip = max_norm > 0.0f && n_tables > 0;
   int n_partials = 0;

@@ -6,21 +6,28 @@
 //     A = X X^T;  B = b A + c A A;  X <- a X + B X       (a, b, c) = (3.4445, -4.7750, 2.0315)
 // on X (m x n, m <= n; a tall input is transposed first, :18-34) runs as three
 // "TN" GEMMs, D[M x N] = P[M x K] * Q[N x K]^T, whose operands are all K-major
-// row-major arrays in HBM:
-//   GEMM1  D = X X^T           P = Q = X          symmetric: upper tiles only
-//   GEMM2  D = A A = A A^T     P = Q = A          symmetric: upper tiles only
-//   GEMM3  D = X^T B  (= (B X)^T)                 P = X^T, Q = B
-// GEMM3 produces X_new^T directly; its epilogue stores both X_new^T and X_new
-// (a transposed store, which the one-row-per-thread TMEM layout makes
+// row-major arrays in HBM.  With f16 operands and m >= 256 the polynomial is
+// folded so that no epilogue reads a second matrix:
+//   GEMM1  A = X X^T and A' = c A + b I   P = Q = X    symmetric: upper tiles only
+//   GEMM2  B' = A A' + a I                P = A, Q = A' (A' symmetric)
+//   GEMM3  X_new^T = X^T B'               P = X^T, Q = B' (B' symmetric)
+// Below 256 rows (and with bf16 operands) GEMM2 forms B = c A A + b A and
+// GEMM3 X_new^T = X^T B + a X^T, the b A and a X^T terms added in f32 by the
+// epilogues.  GEMM3 produces X_new^T directly; its epilogue stores both X_new^T
+// and X_new (a transposed store, which the one-row-per-thread TMEM layout makes
 // coalesced), so no operand ever needs the MN-major layout.  Symmetric tiles
 // store each element above the diagonal twice (at (r, c) and (c, r)), which
 // keeps A and B exactly symmetric in storage.
 //
-// Kernel: persistent, one CTA per SM, 192 threads.  Warp 0 issues TMA loads of
-// 128x64 and 256x64 operand tiles (128-byte swizzle) into a 4-stage ring; warp
-// 1 allocates 512 TMEM columns (two 128x256 f32 accumulators) and one thread
-// issues tcgen05.mma (M=128, N=256, K=16); warps 2-5 drain an accumulator with
-// tcgen05.ld while the next tile accumulates into the other one.
+// Kernel: persistent, one CTA per SM, 320 threads.  Warp 0 issues TMA loads of
+// 128x64 and 256x64 operand tiles (128-byte swizzle, no multicast) into a
+// 4-stage ring; warp 1 allocates 512 TMEM columns (two 128x256 f32
+// accumulators) and one thread issues tcgen05.mma (M=128, N=256, K=16); eight
+// epilogue warps (2..9, two per TMEM lane quadrant, each taking half of the
+// columns) drain one accumulator with tcgen05.ld while the next tile
+// accumulates into the other one.  Every mbarrier wait is bounded (4 s of
+// %globaltimer); a wait that gives up raises a CTA abort flag and records a
+// code in a device status word.
 //
 // Operands are f16 (default) or bf16, accumulation f32.  In f16 mode the first
 // iterate is pre-scaled by a power of two 2^k (undone exactly in the GEMM1 and

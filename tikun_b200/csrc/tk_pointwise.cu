@@ -28,24 +28,29 @@ namespace {
 using namespace pw;
 
 // Tuning knobs (compile time): quads each thread keeps in flight per loop
-// trip, the minimum resident CTAs per SM the register budget must allow, and
-// the cache policy of the streaming accesses (0: default, 1: evict-first).
-// Measured on B200: all-f32 leaves are best at 4 quads per trip with 2 CTAs
-// per SM (unroll {1,2,4,8} x occupancy floor {1..8}); leaves with a bf16 p or
-// g at 2 quads per trip with 3 CTAs per SM (a 100M-element AdamW update
-// 614 -> 487 us for bf16 p and g, 598 -> 482 us for bf16 g), where the
-// f32 setting loses 20 % per element.
+// trip, the minimum resident CTAs per SM the register budget must allow,
+// whether the loop is software-pipelined (TK_PW_PIPE below), and the cache
+// policy of the streaming accesses (0: default, 1: evict-first).  Measured on
+// B200 (AdamW update, CUDA events, SM clock 1965 MHz), all settings giving
+// the same bits:
+//   all-f32 leaves: pipelined, 5 quads per trip, 1 CTA of 256 threads per SM
+//     (GPT-2-small table 0.595 -> 0.579 ms = 6022 GB/s, flat 100M elements
+//     0.478 -> 0.455 ms = 6150 GB/s); unpipelined the best was 4 quads with 2
+//     CTAs per SM; 6 pipelined quads spill and fall to 4500 GB/s;
+//   leaves with a bf16 p or g: 1 quad per trip, 6 CTAs per SM, not pipelined
+//     (flat 100M bf16 p and g 0.491 -> 0.420 ms = 5235 GB/s; 2 quads with 3
+//     CTAs per SM before).
 #ifndef TK_PW_UNROLL
-#define TK_PW_UNROLL 4
+#define TK_PW_UNROLL 5
 #endif
 #ifndef TK_PW_MINBLOCKS
-#define TK_PW_MINBLOCKS 2
+#define TK_PW_MINBLOCKS 1
 #endif
 #ifndef TK_PW_UNROLL_BF16
-#define TK_PW_UNROLL_BF16 2
+#define TK_PW_UNROLL_BF16 1
 #endif
 #ifndef TK_PW_MINBLOCKS_BF16
-#define TK_PW_MINBLOCKS_BF16 3
+#define TK_PW_MINBLOCKS_BF16 6
 #endif
 #ifndef TK_PW_STREAMING
 #define TK_PW_STREAMING 0
@@ -56,6 +61,15 @@ using namespace pw;
 #ifndef TK_PW_OVERSUB
 #define TK_PW_OVERSUB 0
 #endif
+// Software pipelining of the vector loop: 1 = each thread issues the loads of
+// its next trip's quads before it computes and stores the current ones, so a
+// warp's memory requests stay in flight through its arithmetic.
+#ifndef TK_PW_PIPE
+#define TK_PW_PIPE 1
+#endif
+#ifndef TK_PW_PIPE_BF16
+#define TK_PW_PIPE_BF16 0
+#endif
 constexpr int kThreads = 256;
 
 template <int PDT, int GDT>
@@ -63,6 +77,15 @@ struct Tune {
   static constexpr bool all_f32 = PDT == TK_F32 && GDT == TK_F32;
   static constexpr int unroll = all_f32 ? TK_PW_UNROLL : TK_PW_UNROLL_BF16;
   static constexpr int minblocks = all_f32 ? TK_PW_MINBLOCKS : TK_PW_MINBLOCKS_BF16;
+  static constexpr bool pipe = all_f32 ? TK_PW_PIPE != 0 : TK_PW_PIPE_BF16 != 0;
+};
+
+// One trip's quads of one thread: quad lq + u*kThreads for u < U, the ones
+// below `end` active.
+template <int U>
+struct Batch {
+  float P[U][4], G[U][4], M[U][4], V[U][4];
+  bool act[U];
 };
 
 template <typename T>
@@ -207,37 +230,56 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
     // quads [a, full_end) are whole and vector-accessible; the rest go scalar
     const uint64_t full_end = L.vec_ok ? min(b, L.n >> 2) : a;
     constexpr int kUnroll = Tune<PDT, GDT>::unroll;
-    for (uint64_t lq = a + threadIdx.x; lq < full_end; lq += kThreads * kUnroll) {
-      float P[kUnroll][4], G[kUnroll][4], M[kUnroll][4], V[kUnroll][4];
-      bool act[kUnroll];
+    constexpr uint64_t kStride = (uint64_t)kThreads * kUnroll;
+    auto load_batch = [&](uint64_t lq, Batch<kUnroll>& B) {
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
         const uint64_t qq = lq + (uint64_t)u * kThreads;
-        act[u] = qq < full_end;
-        if (act[u]) {
+        B.act[u] = qq < full_end;
+        if (B.act[u]) {
           const uint64_t e = qq * 4;
-          load_quad<GDT>(L.g, e, G[u]);
-          load_quad<PDT>(L.p, e, P[u]);
-          load_quad<TK_F32>(L.m, e, M[u]);
-          if constexpr (KIND == TK_ADAMW) load_quad<TK_F32>(L.v, e, V[u]);
+          load_quad<GDT>(L.g, e, B.G[u]);
+          load_quad<PDT>(L.p, e, B.P[u]);
+          load_quad<TK_F32>(L.m, e, B.M[u]);
+          if constexpr (KIND == TK_ADAMW) load_quad<TK_F32>(L.v, e, B.V[u]);
         }
       }
+    };
+    auto update_store = [&](uint64_t lq, Batch<kUnroll>& B) {
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        if (!act[u]) continue;
+        if (!B.act[u]) continue;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          float g = G[u][j];
+          float g = B.G[u][j];
           if constexpr (SCALE != 0) g = __fmul_rn(g, scale);
-          apply<KIND>(P[u][j], g, M[u][j], V[u][j], k);
+          apply<KIND>(B.P[u][j], g, B.M[u][j], B.V[u][j], k);
         }
         const uint64_t e = (lq + (uint64_t)u * kThreads) * 4;
-        store_quad<PDT>(L.p, e, P[u]);
+        store_quad<PDT>(L.p, e, B.P[u]);
 #pragma unroll
         for (int r = 0; r < kMaxPeers; ++r)  // the updated parameters, into each peer's copy
-          if (r < peers.n) store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, P[u]);
-        store_quad<TK_F32>(L.m, e, M[u]);
-        if constexpr (KIND == TK_ADAMW) store_quad<TK_F32>(L.v, e, V[u]);
+          if (r < peers.n) store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, B.P[u]);
+        store_quad<TK_F32>(L.m, e, B.M[u]);
+        if constexpr (KIND == TK_ADAMW) store_quad<TK_F32>(L.v, e, B.V[u]);
+      }
+    };
+    if constexpr (Tune<PDT, GDT>::pipe) {
+      uint64_t lq = a + threadIdx.x;
+      Batch<kUnroll> cur;
+      if (lq < full_end) load_batch(lq, cur);
+      for (; lq < full_end; lq += kStride) {
+        Batch<kUnroll> nxt;
+        const bool more = lq + kStride < full_end;
+        if (more) load_batch(lq + kStride, nxt);
+        update_store(lq, cur);
+        if (more) cur = nxt;
+      }
+    } else {
+      for (uint64_t lq = a + threadIdx.x; lq < full_end; lq += kStride) {
+        Batch<kUnroll> cur;
+        load_batch(lq, cur);
+        update_store(lq, cur);
       }
     }
     // ragged tail or unaligned leaf: element by element

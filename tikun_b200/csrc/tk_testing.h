@@ -21,6 +21,11 @@ TK_API int tk_testing_gemm_tn(const void* P, const void* Q, void* D, int batch, 
  * TK_ERR_DEVICE.  Exercises the failure path without faulting the GPU. */
 TK_API int tk_testing_bounded_wait(int limit_ms, void* stream);
 
+/* Device memory the library holds on the current device through its own
+ * allocations: the scratch pool's reserved bytes plus the status word (0 when
+ * neither was ever created).  Creates nothing. */
+TK_API int tk_testing_library_device_bytes(uint64_t* bytes_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,49 +25,65 @@ import numpy as np
 from . import _native
 
 
-def _extract_pointer_and_len(tensor) -> tuple[int, int]:
-    """universal.py:22-35.  A strided view (a transposed weight, a slice with a
-    step) is rejected: its first address and element count do not describe
-    its elements, and the step would update the memory between them."""
-    if hasattr(tensor, "data_ptr") and hasattr(tensor, "numel"):
-        if hasattr(tensor, "is_contiguous") and not tensor.is_contiguous():
+def _is_address_pair(x) -> bool:
+    """An (address, length) pair of ints stands for one raw f32 buffer."""
+    return isinstance(x, (tuple, list)) and len(x) == 2 and isinstance(x[0], int) \
+        and isinstance(x[1], int)
+
+
+def _is_container(x) -> bool:
+    if isinstance(x, (dict, list, tuple)):
+        return True
+    # any other iterable except a tensor, an array or a string
+    return hasattr(x, "__iter__") and not hasattr(x, "data_ptr") and \
+        not isinstance(x, (str, bytes, np.ndarray))
+
+
+def flatten_leaves(tree) -> list:
+    """The leaves of a PyTree, in the order the reference's front-end steps them
+    (python/tikun/universal.py:37-59): depth first, dict values in insertion
+    order, list/tuple/iterable items in order; an (address, length) pair of
+    ints is one leaf, and so is anything that is not a container."""
+    leaves = []
+    pending = [tree]
+    while pending:
+        node = pending.pop()
+        if _is_address_pair(node) or not _is_container(node):
+            leaves.append(node)
+            continue
+        children = list(node.values()) if isinstance(node, dict) else list(node)
+        pending.extend(reversed(children))  # leftmost child next
+    return leaves
+
+
+def leaf_address(leaf) -> tuple[int, int]:
+    """(address, element count) of one leaf.  Accepts what the reference's
+    front-end accepts (python/tikun/universal.py:22-35): a tensor with
+    data_ptr()/numel(), a NumPy array, anything with __array__ (a JAX array),
+    or an (address, length) pair.  A strided tensor or array (a transposed
+    weight, a slice with a step) is rejected: its first address and element
+    count do not describe its elements, and the step would write the memory
+    between them."""
+    if hasattr(leaf, "data_ptr") and hasattr(leaf, "numel"):
+        if hasattr(leaf, "is_contiguous") and not leaf.is_contiguous():
             raise ValueError("tikun_b200 steps contiguous tensors only; got a strided view of "
-                             f"shape {tuple(tensor.shape)}")
-        return tensor.data_ptr(), tensor.numel()
-    if isinstance(tensor, np.ndarray):
-        if not tensor.flags.c_contiguous:
+                             f"shape {tuple(leaf.shape)}")
+        return leaf.data_ptr(), leaf.numel()
+    if isinstance(leaf, np.ndarray) or hasattr(leaf, "__array__"):
+        arr = leaf if isinstance(leaf, np.ndarray) else np.asarray(leaf)
+        if not arr.flags.c_contiguous:
             raise ValueError("tikun_b200 steps contiguous arrays only; got a strided view of "
-                             f"shape {tensor.shape}")
-        return tensor.ctypes.data, tensor.size
-    if hasattr(tensor, "__array__"):
-        arr = np.asarray(tensor)
+                             f"shape {arr.shape}")
         return arr.ctypes.data, arr.size
-    if isinstance(tensor, (tuple, list)) and len(tensor) == 2 and isinstance(tensor[0], int):
-        return int(tensor[0]), int(tensor[1])
-    raise TypeError(f"Unsupported tensor type: {type(tensor)}. Must be PyTorch, JAX, NumPy, or (ptr, len).")
+    if isinstance(leaf, (tuple, list)) and len(leaf) == 2 and isinstance(leaf[0], int):
+        return int(leaf[0]), int(leaf[1])
+    raise TypeError(f"cannot step a leaf of type {type(leaf).__name__}: expected a PyTorch "
+                    "tensor, a JAX or NumPy array, or an (address, length) pair")
 
 
-def _flatten_pytree(container) -> list:
-    """universal.py:37-59."""
-    if isinstance(container, dict):
-        items = []
-        for v in container.values():
-            items.extend(_flatten_pytree(v))
-        return items
-    if isinstance(container, (list, tuple)):
-        if len(container) == 2 and isinstance(container[0], int) and isinstance(container[1], int):
-            return [container]
-        items = []
-        for item in container:
-            items.extend(_flatten_pytree(item))
-        return items
-    if hasattr(container, "__iter__") and not hasattr(container, "data_ptr") and not isinstance(
-            container, (str, bytes, np.ndarray)):
-        items = []
-        for item in container:
-            items.extend(_flatten_pytree(item))
-        return items
-    return [container]
+# the reference's names for the two helpers (its MuonND imports them from here)
+_extract_pointer_and_len = leaf_address
+_flatten_pytree = flatten_leaves
 
 
 def _tk_dtype(t) -> int:
