@@ -48,9 +48,11 @@ enum {
 /* element types */
 enum { TK_F32 = 0, TK_BF16 = 1, TK_F16 = 2 };
 
-/* pointwise optimizers: the reference's PointwiseOp
- * (crates/tikun-core/src/ir.rs:74-97; CustomDAG is not executed) */
-enum { TK_ADAMW = 0, TK_LION = 1, TK_SGD = 2 };
+/* pointwise optimizers: the reference's PointwiseOp (crates/tikun-core/src/ir.rs:74-97).
+ * TK_CUSTOM is PointwiseOp::CustomDAG, which the reference executes as one fixed
+ * rule whatever its primitives (crates/tikun-cpu/src/lib.rs:429-440):
+ * m = 0.9 m + 0.1 g;  p -= 1e-3 m  (g clip-scaled; hparams and v unused). */
+enum { TK_ADAMW = 0, TK_LION = 1, TK_SGD = 2, TK_CUSTOM = 3 };
 
 /* schedule roles: WorkloadRole (crates/tikun-core/src/ir.rs:5-12) */
 enum { TK_ROLE_LOAD = 0, TK_ROLE_COMPUTE = 1, TK_ROLE_STORE = 2 };
@@ -132,6 +134,22 @@ TK_API int tk_layout_from_shapes(const uint64_t* num_elements, size_t n_leaves,
 TK_API int tk_step_two_tier(const tk_pipeline* pipeline, const tk_leaf* leaves, size_t n_leaves,
                      int32_t kind, const tk_hparams* hp, uint64_t step,
                      float* clip_scale_out, void* stream);
+
+/* CpuLowering::step_arena (crates/tikun-cpu/src/lib.rs:39-65): the two-tier
+ * step over the slots of four f32 arenas (MemoryArena, crates/tikun-core/src/
+ * arena.rs:69-103): slot i is slot_elems[i] elements at byte offset
+ * slot_offsets[i] of every arena (tk_layout_from_shapes gives the reference's
+ * 64-byte-aligned offsets).  Each arena holds arena_bytes bytes; a slot that
+ * does not fit, or an offset that is not a multiple of 4, is TK_ERR_INVALID.
+ * The padding between slots is not touched.  m2_arena may be NULL unless kind
+ * is TK_ADAMW.  Verifies the pipeline, then runs as tk_step_two_tier over the
+ * slots (device or host arenas); *clip_scale_out (host, may be NULL) receives
+ * the scale and the call returns after it is known. */
+TK_API int tk_step_arena(const tk_pipeline* pipeline, float* params_arena,
+                         const float* grads_arena, float* m1_arena, float* m2_arena,
+                         uint64_t arena_bytes, const uint64_t* slot_offsets,
+                         const uint64_t* slot_elems, size_t n_slots, int32_t kind,
+                         const tk_hparams* hp, uint64_t step, float* clip_scale_out, void* stream);
 
 /* step_fast_buffers (crates/tikun-py/src/lib.rs:155-222): builds the
  * reference's three-node pipeline (load_g / fma_opt / store_p, vector width 8)

@@ -36,7 +36,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "_build", "libtikun_oracle.so")
 _lib = None
 
-ADAMW, LION, SGD = 0, 1, 2
+ADAMW, LION, SGD, CUSTOM = 0, 1, 2, 3
 F32, BF16 = 0, 1
 
 

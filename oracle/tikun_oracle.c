@@ -5,7 +5,8 @@
  *   - Tier 1 global L2 norm and clip scale: crates/tikun-cpu/src/lib.rs:79-125
  *     (x86 branch: f64 scalar accumulation per leaf, :106-113).
  *   - Tier 2 pointwise AdamW / Lion / SGD: lib.rs:144-272 (x86 scalar update
- *     :258-270), :274-359 (scalar :347-358), :361-428 (scalar :419-427).
+ *     :258-270), :274-359 (scalar :347-358), :361-428 (scalar :419-427), and
+ *     the CustomDAG fallback rule :429-440.
  *   - Bias corrections: lib.rs:152-154 (f32 powi of a clamped step).
  *   - Newton-Schulz polar step: crates/tikun-cpu/src/tensor_engine.rs:12-77,
  *     non-macOS GEMM loops :130-142 (gemm_fast) and :177-190 (gemm_trans).
@@ -109,6 +110,18 @@ void tko_pointwise_leaf(const tko_leaf* leaf, int32_t kind, const tko_hparams* h
       p = p - lr * (sign_c + decay * p);
       store_elem(leaf->p, i, leaf->p_dtype, p);
       m1[i] = b2 * m + (1.0f - b2) * g;
+    }
+    return;
+  }
+  if (kind == TKO_CUSTOM) {
+    /* lib.rs:429-440: PointwiseOp::CustomDAG runs one fixed rule whatever its
+     * primitives; the hyperparameters and m2 are not read */
+    for (uint64_t i = 0; i < n; ++i) {
+      float g = load_elem(leaf->g, i, leaf->g_dtype) * clip_scale;
+      m1[i] = 0.9f * m1[i] + 0.1f * g;
+      float p = load_elem(leaf->p, i, leaf->p_dtype);
+      p = p - 1e-3f * m1[i];
+      store_elem(leaf->p, i, leaf->p_dtype, p);
     }
     return;
   }

@@ -25,7 +25,7 @@ extern "C" {
 #endif
 
 enum { TKO_F32 = 0, TKO_BF16 = 1 };
-enum { TKO_ADAMW = 0, TKO_LION = 1, TKO_SGD = 2 };
+enum { TKO_ADAMW = 0, TKO_LION = 1, TKO_SGD = 2, TKO_CUSTOM = 3 };
 
 /* One leaf of the step: the reference's TensorBuffer
  * (crates/tikun-cpu/src/lib.rs:25-32) plus element types for p and g.

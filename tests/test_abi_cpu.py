@@ -194,6 +194,21 @@ def test_argument_checks_need_no_device():
          _native.TK_ERR_INVALID, "null argument"),
         (lambda: L.tk_stream_wait_deadline(None, -1, None),
          _native.TK_ERR_INVALID, "negative timeout"),
+        (lambda: L.tk_step_arena(None, ctypes.c_void_p(256), ctypes.c_void_p(256),
+                                 ctypes.c_void_p(256), None, 1024, (ctypes.c_uint64 * 1)(0),
+                                 (ctypes.c_uint64 * 1)(16), 1, _native.TK_ADAMW,
+                                 ctypes.byref(hp), 1, None, None),
+         _native.TK_ERR_INVALID, "null arena"),
+        (lambda: L.tk_step_arena(None, ctypes.c_void_p(256), ctypes.c_void_p(256),
+                                 ctypes.c_void_p(256), ctypes.c_void_p(256), 1024,
+                                 (ctypes.c_uint64 * 1)(66), (ctypes.c_uint64 * 1)(4), 1,
+                                 _native.TK_ADAMW, ctypes.byref(hp), 1, None, None),
+         _native.TK_ERR_INVALID, "not a multiple of 4"),
+        (lambda: L.tk_step_arena(None, ctypes.c_void_p(256), ctypes.c_void_p(256),
+                                 ctypes.c_void_p(256), None, 1024,
+                                 (ctypes.c_uint64 * 2)(0, 960), (ctypes.c_uint64 * 2)(16, 17), 2,
+                                 _native.TK_LION, ctypes.byref(hp), 1, None, None),
+         _native.TK_ERR_INVALID, "does not fit an arena of 1024 bytes"),
     ]
     for call, code, text in cases:
         status, msg = _err(call())

@@ -5,8 +5,9 @@ AdamW (against torch, to 1e-5); Lion and SGD-momentum rest on the restatement,
 so two restatements written apart from each other must agree exactly.
 
 Sources: AdamW crates/tikun-cpu/src/lib.rs:152-154 and :258-270, Lion
-:347-358, SGD with momentum :419-427; clip scale :117-122; momentum is the b1
-argument (crates/tikun-py/src/lib.rs:201-205).
+:347-358, SGD with momentum :419-427, the CustomDAG fallback rule :429-440;
+clip scale :117-122; momentum is the b1 argument
+(crates/tikun-py/src/lib.rs:201-205).
 """
 import numpy as np
 import pytest
@@ -60,6 +61,12 @@ def sgd(p, g, m, lr, mom, decay, scale):
     p[:] = p - lr * (m + decay * p)
 
 
+def custom_dag(p, g, m, scale):
+    g = g * F(scale)
+    m[:] = F(0.9) * m + F(0.1) * g
+    p[:] = p - F(1e-3) * m
+
+
 def inputs(n, seed):
     rng = np.random.default_rng(seed)
     p = (rng.standard_normal(n) * 0.02).astype(F)
@@ -71,16 +78,17 @@ def inputs(n, seed):
     return p, g
 
 
-@pytest.mark.parametrize("kind", ["adamw", "lion", "sgd"])
+@pytest.mark.parametrize("kind", ["adamw", "lion", "sgd", "custom"])
 @pytest.mark.parametrize("scale", [1.0, 0.00897, 0.5])
 def test_two_restatements_agree_bit_for_bit(kind, scale):
     n = 4099
-    p, g = inputs(n, {"adamw": 1, "lion": 2, "sgd": 3}[kind])
+    p, g = inputs(n, {"adamw": 1, "lion": 2, "sgd": 3, "custom": 4}[kind])
     m = np.zeros(n, F)
     v = np.zeros(n, F)
     pc, mc, vc = p.copy(), m.copy(), v.copy()
     hp = dict(lr=1e-3, b1=0.9, b2=0.999 if kind != "lion" else 0.99, eps=1e-8, decay=0.01)
-    code = {"adamw": oracle.ADAMW, "lion": oracle.LION, "sgd": oracle.SGD}[kind]
+    code = {"adamw": oracle.ADAMW, "lion": oracle.LION, "sgd": oracle.SGD,
+            "custom": oracle.CUSTOM}[kind]
     for step in range(1, 6):
         gs = (g * F(1.0 + 0.1 * step)).astype(F)
         oracle.pointwise_leaf(pc, gs, mc, vc if kind == "adamw" else None, code, hp["lr"],
@@ -89,8 +97,10 @@ def test_two_restatements_agree_bit_for_bit(kind, scale):
             adamw(p, gs, m, v, hp["lr"], hp["b1"], hp["b2"], hp["eps"], hp["decay"], step, scale)
         elif kind == "lion":
             lion(p, gs, m, hp["lr"], hp["b1"], hp["b2"], hp["decay"], scale)
-        else:
+        elif kind == "sgd":
             sgd(p, gs, m, hp["lr"], hp["b1"], hp["decay"], scale)
+        else:
+            custom_dag(p, gs, m, scale)
         for a, b, name in ((pc, p, "p"), (mc, m, "m")) + (((vc, v, "v"),) if kind == "adamw" else ()):
             assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (kind, step, name)
 

@@ -468,3 +468,147 @@ def test_framework_agnostic_frontends_match_oracle():
         opt.step(grads=[(g.ctypes.data, 500)])
         oracle_step(opt, [rp], [g], [rm1], [rm2])
     assert_bitexact(p, rp, "raw/adamw")
+
+
+# -- CustomDAG fallback rule and the arena-resident step ----------------------
+def test_custom_dag_fallback_rule_matches_oracle():
+    """PointwiseOp::CustomDAG (crates/tikun-cpu/src/lib.rs:429-440): the
+    reference runs one fixed rule, m = 0.9 m + 0.1 g; p -= 1e-3 m, with g
+    clip-scaled; bit-identical to the oracle over 5 clipped steps, mixed
+    dtypes and ragged sizes, the second-moment buffers not passed."""
+    sizes = [1, 3, 17, 4097, 65541, 0, 777]
+    pdt = [torch.float32, torch.bfloat16, torch.float32, torch.bfloat16, torch.float32,
+           torch.float32, torch.bfloat16]
+    L = Leaves(sizes, pdt, pdt, seed=31)
+    hp = _native.TkHParams(1e-3, 0.9, 0.999, 1e-8, 0.01)
+    for step in range(1, 6):
+        L.new_grads(0.05)
+        leaves, n = _native.make_leaves(
+            [t.data_ptr() for t in L.p], [t.data_ptr() for t in L.g], [t.data_ptr() for t in L.m],
+            [], [t.numel() for t in L.p], [_native.TK_BF16 if t.dtype == torch.bfloat16 else
+                                           _native.TK_F32 for t in L.p],
+            [_native.TK_BF16 if t.dtype == torch.bfloat16 else _native.TK_F32 for t in L.g])
+        out = ctypes.c_float()
+        _native.check(_native.lib().tk_step_buffers(leaves, n, _native.TK_CUSTOM,
+                                                    ctypes.byref(hp), step, 0.5,
+                                                    ctypes.byref(out), None))
+        ref = oracle.step_two_tier(L.np_p, L.np_g, L.np_m, [None] * len(sizes), oracle.CUSTOM,
+                                   1e-3, 0.9, 0.999, 1e-8, 0.01, step, 0.5)
+        assert out.value == ref
+    for i in range(len(sizes)):
+        assert_bitexact(to_np(L.p[i]), L.np_p[i], f"custom leaf {i} p")
+        assert_bitexact(to_np(L.m[i]), L.np_m[i], f"custom leaf {i} m")
+
+
+@pytest.mark.parametrize("kind", ["adamw", "lion"])
+def test_step_arena_matches_oracle_and_leaves_padding_alone(kind):
+    """CpuLowering::step_arena (crates/tikun-cpu/src/lib.rs:39-65) through
+    tk_step_arena: four flat f32 device arenas at LayoutPlan::from_shapes
+    offsets, the GPT-2-small table at d=128, 3 clipped steps bit-identical to
+    the oracle stepping the same slots; the padding between slots keeps a NaN
+    sentinel (it is never touched)."""
+    from tikun_b200.arena import Arena, LayoutPlan
+
+    d = 128
+    sizes = gpt2_small_sizes(d=d, vocab=1000, ctx=256)
+    offs, total_bytes = _native.layout_from_shapes(sizes)
+    plan = LayoutPlan(sizes)
+    P, G, M, V = (Arena(plan) for _ in range(4))
+    P.flat.fill_(float("nan"))
+    init = gpt2_small_init(sizes, d)
+    for i, t in enumerate(init):
+        P.leaf(i).copy_(t)
+    np_p = [to_np(t) for t in init]
+    np_m = [np.zeros(n, np.float32) for n in sizes]
+    np_v = [np.zeros(n, np.float32) for n in sizes]
+    gen = torch.Generator().manual_seed(3)
+    hp = _native.TkHParams(1e-3, 0.9, 0.99 if kind == "lion" else 0.999, 1e-8, 0.01)
+    code = oracle.opt_kind(kind)
+    U64 = ctypes.c_uint64 * len(sizes)
+    pipe = _native.TkPipeline((_native.TkScheduleNode * 3)(
+        _native.TkScheduleNode(b"load_g", 0, 64, 4, 8, 2),
+        _native.TkScheduleNode(b"fma_opt", 1, 64, 4, 8, 2),
+        _native.TkScheduleNode(b"store_p", 2, 64, 4, 8, 2)), 3, 1.0)
+    for step in range(1, 4):
+        np_g = [(torch.randn(n, generator=gen) * 1e-2).numpy() for n in sizes]
+        for i, g in enumerate(np_g):
+            G.leaf(i).copy_(torch.from_numpy(g))
+        out = ctypes.c_float()
+        _native.check(_native.lib().tk_step_arena(
+            ctypes.byref(pipe), P.flat.data_ptr(), G.flat.data_ptr(), M.flat.data_ptr(),
+            V.flat.data_ptr(), P.flat.numel() * 4, U64(*offs), U64(*sizes), len(sizes),
+            code, ctypes.byref(hp), step, ctypes.byref(out), None))
+        ref = oracle.step_two_tier(np_p, np_g, np_m, np_v, code, 1e-3, 0.9,
+                                   0.99 if kind == "lion" else 0.999, 1e-8, 0.01, step, 1.0)
+        assert out.value == ref and ref < 1.0
+    for i in range(len(sizes)):
+        assert_bitexact(to_np(P.leaf(i)), np_p[i], f"slot {i} p")
+        assert_bitexact(to_np(M.leaf(i)), np_m[i], f"slot {i} m")
+    covered = torch.zeros(P.flat.numel(), dtype=torch.bool, device="cuda")
+    for off, n in plan.slots:
+        covered[off:off + n] = True
+    assert torch.isnan(P.flat[~covered]).all(), "padding between slots was written"
+
+
+def test_universal_optimizer_arena_mode_matches_oracle():
+    """UniversalOptimizer(arena=True): parameters and gradients become views of
+    flat device arenas, the leaf table is built once; 3 clipped AdamW steps over
+    the GPT-2-small table at d=128 are bit-identical to the oracle, and
+    zero_grad clears the gradient arena in place."""
+    import tikun_b200
+
+    d = 128
+    sizes = gpt2_small_sizes(d=d, vocab=1000, ctx=256)
+    params = [t.clone().requires_grad_(True) for t in gpt2_small_init(sizes, d)]
+    np_p = [to_np(t) for t in params]
+    np_m = [np.zeros(n, np.float32) for n in sizes]
+    np_v = [np.zeros(n, np.float32) for n in sizes]
+    opt = tikun_b200.AdamW(params, lr=1e-3, weight_decay=0.01, max_norm=1.0, arena=True)
+    base = opt._arena.params.flat.data_ptr()
+    span = opt._arena.params.flat.numel() * 4
+    assert all(base <= p.data_ptr() < base + span for p in params)
+    grad_ptrs = [p.grad.data_ptr() for p in params]
+    gen = torch.Generator().manual_seed(5)
+    for step in range(1, 4):
+        np_g = [(torch.randn(n, generator=gen) * 1e-2).numpy() for n in sizes]
+        with torch.no_grad():
+            for p, g in zip(params, np_g):
+                p.grad.copy_(torch.from_numpy(g))
+        opt.step()
+        ref = oracle.step_two_tier(np_p, np_g, np_m, np_v, oracle.ADAMW, 1e-3, 0.9, 0.999,
+                                   1e-8, 0.01, step, 1.0)
+        assert float(opt.clip_scale) == ref and ref < 1.0
+    for i, p in enumerate(params):
+        assert_bitexact(to_np(p.detach()), np_p[i], f"leaf {i} p")
+        assert_bitexact(to_np(opt.m2_state[p.data_ptr()]), np_v[i], f"leaf {i} v")
+    opt.zero_grad()
+    assert [p.grad.data_ptr() for p in params] == grad_ptrs
+    assert all(int(torch.count_nonzero(p.grad)) == 0 for p in params)
+
+
+def test_arena_mode_gradients_accumulate_into_the_arena():
+    """With the gradients as arena views, autograd accumulates into them in
+    place: a small MLP trained 3 steps with the arena front-end ends
+    bit-identical to the same model stepped by the per-leaf front-end."""
+    import tikun_b200
+
+    torch.manual_seed(0)
+    net_a = torch.nn.Sequential(torch.nn.Linear(64, 96), torch.nn.ReLU(),
+                                torch.nn.Linear(96, 10)).cuda()
+    net_b = torch.nn.Sequential(torch.nn.Linear(64, 96), torch.nn.ReLU(),
+                                torch.nn.Linear(96, 10)).cuda()
+    net_b.load_state_dict(net_a.state_dict())
+    opt_a = tikun_b200.AdamW(list(net_a.parameters()), lr=1e-2, arena=True)
+    opt_b = tikun_b200.AdamW(list(net_b.parameters()), lr=1e-2)
+    ptrs = [p.grad.data_ptr() for p in net_a.parameters()]
+    x = torch.randn(32, 64, device="cuda")
+    for _ in range(3):
+        opt_a.zero_grad()
+        opt_b.zero_grad()
+        net_a(x).square().mean().backward()
+        net_b(x).square().mean().backward()
+        assert [p.grad.data_ptr() for p in net_a.parameters()] == ptrs
+        opt_a.step()
+        opt_b.step()
+    for pa, pb in zip(net_a.parameters(), net_b.parameters()):
+        assert torch.equal(pa.detach(), pb.detach())

@@ -26,7 +26,7 @@ LIB_PATH = os.path.join(_PKG, "lib", "libtikun_cuda.so")
 # status codes, dtypes, kinds (include/tikun_cuda.h)
 TK_OK, TK_ERR_INVALID, TK_ERR_VERIFY, TK_ERR_CUDA, TK_ERR_ALLOC, TK_ERR_UNSUPPORTED, TK_ERR_DEVICE = range(7)
 TK_F32, TK_BF16, TK_F16 = 0, 1, 2
-TK_ADAMW, TK_LION, TK_SGD = 0, 1, 2
+TK_ADAMW, TK_LION, TK_SGD, TK_CUSTOM = 0, 1, 2, 3
 TK_ROLE_LOAD, TK_ROLE_COMPUTE, TK_ROLE_STORE = 0, 1, 2
 TK_NS_F16, TK_NS_BF16 = 0, 1
 
@@ -120,6 +120,9 @@ _SIGNATURES = {
                         ctypes.POINTER(_F), _P],
     "tk_step_buffers_async": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,
                               _F, _P, _P],
+    "tk_step_arena": [ctypes.POINTER(TkPipeline), _P, _P, _P, _P, _U64, ctypes.POINTER(_U64),
+                      ctypes.POINTER(_U64), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,
+                      ctypes.POINTER(_F), _P],
     "tk_grad_sumsq": [ctypes.POINTER(TkLeaf), _SZ, _P, _P],
     "tk_clip_scale": [_P, _F, _P, _P],
     "tk_apply_pointwise": [ctypes.POINTER(TkLeaf), _SZ, _I32, ctypes.POINTER(TkHParams), _U64,

@@ -222,7 +222,7 @@ static int validate_leaves(const tk_leaf* leaves, size_t n, int kind, Residency*
   *where = Residency::kNone;
   if (n == 0) return TK_OK;
   if (leaves == nullptr) return set_error(TK_ERR_INVALID, "leaves is NULL with n_leaves=%zu", n);
-  if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD)
+  if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD && kind != TK_CUSTOM)
     return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));
@@ -923,6 +923,36 @@ int tk_step_two_tier(const tk_pipeline* pipeline, const tk_leaf* leaves, size_t 
   TK_TRY(verify_pipeline(pipeline));
   return step_entry(leaves, n_leaves, kind, hp, step, pipeline->max_norm, clip_scale_out,
                     nullptr, true, static_cast<cudaStream_t>(stream));
+}
+
+int tk_step_arena(const tk_pipeline* pipeline, float* params_arena, const float* grads_arena,
+                  float* m1_arena, float* m2_arena, uint64_t arena_bytes,
+                  const uint64_t* slot_offsets, const uint64_t* slot_elems, size_t n_slots,
+                  int32_t kind, const tk_hparams* hp, uint64_t step, float* clip_scale_out,
+                  void* stream) {
+  g_last_error.clear();
+  if (n_slots > 0 && (slot_offsets == nullptr || slot_elems == nullptr))
+    return set_error(TK_ERR_INVALID, "null slot offsets or sizes");
+  if (params_arena == nullptr || grads_arena == nullptr || m1_arena == nullptr ||
+      (kind == TK_ADAMW && m2_arena == nullptr))
+    return set_error(TK_ERR_INVALID, "null arena");
+  // lib.rs:47-62: one TensorBuffer per slot, at the same byte offset in every arena
+  std::vector<tk_leaf> leaves(n_slots);
+  for (size_t i = 0; i < n_slots; ++i) {
+    const uint64_t off = slot_offsets[i], n = slot_elems[i];
+    if (off % 4 != 0)
+      return set_error(TK_ERR_INVALID, "slot %zu: byte offset %llu is not a multiple of 4", i,
+                       (unsigned long long)off);
+    if (off > arena_bytes || n > (arena_bytes - off) / 4)
+      return set_error(TK_ERR_INVALID, "slot %zu (%llu elements at byte %llu) does not fit an "
+                       "arena of %llu bytes", i, (unsigned long long)n, (unsigned long long)off,
+                       (unsigned long long)arena_bytes);
+    const uint64_t e = off / 4;
+    leaves[i] = {params_arena + e, grads_arena + e, m1_arena + e,
+                 m2_arena ? m2_arena + e : nullptr, n, TK_F32, TK_F32};
+  }
+  return tk_step_two_tier(pipeline, leaves.data(), n_slots, kind, hp, step, clip_scale_out,
+                          stream);
 }
 
 // The pipeline step_fast_buffers builds (crates/tikun-py/src/lib.rs:183-192).

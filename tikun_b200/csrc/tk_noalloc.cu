@@ -116,7 +116,7 @@ int validate(const tk_leaf* leaves, size_t n, int kind) {
                      "split the call or use tk_step_buffers",
                      kNoallocMaxLeaves, n);
   if (n > 0 && leaves == nullptr) return set_error(TK_ERR_INVALID, "leaves is NULL");
-  if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD)
+  if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD && kind != TK_CUSTOM)
     return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));

@@ -409,6 +409,7 @@ int launch_pointwise(const LeafTable& t, int kind, int p_dtype, int g_dtype,
     case TK_ADAMW: return launch_kind<TK_ADAMW>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
     case TK_LION: return launch_kind<TK_LION>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
     case TK_SGD: return launch_kind<TK_SGD>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
+    case TK_CUSTOM: return launch_kind<TK_CUSTOM>(t, p_dtype, g_dtype, c, partials, n_partials, max_norm, scale_dev, scale_out, s, pr);
     default: return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   }
 }

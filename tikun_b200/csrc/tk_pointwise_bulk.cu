@@ -300,6 +300,7 @@ int launch_pointwise_bulk(const LeafTable& t, int kind, const PointwiseConsts& c
     case TK_ADAMW: return launch_bulk_kind<TK_ADAMW>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
     case TK_LION: return launch_bulk_kind<TK_LION>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
     case TK_SGD: return launch_bulk_kind<TK_SGD>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
+    case TK_CUSTOM: return launch_bulk_kind<TK_CUSTOM>(t, c, partials, n_partials, max_norm, scale_dev, scale_out, s);
     default: return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   }
 }

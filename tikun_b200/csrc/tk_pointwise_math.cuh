@@ -51,12 +51,20 @@ __device__ __forceinline__ void sgd(float& p, float g, float& m, const Pointwise
   p = __fsub_rn(p, __fmul_rn(k.lr, update));
 }
 
+// PointwiseOp::CustomDAG, lib.rs:429-440: one fixed rule, whatever the
+// primitives: m = 0.9 m + 0.1 g; p -= 1e-3 m (f32 literals).
+__device__ __forceinline__ void custom_dag(float& p, float g, float& m) {
+  m = __fadd_rn(__fmul_rn(0.9f, m), __fmul_rn(0.1f, g));
+  p = __fsub_rn(p, __fmul_rn(1e-3f, m));
+}
+
 template <int KIND>
 __device__ __forceinline__ void apply(float& p, float g, float& m, float& v,
                                       const PointwiseConsts& k) {
   if constexpr (KIND == TK_ADAMW) adamw(p, g, m, v, k);
   else if constexpr (KIND == TK_LION) lion(p, g, m, k);
-  else sgd(p, g, m, k);
+  else if constexpr (KIND == TK_SGD) sgd(p, g, m, k);
+  else custom_dag(p, g, m);
 }
 
 // ------------------------------------------------------------------ reductions

@@ -258,7 +258,7 @@ int tk_shard_init(void* nccl_comm, float* p_arena, const float* g_arena, uint64_
     return set_error(TK_ERR_INVALID, "null communicator or arena");
   if (n_leaves > 0 && (leaf_offsets == nullptr || leaf_sizes == nullptr))
     return set_error(TK_ERR_INVALID, "null leaf offsets or sizes");
-  if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD)
+  if (kind != TK_ADAMW && kind != TK_LION && kind != TK_SGD && kind != TK_CUSTOM)
     return set_error(TK_ERR_INVALID, "unknown optimizer kind %d", kind);
   if (exchange != TK_SHARD_ALLGATHER && exchange != TK_SHARD_PEERS && exchange != TK_SHARD_COPY)
     return set_error(TK_ERR_INVALID, "unknown exchange mode %d", exchange);

@@ -15,6 +15,15 @@ Differences, all on the device side:
   nearest even on store); moments are f32.
 * NumPy arrays and raw host ``(ptr, len)`` pairs step synchronously through the
   same C ABI, staged through device memory.
+* ``arena=True`` (CUDA tensors of one dtype on one device) moves the
+  parameters, their gradients and the moments into four flat device arenas
+  laid out by LayoutPlan::from_shapes (the reference's MemoryArena and
+  CpuLowering::step_arena, crates/tikun-core/src/arena.rs:34-103,
+  crates/tikun-cpu/src/lib.rs:39-65): each parameter's ``.data`` and ``.grad``
+  become views of their arenas, so autograd accumulates into the gradient
+  arena, the leaf table is built once and every ``step()`` is one launch
+  sequence over it, and ``zero_grad()`` clears the gradient arena in place
+  (the gradients stay views, where the reference sets them to None).
 """
 from __future__ import annotations
 
@@ -107,7 +116,7 @@ class UniversalOptimizer:
 
     def __init__(self, params, algorithm: str = "adamw", lr: float = 1e-3, beta1: float = 0.9,
                  beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.01,
-                 max_norm: float = 0.0, in_backward: bool = False):
+                 max_norm: float = 0.0, in_backward: bool = False, arena: bool = False):
         self.params = _flatten_pytree(params)
         self.algorithm = algorithm.lower()
         self.lr = lr
@@ -121,6 +130,15 @@ class UniversalOptimizer:
         self.m1_state: dict[int, Any] = {}
         self.m2_state: dict[int, Any] = {}
         self.clip_scale = None  # device f32 tensor (CUDA params) or float (host params)
+        self._arena = None
+        if arena:
+            if in_backward:
+                raise ValueError("arena mode steps every leaf at once; in_backward steps them "
+                                 "one by one")
+            self._arena = _ArenaState(self.params)
+            for p, (m1, m2) in zip(self.params, self._arena.moments()):
+                ptr, _ = _extract_pointer_and_len(p)
+                self.m1_state[ptr], self.m2_state[ptr] = m1, m2
         if self.in_backward:
             self._hooks = []
             for p in self.params:
@@ -186,6 +204,9 @@ class UniversalOptimizer:
         self.step_count += 1
         if self.in_backward:
             return
+        if self._arena is not None:
+            self._arena.step(self, grads)
+            return
         p_ptrs, g_ptrs, m1_ptrs, m2_ptrs, lengths, p_dt, g_dt = [], [], [], [], [], [], []
         flat_grads = _flatten_pytree(grads) if grads is not None else None
         cuda_flags = []
@@ -217,6 +238,9 @@ class UniversalOptimizer:
                    on_device, device)
 
     def zero_grad(self):
+        if self._arena is not None:  # the gradients stay views of the arena
+            self._arena.grads.flat.zero_()
+            return
         for p in self.params:
             if hasattr(p, "grad") and p.grad is not None:
                 p.grad = None
@@ -278,3 +302,71 @@ class UniversalOptimizer:
     def to_mlir(self) -> str:
         raise NotImplementedError("the MLIR text emitter (crates/tikun-core/src/mlir.rs) is "
                                   "not part of the B200 lowering; see to_json()")
+
+
+class _ArenaState:
+    """Four flat device arenas (p and g in the parameters' dtype, m1 and m2 in
+    f32) at LayoutPlan offsets, the parameters and gradients re-pointed into
+    them, and the leaf table of the C ABI built once."""
+
+    def __init__(self, params):
+        import torch
+
+        from .arena import Arena, LayoutPlan
+
+        if not params:
+            raise ValueError("arena mode needs at least one parameter")
+        dtypes = {p.dtype for p in params if isinstance(p, torch.Tensor)}
+        devices = {p.device for p in params if isinstance(p, torch.Tensor)}
+        if (len(dtypes) != 1 or len(devices) != 1 or
+                not all(isinstance(p, torch.Tensor) and p.is_cuda for p in params)):
+            raise ValueError("arena mode takes CUDA tensors of one dtype on one device")
+        dtype, self.device = dtypes.pop(), devices.pop()
+        if dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError(f"arena leaves are float32 or bfloat16, got {dtype}")
+        for p in params:
+            leaf_address(p)  # contiguous only
+        self.plan = LayoutPlan([p.numel() for p in params])
+        self.params = Arena(self.plan, dtype=dtype, device=self.device)
+        self.grads = Arena(self.plan, dtype=dtype, device=self.device)
+        self.m1 = Arena(self.plan, device=self.device)
+        self.m2 = Arena(self.plan, device=self.device)
+        with torch.no_grad():
+            for i, p in enumerate(params):
+                view = self.params.leaf(i).view(p.shape)
+                view.copy_(p)
+                gview = self.grads.leaf(i).view(p.shape)
+                if p.grad is not None:
+                    gview.copy_(p.grad)
+                p.data = view
+                p.grad = gview
+        dt = _tk_dtype(params[0])
+        n = len(params)
+        self.leaves, self.n = _native.make_leaves(
+            self.params.ptrs(), self.grads.ptrs(), self.m1.ptrs(), self.m2.ptrs(),
+            [p.numel() for p in params], [dt] * n, [dt] * n)
+        self.scale = torch.ones((), dtype=torch.float32, device=self.device)
+        self.n_params = n
+
+    def moments(self):
+        return [(self.m1.leaf(i), self.m2.leaf(i)) for i in range(self.n_params)]
+
+    def step(self, opt, grads=None):
+        import ctypes
+
+        import torch
+
+        if grads is not None:  # explicit gradients: copied into the arena first
+            flat = flatten_leaves(grads)
+            if len(flat) != self.n_params:
+                raise ValueError(f"{len(flat)} gradients for {self.n_params} parameters")
+            with torch.no_grad():
+                for i, g in enumerate(flat):
+                    self.grads.leaf(i).copy_(torch.as_tensor(g, device=self.device).reshape(-1))
+        hp = _native.TkHParams(opt.lr, opt.beta1, opt.beta2, opt.eps, opt.weight_decay)
+        with torch.cuda.device(self.device):
+            _native.check(_native.lib().tk_step_buffers_async(
+                self.leaves, self.n, _native.opt_kind(opt.algorithm), ctypes.byref(hp),
+                opt.step_count, opt.max_norm if opt.max_norm > 0 else 0.0,
+                self.scale.data_ptr(), torch.cuda.current_stream().cuda_stream))
+        opt.clip_scale = self.scale
