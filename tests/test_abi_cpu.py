@@ -234,3 +234,21 @@ def test_muon_frontend_rejects_strided_parameters_before_any_launch():
     opt = Muon([p], lr=0.02)
     with pytest.raises(ValueError, match="contiguous"):
         opt.step()
+
+
+def test_torch_optimizer_adamw_shape_needs_no_device():
+    """tikun_b200.optimizer.AdamW keeps the reference's torch.optim.Optimizer
+    shape (python/tikun/optimizer.py:17-117): param_groups defaults under the
+    reference's keys, and a missing gradient raises before any native call."""
+    import torch
+
+    from tikun_b200.optimizer import AdamW
+
+    w = torch.nn.Parameter(torch.zeros(3, 4))
+    opt = AdamW([w], lr=2e-3, betas=(0.8, 0.99), eps=1e-7, weight_decay=0.1, max_norm=1.0)
+    g = opt.param_groups[0]
+    assert (g["lr"], g["beta_one"], g["beta_two"], g["eps"], g["weight_decay"], g["max_norm"]) == \
+        (2e-3, 0.8, 0.99, 1e-7, 0.1, 1.0)
+    assert isinstance(opt, torch.optim.Optimizer) and opt.step_count == 0
+    with pytest.raises(RuntimeError, match=r"Gradient for parameter with shape torch.Size\(\[3, 4\]\) is None."):
+        opt.step()
