@@ -764,7 +764,9 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
             [_native.TK_BF16] * len(seg_list))
 
     hp = _native.TkHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"])
-    mhp = _native.TkMuonHParams(MUON_HP["lr"], MUON_HP["momentum"], 1, 5, _native.TK_NS_F16)
+    ns_prec = {"f16": _native.TK_NS_F16, "bf16": _native.TK_NS_BF16,
+               "f16x3": _native.TK_NS_F16X3}[args.ns_precision]
+    mhp = _native.TkMuonHParams(MUON_HP["lr"], MUON_HP["momentum"], 1, 5, ns_prec)
 
     def mu_leaves(idx):
         arr = (_native.TkMuonLeaf * max(len(idx), 1))()
@@ -784,7 +786,8 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         # NVLink, otherwise all-gathers follow them
         from tikun_b200.distributed import MuonShard, PeerArena
 
-        ms = MuonShard(mats, bf, dev, MUON_HP["lr"], MUON_HP["momentum"], exchange=exchange)
+        ms = MuonShard(mats, bf, dev, MUON_HP["lr"], MUON_HP["momentum"], precision=ns_prec,
+                       exchange=exchange)
         ms.params.normal_(0, 0.02, generator=gen)
         mine = ms.mine
         if not wl["inbackward"]:
@@ -972,7 +975,10 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
                "sample": f"3 timed samples after 1 warm-up, each: {csample} "
                          f"({cms:.0f} ms per full step, extrapolated)"}
     return {
-        "value": value, "ms_per_step": ms_step, "dtype": "bf16 params, f16 tensor-core operands",
+        "value": value, "ms_per_step": ms_step,
+        "dtype": "bf16 params, " + {"f16": "f16", "bf16": "bf16",
+                                    "f16x3": "split f16 (hi+lo)"}[args.ns_precision] +
+                 " tensor-core operands",
         "scaling": "strong",
         "data": "synthetic (seeded N(0,0.02) bf16 params, N(0,1e-3) bf16 grads)",
         "config": muon_config(args.workload, wl),
@@ -1006,6 +1012,10 @@ def main():
     ap.add_argument("--workload", default="muon-llama3-8b", choices=sorted(WORKLOADS) + sorted(MUON))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ns-precision", default="f16", choices=["f16", "bf16", "f16x3"],
+                    help="Newton-Schulz operands for the Muon workloads: f16 (default), bf16, or "
+                         "split f16 pairs (three times the tensor-core work, Newton-Schulz "
+                         "within a few 1e-6 of f32)")
     ap.add_argument("--zero", default="auto", choices=["auto", "fused", "copy", "allgather"],
                     help="multi-GPU exchange of updated parameters: peer stores from the update "
                          "kernel (fused), copies beside the next batch's work (copy: the copy "

@@ -57,8 +57,16 @@ enum { TK_ADAMW = 0, TK_LION = 1, TK_SGD = 2, TK_CUSTOM = 3 };
 /* schedule roles: WorkloadRole (crates/tikun-core/src/ir.rs:5-12) */
 enum { TK_ROLE_LOAD = 0, TK_ROLE_COMPUTE = 1, TK_ROLE_STORE = 2 };
 
-/* Newton-Schulz tensor-core operand type (accumulation is always f32) */
-enum { TK_NS_F16 = 0, TK_NS_BF16 = 1 };
+/* Newton-Schulz tensor-core operands (accumulation is always f32):
+ *   TK_NS_F16    f16 operands (the default);
+ *   TK_NS_BF16   bf16 operands;
+ *   TK_NS_F16X3  every operand value v held as an f16 pair, hi = f16(v) and
+ *                lo = f16(v - hi), each product formed as hi*hi + hi*lo + lo*hi:
+ *                about 22 significant bits at three times the tensor-core work
+ *                and twice the scratch; Newton-Schulz within a few 1e-6 of f32
+ *                (for callers whose parameters are stored in bf16 and must stay
+ *                within 1e-3 of the f32 result over many steps). */
+enum { TK_NS_F16 = 0, TK_NS_BF16 = 1, TK_NS_F16X3 = 2 };
 
 /* One schedule node: ScheduleIRNode (crates/tikun-core/src/ir.rs:16-36). */
 typedef struct {

@@ -3,9 +3,16 @@
 Bars (stated here, used below):
 * NS output: relative Frobenius error against the oracle's f32 Newton-Schulz
   (tensor_engine.rs:12-77) <= 2e-2 with bf16 operands; with f16 operands
-  (the engine's default) the tests hold it to 5e-3.
+  (the engine's default) the tests hold it to 5e-3, and with split f16
+  operands (TK_NS_F16X3) to 1e-4.
 * Muon parameters after 10 steps: relative Frobenius error <= 1e-3 for f32
-  parameters (f16 operands).
+  parameters (f16 operands) and for bf16 parameters with split f16 operands.
+  bf16 parameters with the default f16 operands end 1.1e-3 to 3.0e-3 from
+  the oracle (measured on a B200): an f16 Newton-Schulz output 0.2 % from the
+  f32 one moves p + alpha*O across a bf16 rounding boundary for a sixth to a
+  tenth of the parameters, each then one bf16 ulp (2^-8 to 2^-7 relative)
+  away; tests/test_ns_rounding_model_cpu.py reproduces the 768^2 and
+  768x3072 figures to three digits.  Those cases are held to 3e-3.
 * The momentum buffer is element-wise f32 arithmetic: bit-identical.
 """
 import os
@@ -20,8 +27,9 @@ from tikun_b200 import _native
 
 pytestmark = pytest.mark.gpu
 
-NS_TOL = {_native.TK_NS_F16: 5e-3, _native.TK_NS_BF16: 2e-2}
-PRECISIONS = [pytest.param(_native.TK_NS_F16, id="f16"), pytest.param(_native.TK_NS_BF16, id="bf16")]
+NS_TOL = {_native.TK_NS_F16: 5e-3, _native.TK_NS_BF16: 2e-2, _native.TK_NS_F16X3: 1e-4}
+PRECISIONS = [pytest.param(_native.TK_NS_F16, id="f16"), pytest.param(_native.TK_NS_BF16, id="bf16"),
+              pytest.param(_native.TK_NS_F16X3, id="f16x3")]
 
 
 def relf(a, b):
@@ -80,7 +88,8 @@ def test_ns_2d_matches_oracle(shape, prec):
     _native.newton_schulz_2d_ffi(t.data_ptr(), r, c, 5, precision=prec)
     err = relf(to_np(t), ref)
     print(f"{r}x{c} relative Frobenius error {err:.3e}")
-    assert err <= (NS_TOL[prec] if min(r, c) > 1 else VECTOR_NS_TOL)
+    vector_tol = NS_TOL[prec] if prec == _native.TK_NS_F16X3 else VECTOR_NS_TOL
+    assert err <= (NS_TOL[prec] if min(r, c) > 1 else vector_tol)
 
 
 @pytest.mark.parametrize("prec", PRECISIONS)
@@ -178,8 +187,10 @@ def _muon_oracle_step(p, buf, g, lr, mu, rows, cols, heads, p_bf16):
 
 @pytest.mark.parametrize("rows,cols,heads", [(768, 768, 1), (768, 3072, 1), (3072, 768, 1),
                                              (96, 40, 1), (16, 24, 3), (1, 512, 1)])
-@pytest.mark.parametrize("p_bf16", [False, True], ids=["p_f32", "p_bf16"])
-def test_muon_step_ten_steps(rows, cols, heads, p_bf16):
+@pytest.mark.parametrize("p_bf16,prec", [(False, _native.TK_NS_F16), (True, _native.TK_NS_F16),
+                                         (True, _native.TK_NS_F16X3)],
+                         ids=["p_f32", "p_bf16", "p_bf16-f16x3"])
+def test_muon_step_ten_steps(rows, cols, heads, p_bf16, prec):
     shape = (heads, rows, cols) if heads > 1 else (rows, cols)
     rng = np.random.default_rng(rows + cols + heads)
     p0 = (rng.standard_normal(shape) * 0.02).astype(np.float32)
@@ -198,7 +209,7 @@ def test_muon_step_ten_steps(rows, cols, heads, p_bf16):
         prev = p.float().clone()
         _native.muon_step([(p.data_ptr(), gt.data_ptr(), mom.data_ptr(), heads, rows, cols,
                             _native.TK_BF16 if p_bf16 else _native.TK_F32, _native.TK_F32)],
-                          lr, mu, nesterov=True, ns_steps=5)
+                          lr, mu, nesterov=True, ns_steps=5, precision=prec)
         p_ref, o_ref = _muon_oracle_step(p_ref, buf_ref, g, lr, mu, rows, cols, heads, p_bf16)
         if step == 0:
             assert_bitexact(to_np(mom), buf_ref, "momentum")
@@ -214,7 +225,10 @@ def test_muon_step_ten_steps(rows, cols, heads, p_bf16):
     ref = oracle.bf16_to_f32(p_ref) if p_bf16 else p_ref
     err = relf(got, ref)
     print(f"params rel Frobenius after 10 steps: {err:.3e}")
-    assert err <= (1e-3 if not p_bf16 else 3e-3), err
+    # the BASELINE bar (1e-3) except bf16 parameters with f16 operands (see the
+    # module docstring for the measured figures and their cause)
+    bar = 3e-3 if (p_bf16 and prec == _native.TK_NS_F16) else 1e-3
+    assert err <= bar, err
 
 
 @pytest.mark.parametrize("pinned", [True, False], ids=["pinned", "pageable"])
@@ -346,10 +360,18 @@ def _torch_fp32_ns(G: torch.Tensor, steps: int = 5) -> torch.Tensor:
     return X.T if tall else X
 
 
-@pytest.mark.parametrize("shape", [(4096, 14336), (14336, 4096), (4096, 4096), (4096, 1024),
-                                   (2048, 2048), (2048, 8192), (8192, 2048)],
-                         ids=lambda s: f"{s[0]}x{s[1]}")
-def test_ns_full_model_shapes_against_torch_fp32(shape):
+@pytest.mark.parametrize("shape,prec", [((4096, 14336), _native.TK_NS_F16),
+                                        ((14336, 4096), _native.TK_NS_F16),
+                                        ((4096, 4096), _native.TK_NS_F16),
+                                        ((4096, 1024), _native.TK_NS_F16),
+                                        ((2048, 2048), _native.TK_NS_F16),
+                                        ((2048, 8192), _native.TK_NS_F16),
+                                        ((8192, 2048), _native.TK_NS_F16),
+                                        ((4096, 1024), _native.TK_NS_F16X3),
+                                        ((2048, 2048), _native.TK_NS_F16X3)],
+                         ids=lambda v: f"{v[0]}x{v[1]}" if isinstance(v, tuple) else
+                         {0: "f16", 2: "f16x3"}[v])
+def test_ns_full_model_shapes_against_torch_fp32(shape, prec):
     """The matrix shapes of the 8B workload (4096^2, 4096x1024, 4096x14336 and
     its transpose) and of the 1.3B workload (2048^2, 2048x8192, 8192x2048) at
     full size, where the oracle's CPU loops would take minutes: the engine's
@@ -362,10 +384,11 @@ def test_ns_full_model_shapes_against_torch_fp32(shape):
         G = torch.randn(*shape, device="cuda", generator=g) * 1e-3
         want = _torch_fp32_ns(G)
         X = G.clone()
-        _native.newton_schulz_2d_ffi(X.data_ptr(), shape[0], shape[1], 5)
+        _native.newton_schulz_2d_ffi(X.data_ptr(), shape[0], shape[1], 5, precision=prec)
         torch.cuda.synchronize()
         err = float((X - want).norm() / want.norm())
-        assert err <= NS_TOL[_native.TK_NS_F16], err
+        print(f"{shape} relative Frobenius error {err:.3e}")
+        assert err <= NS_TOL[prec], err
         assert _native.device_status() == 0
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev

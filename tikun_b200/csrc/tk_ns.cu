@@ -89,6 +89,7 @@ struct GemmArgs {
   int64_t out_ld, out_bs;
   uint16_t* out2;  // GEMM1: A' = c A + b I; GEMM3: X (transposed store)
   int64_t out2_ld, out2_bs;
+  int64_t lo_off, lo_off2;  // format 2: lo values of out / out2, in elements after the hi
   int* err;
   // final iteration: per-matrix destination (NS output or parameter).  A tall
   // matrix's output is X_final^T = D itself (O[r][c], row length N); a wide
@@ -120,15 +121,18 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return (uint16_t)(u >> 16);
 }
 
+// Operand formats: 0 = f16, 1 = bf16, 2 = f16 pairs (every operand value v
+// stored as hi = f16(v) and lo = f16(v - hi), lo_off elements after hi in the
+// same row, and each GEMM accumulating hi*hi + hi*lo + lo*hi).
 template <int FMT>
 __device__ __forceinline__ uint16_t to_half_bits(float x) {
-  if constexpr (FMT == 0) return __half_as_ushort(__float2half_rn(x));
+  if constexpr (FMT != 1) return __half_as_ushort(__float2half_rn(x));
   else return f32_to_bf16_bits(x);
 }
 
 template <int FMT>
 __device__ __forceinline__ float from_half_bits(uint16_t h) {
-  if constexpr (FMT == 0) return __half2float(__ushort_as_half(h));
+  if constexpr (FMT != 1) return __half2float(__ushort_as_half(h));
   else return bf16_bits_to_f32(h);
 }
 
@@ -177,12 +181,26 @@ __device__ __forceinline__ bool wait_no_abort(uint64_t* bar, uint32_t parity) {
 // Two f32 values -> one word of two 16-bit values (lo in the low half).
 template <int FMT>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  if constexpr (FMT == 0) {
+  if constexpr (FMT != 1) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);
   } else {
     const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+// 32 f32 values -> their f16 pairs: hi[k] packs f16(v[2k]), f16(v[2k+1]) and
+// lo[k] the f16 roundings of what those leave (v - hi is exact in f32).
+__device__ __forceinline__ void pack_split(const float (&v)[32], uint32_t (&hi)[16],
+                                           uint32_t (&lo)[16]) {
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(v[2 * k] - hf.x, v[2 * k + 1] - hf.y);
+    hi[k] = *reinterpret_cast<const uint32_t*>(&h);
+    lo[k] = *reinterpret_cast<const uint32_t*>(&l);
   }
 }
 
@@ -437,20 +455,37 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
 #pragma unroll
       for (int j = 0; j < 32; ++j) o[j] = acc[j];
       scale_add_aux<FMT>(a, b, r, c0, full, o);
-      uint32_t w[16];
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        w[k] = pack2<FMT>(o[2 * k] + (c0 + 2 * k == r ? a.beta : 0.f),
-                          o[2 * k + 1] + (c0 + 2 * k + 1 == r ? a.beta : 0.f));
-      sym_store(a, a.out + (int64_t)b * a.out_bs, a.out_ld, w, r, r0, c0, full, wfull, tsm);
+      for (int j = 0; j < 32; ++j) o[j] += (c0 + j == r ? a.beta : 0.f);
+      uint16_t* base = a.out + (int64_t)b * a.out_bs;
+      if constexpr (FMT == 2) {
+        uint32_t w[16], wl[16];
+        pack_split(o, w, wl);
+        sym_store(a, base, a.out_ld, w, r, r0, c0, full, wfull, tsm);
+        sym_store(a, base + a.lo_off, a.out_ld, wl, r, r0, c0, full, wfull, tsm);
+      } else {
+        uint32_t w[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
+        sym_store(a, base, a.out_ld, w, r, r0, c0, full, wfull, tsm);
+      }
     }
     if (a.out2 != nullptr) {  // out2 = alpha2*acc + beta2*I
-      uint32_t w[16];
+      float o[32];
 #pragma unroll
-      for (int k = 0; k < 16; ++k)
-        w[k] = pack2<FMT>(a.alpha2 * acc[2 * k] + (c0 + 2 * k == r ? a.beta2 : 0.f),
-                          a.alpha2 * acc[2 * k + 1] + (c0 + 2 * k + 1 == r ? a.beta2 : 0.f));
-      sym_store(a, a.out2 + (int64_t)b * a.out2_bs, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
+      for (int j = 0; j < 32; ++j) o[j] = a.alpha2 * acc[j] + (c0 + j == r ? a.beta2 : 0.f);
+      uint16_t* base = a.out2 + (int64_t)b * a.out2_bs;
+      if constexpr (FMT == 2) {
+        uint32_t w[16], wl[16];
+        pack_split(o, w, wl);
+        sym_store(a, base, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
+        sym_store(a, base + a.lo_off2, a.out2_ld, wl, r, r0, c0, full, wfull, tsm);
+      } else {
+        uint32_t w[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
+        sym_store(a, base, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
+      }
     }
     return;
   }
@@ -461,27 +496,38 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
     for (int j = 0; j < 32; ++j) o[j] = acc[j];
     scale_add_aux<FMT>(a, b, r, c0, full, o);
     if constexpr (EPI == EPI_XUPD) {
-      uint32_t w[16];
-#pragma unroll
-      for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
-      uint16_t* d1 = a.out + (int64_t)b * a.out_bs + (int64_t)r * a.out_ld + c0;
-      if (wfull) {
-        store_block16(a.out + (int64_t)b * a.out_bs, a.out_ld, r0, c0, 32, w, tsm);
-      } else if (full) {
-        store_words16(d1, w);
+      uint32_t w[16], wl[16];
+      if constexpr (FMT == 2) {
+        pack_split(o, w, wl);
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < a.N) d1[j] = half_at(w, j);
+        for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
       }
-      uint16_t* d2 = a.out2 + (int64_t)b * a.out2_bs;
-      if (wfull) {
-        warp_transpose16(tsm, w);
-        store_block16(d2, a.out2_ld, c0, r0, 32, w, tsm);
-      } else {
+      // format 2 stores the lo halves as a second pass over the same code
+      constexpr int kParts = FMT == 2 ? 2 : 1;
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (c0 + j < a.N) d2[(int64_t)(c0 + j) * a.out2_ld + r] = half_at(w, j);
+      for (int part = 0; part < kParts; ++part) {
+        uint32_t (&ww)[16] = part == 0 ? w : wl;
+        uint16_t* d1base = a.out + (int64_t)b * a.out_bs + (part == 0 ? 0 : a.lo_off);
+        uint16_t* d1 = d1base + (int64_t)r * a.out_ld + c0;
+        if (wfull) {
+          store_block16(d1base, a.out_ld, r0, c0, 32, ww, tsm);
+        } else if (full) {
+          store_words16(d1, ww);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < a.N) d1[j] = half_at(ww, j);
+        }
+        uint16_t* d2 = a.out2 + (int64_t)b * a.out2_bs + (part == 0 ? 0 : a.lo_off2);
+        if (wfull) {
+          warp_transpose16(tsm, ww);
+          store_block16(d2, a.out2_ld, c0, r0, 32, ww, tsm);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < a.N) d2[(int64_t)(c0 + j) * a.out2_ld + r] = half_at(ww, j);
+        }
       }
     } else {
       void* dst = a.fin_ptrs[b];
@@ -539,6 +585,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
 template <int EPI, int FMT>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmA_lo, const __grid_constant__ CUtensorMap tmB_lo,
                const __grid_constant__ GemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -566,6 +613,10 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (FMT == 2) {
+      tma_prefetch_desc(&tmA_lo);
+      tma_prefetch_desc(&tmB_lo);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -578,6 +629,10 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   const int n_tiles = args.batch * args.tiles_per_mat;
   const int num_kb = (args.K + BK - 1) / BK;
+  // format 2: three passes over K into one accumulator -- (A hi, B hi),
+  // (A hi, B lo), (A lo, B hi)
+  constexpr int kSegments = FMT == 2 ? 3 : 1;
+  const int total_kb = num_kb * kSegments;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -590,15 +645,18 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x) {
         int b, tm, tn;
         decode_tile(args, t, b, tm, tn);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kt = 0; kt < total_kb; ++kt) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err, 1)) {
             ok = false;
             break;
           }
+          const int seg = kt / num_kb, kb = kt - seg * num_kb;
+          const CUtensorMap* ma = seg == 2 ? &tmA_lo : &tmA;
+          const CUtensorMap* mb = seg == 1 ? &tmB_lo : &tmB;
           uint8_t* st = smem + stage * STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_3d(st, &tmA, &full[stage], kb * BK, tm * BM, b);
-          tma_load_3d(st + A_TILE_BYTES, &tmB, &full[stage], kb * BK, tn * BN, b);
+          tma_load_3d(st, ma, &full[stage], kb * BK, tm * BM, b);
+          tma_load_3d(st + A_TILE_BYTES, mb, &full[stage], kb * BK, tn * BN, b);
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -617,7 +675,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t IDESC = idesc_f16(FMT, BM, BN);
+      constexpr uint32_t IDESC = idesc_f16(FMT == 1 ? 1 : 0, BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -631,7 +689,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < total_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, args.err, 3)) {
             ok = false;
             break;
@@ -807,6 +865,7 @@ template <int SDT, bool MUON, int FMT>
 __global__ void __launch_bounds__(256)
 prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ scales) {
   __shared__ uint16_t tile[32][33];
+  __shared__ uint16_t tile_lo[FMT == 2 ? 32 : 1][33];  // format 2: the lo halves
   const int b = blockIdx.z;
   const float inv = __ldg(scales + b);
   const bool tall = (a.tall[b >> 6] >> (b & 63)) & 1ull;  // G = X^T
@@ -854,23 +913,35 @@ prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ 
   // same-layout target: X (wide) or X^T (tall)
   uint16_t* same = tall ? a.xt + (int64_t)b * a.xt_bs : a.x + (int64_t)b * a.x_bs;
   const int64_t same_ld = tall ? a.xt_ld : a.x_ld;
+  const int64_t same_lo = tall ? a.xt_lo : a.x_lo;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     if (!in[k]) continue;
     const int64_t r = tr * 32 + threadIdx.y + 8 * k;
-    const uint16_t h = to_half_bits<FMT>(__fmul_rn(x[k], a.prescale));
+    const float v = __fmul_rn(x[k], a.prescale);
+    const uint16_t h = to_half_bits<FMT>(v);
     same[r * same_ld + c] = h;
     tile[threadIdx.y + 8 * k][threadIdx.x] = h;
+    if constexpr (FMT == 2) {  // lo = f16(v - hi); v - hi is exact in f32
+      const uint16_t l = to_half_bits<FMT>(v - from_half_bits<FMT>(h));
+      same[r * same_ld + same_lo + c] = l;
+      tile_lo[threadIdx.y + 8 * k][threadIdx.x] = l;
+    }
   }
   __syncthreads();
   // transposed target: element (r, c) of G goes to row c, column r
   uint16_t* other = tall ? a.x + (int64_t)b * a.x_bs : a.xt + (int64_t)b * a.xt_bs;
   const int64_t other_ld = tall ? a.x_ld : a.xt_ld;
+  const int64_t other_lo = tall ? a.x_lo : a.xt_lo;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const int64_t cc = tc * 32 + threadIdx.y + 8 * k;  // row of the target
     const int64_t rr = tr * 32 + threadIdx.x;           // column of the target
-    if (cc < cols && rr < rows) other[cc * other_ld + rr] = tile[threadIdx.x][threadIdx.y + 8 * k];
+    if (cc < cols && rr < rows) {
+      other[cc * other_ld + rr] = tile[threadIdx.x][threadIdx.y + 8 * k];
+      if constexpr (FMT == 2)
+        other[cc * other_ld + other_lo + rr] = tile_lo[threadIdx.x][threadIdx.y + 8 * k];
+    }
   }
 }
 
@@ -921,9 +992,10 @@ static thread_local int g_gemm_reserved_sms = 0;
 
 void set_gemm_reserved_sms(int n) { g_gemm_reserved_sms = n < 0 ? 0 : n; }
 
+// ma_lo / mb_lo: the lo halves' maps in format 2 (the same maps otherwise).
 template <int EPI, int FMT>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
-                       cudaStream_t s) {
+static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma_lo,
+                       const CUtensorMap& mb_lo, const GemmArgs& g, cudaStream_t s) {
   static bool attr_set[64] = {};
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));
@@ -938,42 +1010,62 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmA
   const int n_tiles = g.batch * g.tiles_per_mat;
   if (n_tiles == 0) return TK_OK;
   const int grid = std::min(n_tiles, std::max(1, sms - g_gemm_reserved_sms));
-  gemm_tn_kernel<EPI, FMT><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, g);
+  gemm_tn_kernel<EPI, FMT><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, ma_lo, mb_lo, g);
   TK_CUDA_TRY(cudaGetLastError());
   return TK_OK;
 }
 
+// An operand: the map of its (hi) values and, in format 2, of its lo halves.
+struct Operand {
+  CUtensorMap hi, lo;
+};
+
 template <int EPI>
-static int launch_gemm_fmt(int fmt, const CUtensorMap& ma, const CUtensorMap& mb,
-                           const GemmArgs& g, cudaStream_t s) {
-  return fmt == 0 ? launch_gemm<EPI, 0>(ma, mb, g, s) : launch_gemm<EPI, 1>(ma, mb, g, s);
+static int launch_gemm_fmt(int fmt, const Operand& a, const Operand& b, const GemmArgs& g,
+                           cudaStream_t s) {
+  if (fmt == 2) return launch_gemm<EPI, 2>(a.hi, b.hi, a.lo, b.lo, g, s);
+  return fmt == 0 ? launch_gemm<EPI, 0>(a.hi, b.hi, a.hi, b.hi, g, s)
+                  : launch_gemm<EPI, 1>(a.hi, b.hi, a.hi, b.hi, g, s);
 }
 
-static int launch_gemm_epi(int epi, int fmt, const CUtensorMap& ma, const CUtensorMap& mb,
+static int launch_gemm_epi(int epi, int fmt, const Operand& a, const Operand& b,
                            const GemmArgs& g, cudaStream_t s) {
   switch (epi) {
-    case EPI_PLAIN: return launch_gemm_fmt<EPI_PLAIN>(fmt, ma, mb, g, s);
-    case EPI_SYM: return launch_gemm_fmt<EPI_SYM>(fmt, ma, mb, g, s);
-    case EPI_XUPD: return launch_gemm_fmt<EPI_XUPD>(fmt, ma, mb, g, s);
-    case EPI_FINAL: return launch_gemm_fmt<EPI_FINAL>(fmt, ma, mb, g, s);
+    case EPI_SYM: return launch_gemm_fmt<EPI_SYM>(fmt, a, b, g, s);
+    case EPI_XUPD: return launch_gemm_fmt<EPI_XUPD>(fmt, a, b, g, s);
+    case EPI_FINAL: return launch_gemm_fmt<EPI_FINAL>(fmt, a, b, g, s);
   }
   return set_error(TK_ERR_INVALID, "bad epilogue %d", epi);
+}
+
+// The hi (and, in format 2, lo) maps of an operand stored with row stride
+// `rs` elements, the lo values lo_off elements after the hi ones.
+static int make_operand(Operand* op, const uint16_t* base, int fmt, int64_t inner, int64_t rows,
+                        int64_t rs, int64_t lo_off, int64_t batch, int box_rows) {
+  TK_TRY(make_map(&op->hi, base, fmt == 1 ? 1 : 0, inner, rows, rs, batch, box_rows));
+  if (fmt == 2) TK_TRY(make_map(&op->lo, base + lo_off, 0, inner, rows, rs, batch, box_rows));
+  else op->lo = op->hi;
+  return TK_OK;
 }
 
 static int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 static size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
-GroupLayout group_layout(int64_t m, int64_t n, int64_t batch) {
+GroupLayout group_layout(int64_t m, int64_t n, int64_t batch, bool split) {
   GroupLayout L;
   L.m = m;
   L.n = n;
   L.batch = batch;
+  L.split = split;
   L.ldx = round_up(L.n, 64);
   L.ldm = round_up(L.m, 64);
-  L.x_bytes = align256((size_t)(batch * L.m * L.ldx * 2));
-  L.xt_bytes = align256((size_t)(batch * L.n * L.ldm * 2));
-  L.a_bytes = align256((size_t)(batch * L.m * L.ldm * 2));
+  // format 2: each row holds the hi values, then the lo values
+  L.rsx = split ? 2 * L.ldx : L.ldx;
+  L.rsm = split ? 2 * L.ldm : L.ldm;
+  L.x_bytes = align256((size_t)(batch * L.m * L.rsx * 2));
+  L.xt_bytes = align256((size_t)(batch * L.n * L.rsm * 2));
+  L.a_bytes = align256((size_t)(batch * L.m * L.rsm * 2));
   L.nblk = (int)std::max<int64_t>(1, std::min<int64_t>(256, (m * n + 16383) / 16384));
   L.scratch_bytes = L.x_bytes + 2 * L.xt_bytes + 3 * L.a_bytes +
                     align256(sizeof(double) * batch * L.nblk) + align256(sizeof(float) * batch) +
@@ -984,7 +1076,7 @@ GroupLayout group_layout(int64_t m, int64_t n, int64_t batch) {
 // Power-of-two pre-scale of the first iterate in f16 mode: RMS of the
 // normalised matrix is 1/sqrt(m n); lift it to about 2^-4.
 static int prescale_exp(int fmt, int64_t m, int64_t n) {
-  if (fmt != 0) return 0;
+  if (fmt == 1) return 0;
   const double r = std::sqrt((double)m * (double)n) / 16.0;
   int k = (int)std::floor(std::log2(std::max(r, 1.0)));
   return std::max(0, std::min(k, 60));
@@ -994,6 +1086,8 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
               int* err_dev, cudaStream_t s) {
   if (L.batch == 0 || L.m == 0) return TK_OK;
   if (L.batch > kMaxBatch) return set_error(TK_ERR_INVALID, "batch of %lld > %d", (long long)L.batch, kMaxBatch);
+  if (L.split != (fmt == 2))
+    return set_error(TK_ERR_INVALID, "scratch layout does not match operand format %d", fmt);
   char* cur = static_cast<char*>(scratch);
   uint16_t* X = reinterpret_cast<uint16_t*>(cur);
   cur += L.x_bytes;
@@ -1026,11 +1120,13 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   pa.om = io.om;
   pa.nesterov = io.nesterov;
   pa.x = X;
-  pa.x_ld = L.ldx;
-  pa.x_bs = L.m * L.ldx;
+  pa.x_ld = L.rsx;
+  pa.x_bs = L.m * L.rsx;
+  pa.x_lo = L.ldx;
   pa.xt = XT[0];
-  pa.xt_ld = L.ldm;
-  pa.xt_bs = L.n * L.ldm;
+  pa.xt_ld = L.rsm;
+  pa.xt_bs = L.n * L.rsm;
+  pa.xt_lo = L.ldm;
   pa.prescale = std::ldexp(1.0f, k);
   pa.steps = steps;
   pa.dst_dtype = io.dst_dtype;
@@ -1054,13 +1150,20 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     dim3 g2((unsigned)(((L.m + 31) / 32) * ((L.n + 31) / 32)), 1, (unsigned)L.batch);
     dim3 b2(32, 8);
 #define TK_PREP_WRITE(SDT, MU, F) prep_write_kernel<SDT, MU, F><<<g2, b2, 0, s>>>(pa, scales)
+#define TK_PREP_WRITE_FMT(SDT, MU)                   \
+  do {                                               \
+    if (fmt == 0) TK_PREP_WRITE(SDT, MU, 0);         \
+    else if (fmt == 1) TK_PREP_WRITE(SDT, MU, 1);    \
+    else TK_PREP_WRITE(SDT, MU, 2);                  \
+  } while (0)
     if (io.src_dtype == TK_F32) {
-      if (muon) { if (fmt == 0) TK_PREP_WRITE(TK_F32, true, 0); else TK_PREP_WRITE(TK_F32, true, 1); }
-      else { if (fmt == 0) TK_PREP_WRITE(TK_F32, false, 0); else TK_PREP_WRITE(TK_F32, false, 1); }
+      if (muon) TK_PREP_WRITE_FMT(TK_F32, true);
+      else TK_PREP_WRITE_FMT(TK_F32, false);
     } else {
-      if (muon) { if (fmt == 0) TK_PREP_WRITE(TK_BF16, true, 0); else TK_PREP_WRITE(TK_BF16, true, 1); }
-      else { if (fmt == 0) TK_PREP_WRITE(TK_BF16, false, 0); else TK_PREP_WRITE(TK_BF16, false, 1); }
+      if (muon) TK_PREP_WRITE_FMT(TK_BF16, true);
+      else TK_PREP_WRITE_FMT(TK_BF16, false);
     }
+#undef TK_PREP_WRITE_FMT
 #undef TK_PREP_WRITE
     TK_CUDA_TRY(cudaGetLastError());
   }
@@ -1077,16 +1180,18 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   // under 256 rows a parameter drift over 10 Muon steps close to 1e-3 (it is
   // below 3e-4 from 256 rows up).  There the epilogues add b A and a X^T in
   // f32 instead: GEMM2 B = c A A + b A, GEMM3 X_new^T = X^T B + a X^T.
-  const bool fold = fmt == 0 && L.m >= 256;
-  CUtensorMap mX128, mX256, mA128, mA256, mAp256, mB256, mXT128[2];
-  TK_TRY(make_map(&mX128, X, fmt, L.n, L.m, L.ldx, L.batch, 128));
-  TK_TRY(make_map(&mX256, X, fmt, L.n, L.m, L.ldx, L.batch, 256));
-  TK_TRY(make_map(&mA128, Am, fmt, L.m, L.m, L.ldm, L.batch, 128));
-  TK_TRY(make_map(&mA256, Am, fmt, L.m, L.m, L.ldm, L.batch, 256));
-  TK_TRY(make_map(&mAp256, Ap, fmt, L.m, L.m, L.ldm, L.batch, 256));
-  TK_TRY(make_map(&mB256, Bm, fmt, L.m, L.m, L.ldm, L.batch, 256));
-  TK_TRY(make_map(&mXT128[0], XT[0], fmt, L.m, L.n, L.ldm, L.batch, 128));
-  TK_TRY(make_map(&mXT128[1], XT[1], fmt, L.m, L.n, L.ldm, L.batch, 128));
+  // Split operands (format 2) keep every stored value to about 22 bits, so
+  // the folded form's roundings cost nothing there and it is used at all sizes.
+  const bool fold = fmt == 2 || (fmt == 0 && L.m >= 256);
+  Operand mX128, mX256, mA128, mA256, mAp256, mB256, mXT128[2];
+  TK_TRY(make_operand(&mX128, X, fmt, L.n, L.m, L.rsx, L.ldx, L.batch, 128));
+  TK_TRY(make_operand(&mX256, X, fmt, L.n, L.m, L.rsx, L.ldx, L.batch, 256));
+  TK_TRY(make_operand(&mA128, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 128));
+  TK_TRY(make_operand(&mA256, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
+  TK_TRY(make_operand(&mAp256, Ap, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
+  TK_TRY(make_operand(&mB256, Bm, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
+  TK_TRY(make_operand(&mXT128[0], XT[0], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
+  TK_TRY(make_operand(&mXT128[1], XT[1], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
 
   const int tm_sq = (int)((L.m + BM - 1) / BM), tn_sq = (int)((L.m + BN - 1) / BN);
   const int tm_x = (int)((L.n + BM - 1) / BM);
@@ -1108,14 +1213,15 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     g.alpha = it == 0 ? inv_pre2 : 1.0f;
     g.beta = 0.0f;
     g.out = Am;
-    g.out_ld = L.ldm;
-    g.out_bs = L.m * L.ldm;
+    g.out_ld = L.rsm;
+    g.out_bs = L.m * L.rsm;
+    g.lo_off = g.lo_off2 = L.ldm;
     if (fold) {
       g.alpha2 = NS_C * g.alpha;
       g.beta2 = NS_B;
       g.out2 = Ap;
-      g.out2_ld = L.ldm;
-      g.out2_bs = L.m * L.ldm;
+      g.out2_ld = L.rsm;
+      g.out2_bs = L.m * L.rsm;
     }
     TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mX128, mX256, g, s));
     // GEMM2: B' = A A' + a I  (bf16: B = c A A + b A)
@@ -1130,8 +1236,8 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       g.alpha = NS_C;
       g.gamma = NS_B;
       g.aux = Am;
-      g.aux_ld = L.ldm;
-      g.aux_bs = L.m * L.ldm;
+      g.aux_ld = L.rsm;
+      g.aux_bs = L.m * L.rsm;
       TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mA128, mA256, g, s));
     }
     // GEMM3: X_new^T = post * X^T B' (post undoes the first iterate's pre-scale)
@@ -1146,19 +1252,21 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     h.tiles_per_mat = tm_x * tn_sq;
     h.symmetric = 0;
     h.alpha = it == 0 ? inv_pre : 1.0f;
+    h.lo_off = L.ldm;   // X^T rows
+    h.lo_off2 = L.ldx;  // X rows
     if (!fold) {  // + a X^T
       h.gamma = NS_A * h.alpha;
       h.aux = XT[cur_xt];
-      h.aux_ld = L.ldm;
-      h.aux_bs = L.n * L.ldm;
+      h.aux_ld = L.rsm;
+      h.aux_bs = L.n * L.rsm;
     }
     if (it + 1 < steps) {
       h.out = XT[cur_xt ^ 1];
-      h.out_ld = L.ldm;
-      h.out_bs = L.n * L.ldm;
+      h.out_ld = L.rsm;
+      h.out_bs = L.n * L.rsm;
       h.out2 = X;
-      h.out2_ld = L.ldx;
-      h.out2_bs = L.m * L.ldx;
+      h.out2_ld = L.rsx;
+      h.out2_bs = L.m * L.rsx;
       TK_TRY(launch_gemm_epi(EPI_XUPD, fmt, mXT128[cur_xt], mB256, h, s));
       cur_xt ^= 1;
     } else {
@@ -1267,6 +1375,7 @@ int bounded_wait_probe(int* err_dev, int limit_ms, cudaStream_t s) {
 int plain_gemm(const uint16_t* P, const uint16_t* Q, uint16_t* D, int batch, int M, int N, int K,
                int64_t ldp, int64_t ldq, int64_t ldd, float alpha, int fmt, int* err_dev,
                cudaStream_t s) {
+  if (fmt != 0 && fmt != 1) return set_error(TK_ERR_INVALID, "plain GEMM format %d", fmt);
   CUtensorMap ma, mb;
   TK_TRY(make_map(&ma, P, fmt, K, M, ldp, batch, 128));
   TK_TRY(make_map(&mb, Q, fmt, K, N, ldq, batch, 256));
@@ -1284,7 +1393,8 @@ int plain_gemm(const uint16_t* P, const uint16_t* Q, uint16_t* D, int batch, int
   g.out_ld = ldd;
   g.out_bs = (int64_t)M * ldd;
   g.err = err_dev;
-  return launch_gemm_epi(EPI_PLAIN, fmt, ma, mb, g, s);
+  return fmt == 0 ? launch_gemm<EPI_PLAIN, 0>(ma, mb, ma, mb, g, s)
+                  : launch_gemm<EPI_PLAIN, 1>(ma, mb, ma, mb, g, s);
 }
 
 }  // namespace ns

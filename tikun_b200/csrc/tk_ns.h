@@ -19,16 +19,19 @@ constexpr int kMaxBatch = 256;
 // Scratch layout of one batch of matrices that are all m x n or n x m
 // (m <= n): X is m x n, two X^T buffers (ping-pong) are n x m, and A, A' and
 // B are m x m, all half precision with rows padded to a multiple of 64
-// elements.
+// elements (ldx, ldm).  With split operands (format 2) each row holds ld hi
+// values followed by ld lo values: row strides rsx = 2 ldx, rsm = 2 ldm.
 struct GroupLayout {
   int64_t m, n, batch;
   int64_t ldx, ldm;
+  int64_t rsx, rsm;
+  bool split;
   size_t x_bytes, xt_bytes, a_bytes;
   int nblk;
   size_t scratch_bytes;
 };
 
-GroupLayout group_layout(int64_t m, int64_t n, int64_t batch);
+GroupLayout group_layout(int64_t m, int64_t n, int64_t batch, bool split = false);
 
 // Inputs and outputs of one batch (host arrays of device pointers, length
 // batch <= kMaxBatch).  A "tall" matrix is stored n x m (rows > cols).
@@ -54,9 +57,9 @@ struct PrepArgs {
   float mu, om;
   int nesterov;
   uint16_t* x;
-  int64_t x_ld, x_bs;
+  int64_t x_ld, x_bs, x_lo;  // x_lo, xt_lo: offset of the lo values (split operands)
   uint16_t* xt;
-  int64_t xt_ld, xt_bs;
+  int64_t xt_ld, xt_bs, xt_lo;
   float prescale;
   int steps;
   int dst_dtype;

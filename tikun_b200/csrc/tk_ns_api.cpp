@@ -26,8 +26,14 @@ static size_t ns_scratch_budget() {
   return (size_t)(gb * (1ull << 30));
 }
 
+// Operand format of the Newton-Schulz kernels: 0 f16, 1 bf16, 2 f16 pairs.
 static int fmt_of(int precision) {
-  return precision == TK_NS_BF16 ? 1 : (precision == TK_NS_F16 ? 0 : -1);
+  switch (precision) {
+    case TK_NS_F16: return 0;
+    case TK_NS_BF16: return 1;
+    case TK_NS_F16X3: return 2;
+  }
+  return -1;
 }
 
 // Reads and clears the device status word after the stream has drained.
@@ -143,7 +149,7 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
                        int steps, int fmt, cudaStream_t s, const PeerSet* peers = nullptr,
                        PeerCopy* copy = nullptr) {
   const int64_t count = (int64_t)src.size();
-  const ns::GroupLayout one = ns::group_layout(m, n, 1);
+  const ns::GroupLayout one = ns::group_layout(m, n, 1, fmt == 2);
   const int64_t per_wave = std::max<int64_t>(
       1, std::min<int64_t>({count, (int64_t)(ns_scratch_budget() / one.scratch_bytes),
                             (int64_t)ns::kMaxBatch}));
@@ -151,7 +157,7 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
   TK_TRY(device_status_word(&status));
   for (int64_t first = 0; first < count; first += per_wave) {
     const int64_t nb = std::min(per_wave, count - first);
-    const ns::GroupLayout L = ns::group_layout(m, n, nb);
+    const ns::GroupLayout L = ns::group_layout(m, n, nb, fmt == 2);
     Scratch scratch;
     TK_TRY(scratch.alloc(L.scratch_bytes, s));
     ns::GroupIO io;
