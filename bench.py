@@ -611,13 +611,14 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
     return res
 
 
-def ns_scratch_bytes(m, n):
+def ns_scratch_bytes(m, n, split=False):
     """Newton-Schulz scratch of one m x n matrix (m <= n), as the library lays
     it out (rows padded to 64 elements, buffers 256-byte aligned): X, two X^T,
-    A, A' and B in 16-bit, the norm partials and the scale."""
+    A, A' and B in 16-bit (twice as wide with split f16 operands), the norm
+    partials and the scale."""
     r64 = lambda x: (x + 63) // 64 * 64  # noqa: E731
     a256 = lambda x: (x + 255) // 256 * 256  # noqa: E731
-    ldx, ldm = r64(n), r64(m)
+    ldx, ldm = r64(n) * (2 if split else 1), r64(m) * (2 if split else 1)
     nblk = max(1, min(256, (m * n + 16383) // 16384))
     return (a256(m * ldx * 2) + 2 * a256(n * ldm * 2) + 3 * a256(m * ldm * 2) + a256(8 * nblk)
             + a256(4) + 256)
@@ -939,7 +940,10 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
             groups[key] = groups.get(key, 0) + 1
         n = 0
         for (m, nn), cnt in groups.items():
-            per_wave = max(1, min(cnt, 256, (8 << 30) // ns_scratch_bytes(m, nn)))
+            per_wave = max(1, min(cnt, 256, (8 << 30) // ns_scratch_bytes(
+                m, nn, args.ns_precision == "f16x3")))
+            if world > 1 and exchange == "copy":  # at least three waves per group
+                per_wave = max(1, min(per_wave, (cnt + 2) // 3))
             waves = -(-cnt // per_wave)
             n += waves * (3 + 15 + (1 if world > 1 and exchange == "copy" else 0))
         return n

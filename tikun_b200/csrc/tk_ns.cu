@@ -733,11 +733,11 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc_fence_after();
       const int r = tm * BM + row_in_tile;
       const int c_base = tn * BN;
+      const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * BN) +
+                             (static_cast<uint32_t>(q * 32) << 16);
       for (int cc = col0; cc < col0 + BN / 2; cc += 32) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(acc * BN + cc) +
-                               (static_cast<uint32_t>(q * 32) << 16),
-                           v);
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(cc), v);
         tmem_ld_wait();
         if (c_base + cc < args.N) epilogue_chunk<EPI, FMT>(args, b, r, c_base + cc, v, tsm);
       }

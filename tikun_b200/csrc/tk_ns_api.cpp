@@ -150,9 +150,13 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
                        PeerCopy* copy = nullptr) {
   const int64_t count = (int64_t)src.size();
   const ns::GroupLayout one = ns::group_layout(m, n, 1, fmt == 2);
-  const int64_t per_wave = std::max<int64_t>(
+  int64_t per_wave = std::max<int64_t>(
       1, std::min<int64_t>({count, (int64_t)(ns_scratch_budget() / one.scratch_bytes),
                             (int64_t)ns::kMaxBatch}));
+  // With a copy exchange, a group runs in at least three waves: the copies of
+  // one wave's parameters then cross NVLink while the next waves compute,
+  // instead of all after the group's last GEMM.
+  if (copy != nullptr && copy->n > 0) per_wave = std::max<int64_t>(1, std::min(per_wave, (count + 2) / 3));
   int* status = nullptr;
   TK_TRY(device_status_word(&status));
   for (int64_t first = 0; first < count; first += per_wave) {
