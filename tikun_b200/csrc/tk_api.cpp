@@ -218,7 +218,44 @@ int check_overlaps(ByteRange* ranges, size_t n) {
 // Rejects null or mismatched fields, bad dtypes, any overlap between a range
 // the step writes (p, m, v) and any other range, and a mix of host and device
 // leaves.  Reports where the leaves live.
+static int validate_leaves_full(const tk_leaf* leaves, size_t n, int kind, Residency* where);
+
+// A training loop steps the same leaf table every time; classifying its
+// pointers costs one driver query per buffer (four per leaf), which for a
+// few hundred leaves is a good part of a sub-millisecond step's host time.
+// The last table that passed on this thread (with its device and kind) is
+// remembered, and an identical table is accepted without the queries.
+struct ValidatedTable {
+  bool valid = false;
+  int dev = -1, kind = -1;
+  std::vector<tk_leaf> leaves;
+  Residency where = Residency::kNone;
+};
+static thread_local ValidatedTable g_validated;
+
 static int validate_leaves(const tk_leaf* leaves, size_t n, int kind, Residency* where) {
+  int dev = 0;
+  if (n > 0 && leaves != nullptr) {
+    TK_CUDA_TRY(cudaGetDevice(&dev));
+    const ValidatedTable& v = g_validated;
+    if (v.valid && v.dev == dev && v.kind == kind && v.leaves.size() == n &&
+        std::memcmp(v.leaves.data(), leaves, n * sizeof(tk_leaf)) == 0) {
+      *where = v.where;
+      return TK_OK;
+    }
+  }
+  const int st = validate_leaves_full(leaves, n, kind, where);
+  if (st == TK_OK && n > 0) {
+    g_validated.valid = true;
+    g_validated.dev = dev;
+    g_validated.kind = kind;
+    g_validated.leaves.assign(leaves, leaves + n);
+    g_validated.where = *where;
+  }
+  return st;
+}
+
+static int validate_leaves_full(const tk_leaf* leaves, size_t n, int kind, Residency* where) {
   *where = Residency::kNone;
   if (n == 0) return TK_OK;
   if (leaves == nullptr) return set_error(TK_ERR_INVALID, "leaves is NULL with n_leaves=%zu", n);
