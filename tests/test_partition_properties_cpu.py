@@ -170,13 +170,16 @@ def test_peer_copy_split_copies_every_byte_once(entry_bytes, grid):
     assert all((c == 1).all() for c in cover)
 
 
-# -- the pointwise update's work split (pointwise_kernel in tk_pointwise.cu) --
+# -- the pointwise update's and the Tier-1 norm's work split
+# (pointwise_kernel and sumsq_partials_kernel in tk_pointwise.cu) --
 def _pointwise_cover(sizes, vec_ok, grid, threads=256, unroll=4):
-    """The kernel's split restated: the leaves' 4-element groups ("quads") in
+    """The kernels' split restated: the leaves' 4-element groups ("quads") in
     one index space, an equal contiguous quad range per CTA, the leaf found by
     binary search on q_begin, whole quads of aligned leaves through the
-    unrolled vector loop and the rest element by element.  Returns per-leaf
-    element coverage, and whether any vector access ran past a leaf's end."""
+    unrolled vector loop (trips of `unroll` quads `threads` apart; the
+    pipelined update loop visits the same trips, loading one ahead) and the
+    rest element by element.  Returns per-leaf element coverage, and whether
+    any vector access ran past a leaf's end."""
     q_begin, total = [], 0
     for n in sizes:
         q_begin.append(total)
@@ -214,8 +217,11 @@ def _pointwise_cover(sizes, vec_ok, grid, threads=256, unroll=4):
 @settings(max_examples=60, deadline=None)
 @given(st.lists(st.tuples(st.integers(min_value=1, max_value=6000), st.booleans()),
                 min_size=1, max_size=6),
-       st.integers(min_value=1, max_value=9), st.sampled_from([(32, 4), (64, 2), (16, 1)]))
+       st.integers(min_value=1, max_value=9),
+       st.sampled_from([(32, 4), (64, 2), (16, 1), (256, 5), (256, 4), (256, 1)]))
 def test_pointwise_split_updates_every_element_once(leaves, grid, shape):
+    # (256, 5): the pipelined f32 update; (256, 1): bf16 leaves; (256, 4): the
+    # Tier-1 norm's four accumulators
     sizes = [n for n, _ in leaves]
     vec_ok = [v for _, v in leaves]
     cover, past_end = _pointwise_cover(sizes, vec_ok, grid, threads=shape[0], unroll=shape[1])

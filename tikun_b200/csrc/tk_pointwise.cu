@@ -72,12 +72,19 @@ using namespace pw;
 #endif
 constexpr int kThreads = 256;
 
-template <int PDT, int GDT>
+// PEER: the variant that also stores every updated parameter into the peers'
+// copies over NVLink.  It keeps the settings measured for it before the
+// local update was retuned (4 quads with 2 CTAs per SM for f32, 2 quads with
+// 3 CTAs for bf16, not pipelined): with 6 CTAs of 40 registers the bf16
+// variant's seven peer stores per quad spilled, and the 2-GPU Muon+AdamW step
+// lost 9 ms to it.
+template <int PDT, int GDT, bool PEER = false>
 struct Tune {
   static constexpr bool all_f32 = PDT == TK_F32 && GDT == TK_F32;
-  static constexpr int unroll = all_f32 ? TK_PW_UNROLL : TK_PW_UNROLL_BF16;
-  static constexpr int minblocks = all_f32 ? TK_PW_MINBLOCKS : TK_PW_MINBLOCKS_BF16;
-  static constexpr bool pipe = all_f32 ? TK_PW_PIPE != 0 : TK_PW_PIPE_BF16 != 0;
+  static constexpr int unroll = PEER ? (all_f32 ? 4 : 2) : (all_f32 ? TK_PW_UNROLL : TK_PW_UNROLL_BF16);
+  static constexpr int minblocks =
+      PEER ? (all_f32 ? 2 : 3) : (all_f32 ? TK_PW_MINBLOCKS : TK_PW_MINBLOCKS_BF16);
+  static constexpr bool pipe = PEER ? false : (all_f32 ? TK_PW_PIPE != 0 : TK_PW_PIPE_BF16 != 0);
 };
 
 // One trip's quads of one thread: quad lq + u*kThreads for u < U, the ones
@@ -143,7 +150,10 @@ sumsq_partials_kernel(const __grid_constant__ LeafTable t, double* __restrict__ 
   const uint64_t total = t.total_quads;
   const uint64_t q0 = total * blockIdx.x / gridDim.x;
   const uint64_t q1 = total * (blockIdx.x + 1) / gridDim.x;
-  double acc = 0.0;
+  // four independent accumulators, one per quad of a loop trip, so that four
+  // loads per thread are in flight; summed in a fixed order at the end
+  constexpr int kU = 4;
+  double acc[kU] = {0.0, 0.0, 0.0, 0.0};
   if (q0 < q1) {
     int li = find_leaf(t, q0);
     uint64_t q = q0;
@@ -151,18 +161,25 @@ sumsq_partials_kernel(const __grid_constant__ LeafTable t, double* __restrict__ 
       const LeafDesc& L = t.leaf[li];
       const uint64_t seg_end = min(q1, L.q_begin + leaf_quads(L));
       const uint64_t a = q - L.q_begin, b = seg_end - L.q_begin;
-      for (uint64_t lq = a + threadIdx.x; lq < b; lq += kThreads) {
-        const uint64_t e = lq * 4;
-        if (L.vec_ok && e + 4 <= L.n) {
-          float x[4];
-          load_quad<GDT>(L.g, e, x);
+      // quads [a, full_end) are whole and vector-accessible; the rest go scalar
+      const uint64_t full_end = L.vec_ok ? min(b, L.n >> 2) : a;
+      for (uint64_t lq = a + threadIdx.x; lq < full_end; lq += (uint64_t)kThreads * kU) {
+        float x[kU][4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc = fma((double)x[j], (double)x[j], acc);
-        } else {
-          for (uint64_t j = e; j < min(e + 4, L.n); ++j) {
-            const double x = load1<GDT>(L.g, j);
-            acc = fma(x, x, acc);
-          }
+        for (int u = 0; u < kU; ++u) {
+          const uint64_t qq = lq + (uint64_t)u * kThreads;
+          if (qq < full_end) load_quad<GDT>(L.g, qq * 4, x[u]);
+          else x[u][0] = x[u][1] = x[u][2] = x[u][3] = 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[u] = fma((double)x[u][j], (double)x[u][j], acc[u]);
+      }
+      for (uint64_t lq = max(a, full_end) + threadIdx.x; lq < b; lq += kThreads) {
+        for (uint64_t j = lq * 4; j < min(lq * 4 + 4, L.n); ++j) {
+          const double x = load1<GDT>(L.g, j);
+          acc[0] = fma(x, x, acc[0]);
         }
       }
       q = seg_end;
@@ -170,7 +187,7 @@ sumsq_partials_kernel(const __grid_constant__ LeafTable t, double* __restrict__ 
     }
   }
   // x*x of an f32 value is exact in f64, so fma == multiply-then-add here.
-  const double s = block_sum<kThreads>(acc);
+  const double s = block_sum<kThreads>((acc[0] + acc[1]) + (acc[2] + acc[3]));
   if (threadIdx.x == 0) partials[blockIdx.x] = s;
 }
 
@@ -193,8 +210,8 @@ clip_scale_kernel(const double* __restrict__ partials, int n, float max_norm,
 
 // ------------------------------------------------------------------ Tier 2
 // SCALE: 0 = no clipping, 1 = fold partials in every CTA, 2 = read scale_dev.
-template <int KIND, int PDT, int GDT, int SCALE>
-__global__ void __launch_bounds__(kThreads, (Tune<PDT, GDT>::minblocks))
+template <int KIND, int PDT, int GDT, int SCALE, bool PEER>
+__global__ void __launch_bounds__(kThreads, (Tune<PDT, GDT, PEER>::minblocks))
 pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
                  const double* __restrict__ partials, int n_partials, float max_norm,
                  const float* __restrict__ scale_dev, float* __restrict__ scale_out,
@@ -229,7 +246,7 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
     const uint64_t a = q - L.q_begin, b = seg_end - L.q_begin;
     // quads [a, full_end) are whole and vector-accessible; the rest go scalar
     const uint64_t full_end = L.vec_ok ? min(b, L.n >> 2) : a;
-    constexpr int kUnroll = Tune<PDT, GDT>::unroll;
+    constexpr int kUnroll = Tune<PDT, GDT, PEER>::unroll;
     constexpr uint64_t kStride = (uint64_t)kThreads * kUnroll;
     auto load_batch = [&](uint64_t lq, Batch<kUnroll>& B) {
 #pragma unroll
@@ -257,14 +274,16 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         }
         const uint64_t e = (lq + (uint64_t)u * kThreads) * 4;
         store_quad<PDT>(L.p, e, B.P[u]);
+        if constexpr (PEER) {
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r)  // the updated parameters, into each peer's copy
-          if (r < peers.n) store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, B.P[u]);
+          for (int r = 0; r < kMaxPeers; ++r)  // the updated parameters, into each peer's copy
+            if (r < peers.n) store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, B.P[u]);
+        }
         store_quad<TK_F32>(L.m, e, B.M[u]);
         if constexpr (KIND == TK_ADAMW) store_quad<TK_F32>(L.v, e, B.V[u]);
       }
     };
-    if constexpr (Tune<PDT, GDT>::pipe) {
+    if constexpr (Tune<PDT, GDT, PEER>::pipe) {
       uint64_t lq = a + threadIdx.x;
       Batch<kUnroll> cur;
       if (lq < full_end) load_batch(lq, cur);
@@ -293,9 +312,11 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         if constexpr (KIND == TK_ADAMW) v = L.v[e];
         apply<KIND>(p, g, m, v, k);
         store1<PDT>(L.p, e, p);
+        if constexpr (PEER) {
 #pragma unroll
-        for (int r = 0; r < kMaxPeers; ++r)
-          if (r < peers.n) store1<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, p);
+          for (int r = 0; r < kMaxPeers; ++r)
+            if (r < peers.n) store1<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, p);
+        }
         L.m[e] = m;
         if constexpr (KIND == TK_ADAMW) L.v[e] = v;
       }
@@ -303,16 +324,18 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
     q = seg_end;
     ++li;
   }
-  if (peers.n) __threadfence_system();  // peer stores visible before the kernel ends
+  if constexpr (PEER) {
+    if (peers.n) __threadfence_system();  // peer stores visible before the kernel ends
+  }
 }
 
-template <int KIND, int PDT, int GDT, int SCALE>
+template <int KIND, int PDT, int GDT, int SCALE, bool PEER>
 int occupancy_grid(uint64_t total_quads) {
   static int per_sm = 0;
   if (per_sm == 0) {
     int occ = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &occ, pointwise_kernel<KIND, PDT, GDT, SCALE>, kThreads, 0) != cudaSuccess ||
+            &occ, pointwise_kernel<KIND, PDT, GDT, SCALE, PEER>, kThreads, 0) != cudaSuccess ||
         occ < 1)
       occ = 1;
     per_sm = occ;
@@ -320,7 +343,7 @@ int occupancy_grid(uint64_t total_quads) {
   int sms = 0;
   if (pointwise_sms(&sms) != TK_OK) return 0;
   const int cap = sms * per_sm;
-  constexpr int kUnroll = Tune<PDT, GDT>::unroll;
+  constexpr int kUnroll = Tune<PDT, GDT, PEER>::unroll;
   const uint64_t want = (total_quads + kThreads * kUnroll - 1) / (kThreads * kUnroll);
   if (TK_PW_OVERSUB) return (int)std::min<uint64_t>(want ? want : 1, 1u << 30);
   return (int)(want < (uint64_t)cap ? (want ? want : 1) : cap);
@@ -330,10 +353,17 @@ template <int KIND, int PDT, int GDT, int SCALE>
 int launch_t(const LeafTable& t, const PointwiseConsts& c, const double* partials,
              int n_partials, float max_norm, const float* scale_dev, float* scale_out,
              cudaStream_t s, const PeerSet& peers) {
-  const int grid = occupancy_grid<KIND, PDT, GDT, SCALE>(t.total_quads);
-  if (grid <= 0) return set_error(TK_ERR_CUDA, "could not size the pointwise grid");
-  pointwise_kernel<KIND, PDT, GDT, SCALE><<<grid, kThreads, 0, s>>>(
-      t, c, partials, n_partials, max_norm, scale_dev, scale_out, peers);
+  if (peers.n > 0) {
+    const int grid = occupancy_grid<KIND, PDT, GDT, SCALE, true>(t.total_quads);
+    if (grid <= 0) return set_error(TK_ERR_CUDA, "could not size the pointwise grid");
+    pointwise_kernel<KIND, PDT, GDT, SCALE, true><<<grid, kThreads, 0, s>>>(
+        t, c, partials, n_partials, max_norm, scale_dev, scale_out, peers);
+  } else {
+    const int grid = occupancy_grid<KIND, PDT, GDT, SCALE, false>(t.total_quads);
+    if (grid <= 0) return set_error(TK_ERR_CUDA, "could not size the pointwise grid");
+    pointwise_kernel<KIND, PDT, GDT, SCALE, false><<<grid, kThreads, 0, s>>>(
+        t, c, partials, n_partials, max_norm, scale_dev, scale_out, peers);
+  }
   TK_CUDA_TRY(cudaGetLastError());
   return TK_OK;
 }
