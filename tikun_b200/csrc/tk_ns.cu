@@ -855,77 +855,139 @@ prep_scale_kernel(const double* __restrict__ partials, int nblk, float* __restri
   }
 }
 
-// Pass 2: normalise (x * 1/max(||U||, 1e-7) in f32, tensor_engine.rs:42-44),
-// pre-scale by 2^k, round to the operand type and write X (m x n) and X^T
-// (n x m) through a 32x32 shared-memory transpose.  The input G is R x C
-// (m x n for a wide matrix, n x m for a tall one); grid (ceil(m/32) *
-// ceil(n/32), 1, batch) covers G's 32x32 tiles, block (32, 8).  With
-// steps == 0 it writes the output (or applies the update) instead.
-template <int SDT, bool MUON, int FMT>
+// Normalised Newton-Schulz input u * 1/max(||U||, 1e-7) in f32
+// (tensor_engine.rs:42-44) of element i, u = the Nesterov/momentum value
+// (python/tikun/muon_nd.py:112-115) or the input itself.
+template <int SDT, bool MUON>
+__device__ __forceinline__ float prep_value(const PrepArgs& a, const void* src, const float* mom,
+                                            int64_t i, float inv) {
+  const float g = load_src1<SDT>(src, i);
+  float u = g;
+  if constexpr (MUON) {
+    const float buf = mom[i];
+    u = a.nesterov ? __fadd_rn(__fmul_rn(a.mu, buf), __fmul_rn(a.om, g)) : buf;
+  }
+  return __fmul_rn(u, inv);
+}
+
+// Pass 2 with zero iterations: the normalised matrix is the output (or the
+// update) itself.  Grid (ceil(m/32) * ceil(n/32), 1, batch) over the input's
+// 32x32 tiles, block (32, 8).
+template <int SDT, bool MUON>
 __global__ void __launch_bounds__(256)
-prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ scales) {
-  __shared__ uint16_t tile[32][33];
-  __shared__ uint16_t tile_lo[FMT == 2 ? 32 : 1][33];  // format 2: the lo halves
+prep_output_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ scales) {
   const int b = blockIdx.z;
   const float inv = __ldg(scales + b);
-  const bool tall = (a.tall[b >> 6] >> (b & 63)) & 1ull;  // G = X^T
+  const bool tall = (a.tall[b >> 6] >> (b & 63)) & 1ull;
   const int64_t rows = tall ? a.n : a.m, cols = tall ? a.m : a.n;
   const int64_t tiles_c = (cols + 31) / 32;
   const int64_t tr = blockIdx.x / tiles_c, tc = blockIdx.x - tr * tiles_c;
   const void* src = a.src[b];
   const float* mom = MUON ? a.mom[b] : nullptr;
   const int64_t c = tc * 32 + threadIdx.x;
-  float x[4];
-  bool in[4];
+  void* dst = a.dst[b];
+  const float sc = tall ? a.upd_scale_tall : a.upd_scale_wide;
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {  // loads first, so they overlap
+  for (int k = 0; k < 4; ++k) {
     const int64_t r = tr * 32 + threadIdx.y + 8 * k;
-    in[k] = r < rows && c < cols;
-    x[k] = 0.f;
-    if (in[k]) {
-      const int64_t i = r * cols + c;
-      const float g = load_src1<SDT>(src, i);
-      float u = g;
-      if constexpr (MUON) {
-        const float buf = mom[i];
-        u = a.nesterov ? __fadd_rn(__fmul_rn(a.mu, buf), __fmul_rn(a.om, g)) : buf;
-      }
-      x[k] = __fmul_rn(u, inv);
+    if (r >= rows || c >= cols) continue;
+    const int64_t i = r * cols + c;
+    const float x = prep_value<SDT, MUON>(a, src, mom, i, inv);
+    if (a.dst_dtype == TK_F32) {
+      float* p = static_cast<float*>(dst) + i;
+      *p = a.update ? __fadd_rn(*p, __fmul_rn(sc, x)) : x;
+    } else {
+      uint16_t* p = static_cast<uint16_t*>(dst) + i;
+      *p = f32_to_bf16_bits(a.update ? __fadd_rn(bf16_bits_to_f32(*p), __fmul_rn(sc, x)) : x);
     }
   }
-  if (a.steps == 0) {
-    void* dst = a.dst[b];
-    const float sc = tall ? a.upd_scale_tall : a.upd_scale_wide;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      if (!in[k]) continue;
-      const int64_t i = (tr * 32 + threadIdx.y + 8 * k) * cols + c;
-      if (a.dst_dtype == TK_F32) {
-        float* p = static_cast<float*>(dst) + i;
-        *p = a.update ? __fadd_rn(*p, __fmul_rn(sc, x[k])) : x[k];
-      } else {
-        uint16_t* p = static_cast<uint16_t*>(dst) + i;
-        *p = f32_to_bf16_bits(a.update ? __fadd_rn(bf16_bits_to_f32(*p), __fmul_rn(sc, x[k])) : x[k]);
-      }
-    }
-    return;
-  }
-  // same-layout target: X (wide) or X^T (tall)
+}
+
+// Pass 2: normalise, pre-scale by 2^k, round to the operand type and write X
+// (m x n) and X^T (n x m).  The input G is R x C (m x n for a wide matrix,
+// n x m for a tall one).  Grid (ceil(m/64) * ceil(n/64), 1, batch) over G's
+// 64x64 tiles, 256 threads: thread (q, y) = (tid % 16, tid / 16) takes
+// columns 4q .. 4q+3 of tile rows y, y+16, y+32, y+48 -- a 16-byte momentum
+// load, an 8-byte (bf16) or 16-byte (f32) input load and an 8-byte store
+// into the same-layout target per row when the four are in range and
+// aligned -- and, after a shared-memory transpose, rows 4q .. 4q+3 of tile
+// columns y, y+16, y+32, y+48 into the transposed target, again 8 bytes per
+// store.  Rows of 65 halves keep the transposed reads to two-way bank
+// conflicts.
+template <int SDT, bool MUON, int FMT>
+__global__ void __launch_bounds__(256)
+prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ scales) {
+  constexpr int T = 64, S = T + 1;
+  __shared__ uint16_t tile[T][S];
+  __shared__ uint16_t tile_lo[FMT == 2 ? T : 1][S];  // format 2: the lo halves
+  const int b = blockIdx.z;
+  const float inv = __ldg(scales + b);
+  const bool tall = (a.tall[b >> 6] >> (b & 63)) & 1ull;  // G = X^T
+  const int64_t rows = tall ? a.n : a.m, cols = tall ? a.m : a.n;
+  const int64_t tiles_c = (cols + T - 1) / T;
+  const int64_t r0 = (blockIdx.x / tiles_c) * T, c0 = (blockIdx.x % tiles_c) * T;
+  const void* src = a.src[b];
+  const float* mom = MUON ? a.mom[b] : nullptr;
+  const int q = threadIdx.x & 15, y = threadIdx.x >> 4;
+  // 4-element vector accesses of a row need every row start aligned
+  const bool vec = (cols & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(src) & (SDT == TK_F32 ? 15 : 7)) == 0 &&
+                   (!MUON || (reinterpret_cast<uintptr_t>(mom) & 15) == 0);
+  // same-layout target: X (wide) or X^T (tall); rows are 64-element padded,
+  // so the 4-element stores are 8-byte aligned
   uint16_t* same = tall ? a.xt + (int64_t)b * a.xt_bs : a.x + (int64_t)b * a.x_bs;
   const int64_t same_ld = tall ? a.xt_ld : a.x_ld;
   const int64_t same_lo = tall ? a.xt_lo : a.x_lo;
+  const int64_t c = c0 + 4 * q;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    if (!in[k]) continue;
-    const int64_t r = tr * 32 + threadIdx.y + 8 * k;
-    const float v = __fmul_rn(x[k], a.prescale);
-    const uint16_t h = to_half_bits<FMT>(v);
-    same[r * same_ld + c] = h;
-    tile[threadIdx.y + 8 * k][threadIdx.x] = h;
-    if constexpr (FMT == 2) {  // lo = f16(v - hi); v - hi is exact in f32
-      const uint16_t l = to_half_bits<FMT>(v - from_half_bits<FMT>(h));
-      same[r * same_ld + same_lo + c] = l;
-      tile_lo[threadIdx.y + 8 * k][threadIdx.x] = l;
+    const int ty = y + 16 * k;
+    const int64_t r = r0 + ty;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool whole = r < rows && c + 3 < cols;
+    if (whole && vec) {
+      const int64_t i = r * cols + c;
+      float g[4], buf[4] = {0.f, 0.f, 0.f, 0.f};
+      load_src4<SDT>(src, i, g);
+      if constexpr (MUON) {
+        const float4 m4 = *reinterpret_cast<const float4*>(mom + i);
+        buf[0] = m4.x; buf[1] = m4.y; buf[2] = m4.z; buf[3] = m4.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float u = g[j];
+        if constexpr (MUON)
+          u = a.nesterov ? __fadd_rn(__fmul_rn(a.mu, buf[j]), __fmul_rn(a.om, g[j])) : buf[j];
+        x[j] = __fmul_rn(u, inv);
+      }
+    } else if (r < rows) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (c + j < cols) x[j] = prep_value<SDT, MUON>(a, src, mom, r * cols + c + j, inv);
+    }
+    uint16_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float v = __fmul_rn(x[j], a.prescale);
+      h[j] = to_half_bits<FMT>(v);
+      l[j] = 0;
+      if constexpr (FMT == 2) l[j] = to_half_bits<FMT>(v - from_half_bits<FMT>(h[j]));
+      tile[ty][4 * q + j] = h[j];
+      if constexpr (FMT == 2) tile_lo[ty][4 * q + j] = l[j];
+    }
+    if (whole) {
+      *reinterpret_cast<uint2*>(same + r * same_ld + c) =
+          make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+      if constexpr (FMT == 2)
+        *reinterpret_cast<uint2*>(same + r * same_ld + same_lo + c) =
+            make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+    } else if (r < rows) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (c + j < cols) {
+          same[r * same_ld + c + j] = h[j];
+          if constexpr (FMT == 2) same[r * same_ld + same_lo + c + j] = l[j];
+        }
     }
   }
   __syncthreads();
@@ -933,14 +995,33 @@ prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ 
   uint16_t* other = tall ? a.x + (int64_t)b * a.x_bs : a.xt + (int64_t)b * a.xt_bs;
   const int64_t other_ld = tall ? a.x_ld : a.xt_ld;
   const int64_t other_lo = tall ? a.x_lo : a.xt_lo;
+  const int64_t rr = r0 + 4 * q;  // columns of the target
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int64_t cc = tc * 32 + threadIdx.y + 8 * k;  // row of the target
-    const int64_t rr = tr * 32 + threadIdx.x;           // column of the target
-    if (cc < cols && rr < rows) {
-      other[cc * other_ld + rr] = tile[threadIdx.x][threadIdx.y + 8 * k];
+    const int tx = y + 16 * k;
+    const int64_t cc = c0 + tx;  // row of the target
+    if (cc >= cols) continue;
+    uint16_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      h[j] = tile[4 * q + j][tx];
+      l[j] = 0;
+      if constexpr (FMT == 2) l[j] = tile_lo[4 * q + j][tx];
+    }
+    uint16_t* d = other + cc * other_ld + rr;
+    if (rr + 3 < rows) {
+      *reinterpret_cast<uint2*>(d) =
+          make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
       if constexpr (FMT == 2)
-        other[cc * other_ld + other_lo + rr] = tile_lo[threadIdx.x][threadIdx.y + 8 * k];
+        *reinterpret_cast<uint2*>(d + other_lo) =
+            make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (rr + j < rows) {
+          d[j] = h[j];
+          if constexpr (FMT == 2) d[other_lo + j] = l[j];
+        }
     }
   }
 }
@@ -1147,8 +1228,21 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     TK_CUDA_TRY(cudaGetLastError());
     prep_scale_kernel<<<(unsigned)L.batch, 32, 0, s>>>(partials, L.nblk, scales);
     TK_CUDA_TRY(cudaGetLastError());
-    dim3 g2((unsigned)(((L.m + 31) / 32) * ((L.n + 31) / 32)), 1, (unsigned)L.batch);
-    dim3 b2(32, 8);
+    if (steps == 0) {  // the normalised matrix is the result
+      dim3 g0((unsigned)(((L.m + 31) / 32) * ((L.n + 31) / 32)), 1, (unsigned)L.batch);
+      dim3 b0(32, 8);
+      if (io.src_dtype == TK_F32) {
+        if (muon) prep_output_kernel<TK_F32, true><<<g0, b0, 0, s>>>(pa, scales);
+        else prep_output_kernel<TK_F32, false><<<g0, b0, 0, s>>>(pa, scales);
+      } else {
+        if (muon) prep_output_kernel<TK_BF16, true><<<g0, b0, 0, s>>>(pa, scales);
+        else prep_output_kernel<TK_BF16, false><<<g0, b0, 0, s>>>(pa, scales);
+      }
+      TK_CUDA_TRY(cudaGetLastError());
+      return TK_OK;
+    }
+    dim3 g2((unsigned)(((L.m + 63) / 64) * ((L.n + 63) / 64)), 1, (unsigned)L.batch);
+    dim3 b2(256);
 #define TK_PREP_WRITE(SDT, MU, F) prep_write_kernel<SDT, MU, F><<<g2, b2, 0, s>>>(pa, scales)
 #define TK_PREP_WRITE_FMT(SDT, MU)                   \
   do {                                               \
