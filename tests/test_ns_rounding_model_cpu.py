@@ -11,7 +11,7 @@ One iteration of tikun_b200's Newton-Schulz is three tensor-core GEMMs with
 and from 256 rows up with f16 operands (the folded form):
 
     A = round16(X X^T),  A' = round16(c X X^T + b I)   (one product)
-    B' = round16(A A' + a I)                           (upper tiles, mirrored)
+    B' = round16(A A' + a I)                (upper tiles, mirrored, for m > 512)
     X = round16(B' X)
 
 with X = round16(2^k x / ||x||) first, the pre-scale 2^k undone exactly in

@@ -67,6 +67,19 @@ constexpr uint32_t TMEM_COLS = 512;
 
 constexpr float NS_A = 3.4445f, NS_B = -4.7750f, NS_C = 2.0315f;
 
+// The symmetric products X X^T (GEMM1, over K = n) and A A' (GEMM2, over
+// K = m) compute only the tiles on or above the diagonal and mirror them, or
+// -- up to these K -- every tile, stored once with no mirror stores or
+// transposes.  At short K the epilogues set the pace and the full grid, 1.5x
+// the MMA work, is faster (measured on B200: 48 x 768^2 +9 %, 24 x 1024^2
+// +20 %, 96 x 512^2 +25 %; GEMM2 at K = 768-1024 gained nothing).
+#ifndef TK_NS_FULL_K1
+#define TK_NS_FULL_K1 1024
+#endif
+#ifndef TK_NS_FULL_K2
+#define TK_NS_FULL_K2 512
+#endif
+
 // Epilogues, each on v = alpha*acc (+ gamma*aux when aux is set: a second
 // matrix of the output's shape, read in the epilogue).  SYM: a symmetric
 // product (upper tiles only, mirrored), stored as v + beta*I and, when out2 is
@@ -79,7 +92,8 @@ struct GemmArgs {
   int M, N, K;
   int batch;
   int tiles_m, tiles_n, tiles_per_mat;
-  int symmetric;
+  int symmetric;  // enumerate only the tiles on or above the diagonal
+  int mirror;     // SYM epilogue: store each entry above the diagonal twice
   float alpha, beta;    // SYM: out = alpha*acc + beta*I; XUPD/FINAL: alpha*acc
   float alpha2, beta2;  // SYM with out2: out2 = alpha2*acc + beta2*I
   float gamma;          // weight of aux
@@ -322,6 +336,32 @@ __device__ __forceinline__ void sym_store(const GemmArgs& a, uint16_t* base, int
   }
 }
 
+// A chunk of a symmetric product computed over every tile (no mirror): the
+// row part as it is.
+__device__ __forceinline__ void row_store(const GemmArgs& a, uint16_t* base, int64_t ld,
+                                          uint32_t (&w)[16], int r, int r0, int c0, bool full,
+                                          bool wfull, uint32_t* tsm) {
+  if (wfull) {
+    store_block16(base, ld, r0, c0, 32, w, tsm);
+    return;
+  }
+  if (r >= a.M) return;
+  if (full) {
+    store_words16(base + (int64_t)r * ld + c0, w);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (c0 + j < a.N) base[(int64_t)r * ld + c0 + j] = half_at(w, j);
+}
+
+__device__ __forceinline__ void sym_out(const GemmArgs& a, uint16_t* base, int64_t ld,
+                                        uint32_t (&w)[16], int r, int r0, int c0, bool full,
+                                        bool wfull, uint32_t* tsm) {
+  if (a.mirror) sym_store(a, base, ld, w, r, r0, c0, full, wfull, tsm);
+  else row_store(a, base, ld, w, r, r0, c0, full, wfull, tsm);
+}
+
 // The final parameter update of a 32 x 32 block whose lane l holds the
 // Newton-Schulz output for parameter row row0 + l, columns col0 .. col0+31:
 // p = p + scale * o (or p = o), in the parameter's dtype, locally and into
@@ -461,13 +501,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
       if constexpr (FMT == 2) {
         uint32_t w[16], wl[16];
         pack_split(o, w, wl);
-        sym_store(a, base, a.out_ld, w, r, r0, c0, full, wfull, tsm);
-        sym_store(a, base + a.lo_off, a.out_ld, wl, r, r0, c0, full, wfull, tsm);
+        sym_out(a, base, a.out_ld, w, r, r0, c0, full, wfull, tsm);
+        sym_out(a, base + a.lo_off, a.out_ld, wl, r, r0, c0, full, wfull, tsm);
       } else {
         uint32_t w[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
-        sym_store(a, base, a.out_ld, w, r, r0, c0, full, wfull, tsm);
+        sym_out(a, base, a.out_ld, w, r, r0, c0, full, wfull, tsm);
       }
     }
     if (a.out2 != nullptr) {  // out2 = alpha2*acc + beta2*I
@@ -478,13 +518,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
       if constexpr (FMT == 2) {
         uint32_t w[16], wl[16];
         pack_split(o, w, wl);
-        sym_store(a, base, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
-        sym_store(a, base + a.lo_off2, a.out2_ld, wl, r, r0, c0, full, wfull, tsm);
+        sym_out(a, base, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
+        sym_out(a, base + a.lo_off2, a.out2_ld, wl, r, r0, c0, full, wfull, tsm);
       } else {
         uint32_t w[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
-        sym_store(a, base, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
+        sym_out(a, base, a.out2_ld, w, r, r0, c0, full, wfull, tsm);
       }
     }
     return;
@@ -1288,6 +1328,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   TK_TRY(make_operand(&mXT128[1], XT[1], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
 
   const int tm_sq = (int)((L.m + BM - 1) / BM), tn_sq = (int)((L.m + BN - 1) / BN);
+  const bool mirror1 = L.n > TK_NS_FULL_K1, mirror2 = L.m > TK_NS_FULL_K2;
   const int tm_x = (int)((L.n + BM - 1) / BM);
   const float inv_pre = std::ldexp(1.0f, -k), inv_pre2 = std::ldexp(1.0f, -2 * k);
   int cur_xt = 0;
@@ -1302,8 +1343,8 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     g.K = (int)L.n;
     g.tiles_m = tm_sq;
     g.tiles_n = tn_sq;
-    g.tiles_per_mat = sym_tiles(tm_sq, tn_sq);
-    g.symmetric = 1;
+    g.symmetric = g.mirror = mirror1 ? 1 : 0;
+    g.tiles_per_mat = mirror1 ? sym_tiles(tm_sq, tn_sq) : tm_sq * tn_sq;
     g.alpha = it == 0 ? inv_pre2 : 1.0f;
     g.beta = 0.0f;
     g.out = Am;
@@ -1320,6 +1361,8 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mX128, mX256, g, s));
     // GEMM2: B' = A A' + a I  (bf16: B = c A A + b A)
     g.K = (int)L.m;
+    g.symmetric = g.mirror = mirror2 ? 1 : 0;
+    g.tiles_per_mat = mirror2 ? sym_tiles(tm_sq, tn_sq) : tm_sq * tn_sq;
     g.out = Bm;
     g.out2 = nullptr;
     if (fold) {
