@@ -392,3 +392,68 @@ def test_ns_full_model_shapes_against_torch_fp32(shape, prec):
         assert _native.device_status() == 0
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@pytest.mark.parametrize("prec", [_native.TK_NS_F16, _native.TK_NS_F16X3], ids=["f16", "f16x3"])
+def test_gpt2_muon_workload_full_size(prec):
+    """The GPT-2 Muon workload at full size: 12 layers x {4 x 768^2, 768x3072,
+    3072x768} bf16 matrices through tk_muon_step (momentum 0.95, Nesterov,
+    5 Newton-Schulz steps, lr 0.02) and the wte 50257x768 embedding plus 25
+    LayerNorm vectors through the AdamW step (lr 1e-3, betas 0.9/0.999, eps
+    1e-8, decay 0.01), bf16 parameters and gradients, 3 steps with fresh
+    gradients.  Against the oracle (muon_nd.py:112-126 with f32
+    Newton-Schulz; lib.rs:258-270): the AdamW leaves and every momentum
+    buffer bit-identical; the matrices within 1e-3 relative with split f16
+    operands, within 3e-3 with f16 operands (the bf16-parameter figure and
+    its cause are in this module's docstring)."""
+    rng = np.random.default_rng(2024)
+    mats = ([(768, 768)] * 4 + [(768, 3072), (3072, 768)]) * 12
+    aw_sizes = [50257 * 768] + [768] * 25
+    lr, mu = 0.02, 0.95
+
+    def bf16(a):
+        return oracle.f32_to_bf16(np.ascontiguousarray(a, dtype=np.float32))
+
+    p_ref = [bf16(rng.standard_normal(s) * 0.02) for s in mats]
+    p_dev = [torch.from_numpy(p.view(np.int16).copy()).view(torch.bfloat16).cuda() for p in p_ref]
+    buf_ref = [np.zeros(s, np.float32) for s in mats]
+    mom = [torch.zeros(s, device="cuda") for s in mats]
+    ap_ref = [bf16(rng.standard_normal(n) * 0.02) for n in aw_sizes]
+    ap_dev = [torch.from_numpy(p.view(np.int16).copy()).view(torch.bfloat16).cuda() for p in ap_ref]
+    am_ref = [np.zeros(n, np.float32) for n in aw_sizes]
+    av_ref = [np.zeros(n, np.float32) for n in aw_sizes]
+    am = [torch.zeros(n, device="cuda") for n in aw_sizes]
+    av = [torch.zeros(n, device="cuda") for n in aw_sizes]
+    for step in range(1, 4):
+        g_ref = [bf16(rng.standard_normal(s) * 1e-3) for s in mats]
+        ag_ref = [bf16(rng.standard_normal(n) * 1e-3) for n in aw_sizes]
+        g_dev = [torch.from_numpy(g.view(np.int16).copy()).view(torch.bfloat16).cuda()
+                 for g in g_ref]
+        ag_dev = [torch.from_numpy(g.view(np.int16).copy()).view(torch.bfloat16).cuda()
+                  for g in ag_ref]
+        _native.muon_step([(p.data_ptr(), g.data_ptr(), m.data_ptr(), 1, r, c, _native.TK_BF16,
+                            _native.TK_BF16)
+                           for p, g, m, (r, c) in zip(p_dev, g_dev, mom, mats)],
+                          lr, mu, nesterov=True, ns_steps=5, precision=prec)
+        _native.step_fast_buffers(
+            [t.data_ptr() for t in ap_dev], [t.data_ptr() for t in ag_dev],
+            [t.data_ptr() for t in am], [t.data_ptr() for t in av], aw_sizes, 0.0, "adamw", step,
+            1e-3, 0.9, 0.999, 1e-8, 0.01, p_dtypes=[_native.TK_BF16] * len(aw_sizes),
+            g_dtypes=[_native.TK_BF16] * len(aw_sizes))
+        for i, (r, c) in enumerate(mats):
+            p_ref[i], _ = _muon_oracle_step(p_ref[i], buf_ref[i], oracle.bf16_to_f32(g_ref[i]),
+                                            lr, mu, r, c, 1, True)
+        oracle.step_two_tier(ap_ref, ag_ref, am_ref, av_ref, oracle.ADAMW, 1e-3, 0.9, 0.999,
+                             1e-8, 0.01, step, 0.0, 8)
+    torch.cuda.synchronize()
+    assert _native.device_status() == 0
+    for i in range(len(aw_sizes)):
+        assert_bitexact(to_np(ap_dev[i]), ap_ref[i], f"AdamW leaf {i} p")
+        assert_bitexact(to_np(am[i]), am_ref[i], f"AdamW leaf {i} m")
+        assert_bitexact(to_np(av[i]), av_ref[i], f"AdamW leaf {i} v")
+    worst = 0.0
+    for i in range(len(mats)):
+        assert_bitexact(to_np(mom[i]), buf_ref[i], f"matrix {i} momentum")
+        worst = max(worst, relf(oracle.bf16_to_f32(to_np(p_dev[i])), oracle.bf16_to_f32(p_ref[i])))
+    print(f"worst matrix parameter error after 3 steps: {worst:.3e}")
+    assert worst <= (1e-3 if prec == _native.TK_NS_F16X3 else 3e-3), worst
