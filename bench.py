@@ -613,15 +613,14 @@ def run_pointwise(args, wl, world, rank, dev, torch, dist):
 
 def ns_scratch_bytes(m, n, split=False):
     """Newton-Schulz scratch of one m x n matrix (m <= n), as the library lays
-    it out (rows padded to 64 elements, buffers 256-byte aligned): X, two X^T,
-    A, A' and B in 16-bit (twice as wide with split f16 operands), the norm
+    it out (rows padded to 64 elements, buffers 256-byte aligned): two X^T, A,
+    A' and B in 16-bit (twice as wide with split f16 operands), the norm
     partials and the scale."""
     r64 = lambda x: (x + 63) // 64 * 64  # noqa: E731
     a256 = lambda x: (x + 255) // 256 * 256  # noqa: E731
-    ldx, ldm = r64(n) * (2 if split else 1), r64(m) * (2 if split else 1)
+    ldm = r64(m) * (2 if split else 1)
     nblk = max(1, min(256, (m * n + 16383) // 16384))
-    return (a256(m * ldx * 2) + 2 * a256(n * ldm * 2) + 3 * a256(m * ldm * 2) + a256(8 * nblk)
-            + a256(4) + 256)
+    return 2 * a256(n * ldm * 2) + 3 * a256(m * ldm * 2) + a256(8 * nblk) + a256(4) + 256
 
 
 def muon_host_e2e(args, wl, world, dev, torch, dist, stream, mine, mats, hp, mhp, p_of, g_of,

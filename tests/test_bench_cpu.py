@@ -25,12 +25,14 @@ def test_workload_shapes():
 
 
 def test_ns_scratch_bytes_follow_the_library_layout():
-    # 2(3mn + 3m^2) bytes for 64-multiple shapes, plus 256 f64 norm partials,
-    # the scale and the 256-byte tail
+    # two X^T and A, A', B: 2(2mn + 3m^2) bytes for 64-multiple shapes, plus
+    # 256 f64 norm partials, the scale and the 256-byte tail
     m, n = 4096, 14336
-    assert bench.ns_scratch_bytes(m, n) == 2 * (3 * m * n + 3 * m * m) + 8 * 256 + 256 + 256
+    assert bench.ns_scratch_bytes(m, n) == 2 * (2 * m * n + 3 * m * m) + 8 * 256 + 256 + 256
+    # split f16 operands: the 16-bit buffers twice as wide
+    assert bench.ns_scratch_bytes(m, n, split=True) == 4 * (2 * m * n + 3 * m * m) + 8 * 256 + 512
     # padding: a 17 x 45 matrix uses 64-element rows
-    assert bench.ns_scratch_bytes(17, 45) >= 2 * (17 * 64 + 2 * 45 * 64 + 3 * 17 * 64)
+    assert bench.ns_scratch_bytes(17, 45) >= 2 * (2 * 45 * 64 + 3 * 17 * 64)
 
 
 def test_cpu_reference_arms_run_on_tiny_workloads():

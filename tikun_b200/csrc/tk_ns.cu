@@ -8,16 +8,16 @@
 // "TN" GEMMs, D[M x N] = P[M x K] * Q[N x K]^T, whose operands are all K-major
 // row-major arrays in HBM.  With f16 operands and m >= 256 the polynomial is
 // folded so that no epilogue reads a second matrix:
-//   GEMM1  A = X X^T and A' = c A + b I   P = Q = X    symmetric: upper tiles only
+//   GEMM1  A = X X^T and A' = c A + b I   P = Q = X (read from X^T, MN-major)
 //   GEMM2  B' = A A' + a I                P = A, Q = A' (A' symmetric)
 //   GEMM3  X_new^T = X^T B'               P = X^T, Q = B' (B' symmetric)
 // Below 256 rows (and with bf16 operands) GEMM2 forms B = c A A + b A and
 // GEMM3 X_new^T = X^T B + a X^T, the b A and a X^T terms added in f32 by the
-// epilogues.  GEMM3 produces X_new^T directly; its epilogue stores both X_new^T
-// and X_new (a transposed store, which the one-row-per-thread TMEM layout makes
-// coalesced), so no operand ever needs the MN-major layout.  Symmetric tiles
-// store each element above the diagonal twice (at (r, c) and (c, r)), which
-// keeps A and B exactly symmetric in storage.
+// epilogues.  GEMM3 produces X_new^T directly and stores only that; GEMM1
+// reads X^T as both of its operands in the MN-major layout (64 x 64 TMA boxes
+// of X^T, K along its rows), so no m x n copy of X is ever written.  Symmetric
+// tiles store each element above the diagonal twice (at (r, c) and (c, r)),
+// which keeps A and B exactly symmetric in storage.
 //
 // Kernel: persistent, one CTA per SM, 320 threads.  Warp 0 issues TMA loads of
 // 128x64 and 256x64 operand tiles (128-byte swizzle, no multicast) into a
@@ -559,6 +559,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
           for (int j = 0; j < 32; ++j)
             if (c0 + j < a.N) d1[j] = half_at(ww, j);
         }
+        if (a.out2 == nullptr) continue;  // no transposed copy wanted
         uint16_t* d2 = a.out2 + (int64_t)b * a.out2_bs + (part == 0 ? 0 : a.lo_off2);
         if (wfull) {
           warp_transpose16(tsm, ww);
@@ -622,7 +623,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
 }
 
 // ------------------------------------------------------------------ GEMM kernel
-template <int EPI, int FMT>
+template <int EPI, int FMT, bool MN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmA_lo, const __grid_constant__ CUtensorMap tmB_lo,
@@ -695,8 +696,20 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const CUtensorMap* mb = seg == 1 ? &tmB_lo : &tmB;
           uint8_t* st = smem + stage * STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_3d(st, ma, &full[stage], kb * BK, tm * BM, b);
-          tma_load_3d(st + A_TILE_BYTES, mb, &full[stage], kb * BK, tn * BN, b);
+          if constexpr (MN) {
+            // operands stored K x MN (rows along K): 64-element MN atoms of
+            // 64 K rows, 8 KB each -- 2 for A, 4 for B
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_3d(st + j * 8192, ma, &full[stage], tm * BM + 64 * j, kb * BK, b);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(st + A_TILE_BYTES + j * 8192, mb, &full[stage], tn * BN + 64 * j,
+                          kb * BK, b);
+          } else {
+            tma_load_3d(st, ma, &full[stage], kb * BK, tm * BM, b);
+            tma_load_3d(st + A_TILE_BYTES, mb, &full[stage], kb * BK, tn * BN, b);
+          }
           issued |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == STAGES) {
@@ -715,7 +728,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      constexpr uint32_t IDESC = idesc_f16(FMT == 1 ? 1 : 0, BM, BN);
+      constexpr uint32_t IDESC =
+          MN ? idesc_f16_mn(FMT == 1 ? 1 : 0, BM, BN) : idesc_f16(FMT == 1 ? 1 : 0, BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -736,11 +750,20 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
-          const uint64_t da = smem_desc_k_sw128(sa);
-          const uint64_t db = smem_desc_k_sw128(sa + A_TILE_BYTES);
+          if constexpr (MN) {
+            // a K step of 16 rows is 2048 bytes (two 8-row groups)
+            const uint64_t da = smem_desc_mn_sw128(sa, 8192);
+            const uint64_t db = smem_desc_mn_sw128(sa + A_TILE_BYTES, 8192);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16(d, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < BK / 16; ++k)
+              umma_f16(d, da + 128 * k, db + 128 * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+          } else {
+            const uint64_t da = smem_desc_k_sw128(sa);
+            const uint64_t db = smem_desc_k_sw128(sa + A_TILE_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_f16(d, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -943,9 +966,9 @@ prep_output_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__
   }
 }
 
-// Pass 2: normalise, pre-scale by 2^k, round to the operand type and write X
-// (m x n) and X^T (n x m).  The input G is R x C (m x n for a wide matrix,
-// n x m for a tall one).  Grid (ceil(m/64) * ceil(n/64), 1, batch) over G's
+// Pass 2: normalise, pre-scale by 2^k, round to the operand type and write
+// X^T (n x m).  The input G is R x C (m x n for a wide matrix, n x m for a
+// tall one).  Grid (ceil(m/64) * ceil(n/64), 1, batch) over G's
 // 64x64 tiles, 256 threads: thread (q, y) = (tid % 16, tid / 16) takes
 // columns 4q .. 4q+3 of tile rows y, y+16, y+32, y+48 -- a 16-byte momentum
 // load, an 8-byte (bf16) or 16-byte (f32) input load and an 8-byte store
@@ -973,11 +996,14 @@ prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ 
   const bool vec = (cols & 3) == 0 &&
                    (reinterpret_cast<uintptr_t>(src) & (SDT == TK_F32 ? 15 : 7)) == 0 &&
                    (!MUON || (reinterpret_cast<uintptr_t>(mom) & 15) == 0);
-  // same-layout target: X (wide) or X^T (tall); rows are 64-element padded,
-  // so the 4-element stores are 8-byte aligned
-  uint16_t* same = tall ? a.xt + (int64_t)b * a.xt_bs : a.x + (int64_t)b * a.x_bs;
-  const int64_t same_ld = tall ? a.xt_ld : a.x_ld;
-  const int64_t same_lo = tall ? a.xt_lo : a.x_lo;
+  // The target is X^T, the only copy of the iterate the GEMMs read: a tall
+  // input already has its layout (stored as it is); a wide one is stored
+  // through the shared-memory transpose.  X^T rows are 64-element padded, so
+  // the 4-element stores are 8-byte aligned.
+  uint16_t* xt = a.xt + (int64_t)b * a.xt_bs;
+  const bool want_same = tall, want_other = !tall;
+  uint16_t* same = xt;
+  const int64_t same_ld = a.xt_ld, same_lo = a.xt_lo;
   const int64_t c = c0 + 4 * q;
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -1015,7 +1041,8 @@ prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ 
       tile[ty][4 * q + j] = h[j];
       if constexpr (FMT == 2) tile_lo[ty][4 * q + j] = l[j];
     }
-    if (whole) {
+    if (!want_same) {
+    } else if (whole) {
       *reinterpret_cast<uint2*>(same + r * same_ld + c) =
           make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
       if constexpr (FMT == 2)
@@ -1031,10 +1058,10 @@ prep_write_kernel(const __grid_constant__ PrepArgs a, const float* __restrict__ 
     }
   }
   __syncthreads();
+  if (!want_other) return;
   // transposed target: element (r, c) of G goes to row c, column r
-  uint16_t* other = tall ? a.x + (int64_t)b * a.x_bs : a.xt + (int64_t)b * a.xt_bs;
-  const int64_t other_ld = tall ? a.x_ld : a.xt_ld;
-  const int64_t other_lo = tall ? a.x_lo : a.xt_lo;
+  uint16_t* other = xt;
+  const int64_t other_ld = a.xt_ld, other_lo = a.xt_lo;
   const int64_t rr = r0 + 4 * q;  // columns of the target
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
@@ -1114,7 +1141,7 @@ static thread_local int g_gemm_reserved_sms = 0;
 void set_gemm_reserved_sms(int n) { g_gemm_reserved_sms = n < 0 ? 0 : n; }
 
 // ma_lo / mb_lo: the lo halves' maps in format 2 (the same maps otherwise).
-template <int EPI, int FMT>
+template <int EPI, int FMT, bool MN = false>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma_lo,
                        const CUtensorMap& mb_lo, const GemmArgs& g, cudaStream_t s) {
   static bool attr_set[64] = {};
@@ -1122,7 +1149,7 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   TK_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
   if (!attr_set[dev]) {
-    TK_CUDA_TRY(cudaFuncSetAttribute(gemm_tn_kernel<EPI, FMT>,
+    TK_CUDA_TRY(cudaFuncSetAttribute(gemm_tn_kernel<EPI, FMT, MN>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     attr_set[dev] = true;
   }
@@ -1131,7 +1158,7 @@ static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   const int n_tiles = g.batch * g.tiles_per_mat;
   if (n_tiles == 0) return TK_OK;
   const int grid = std::min(n_tiles, std::max(1, sms - g_gemm_reserved_sms));
-  gemm_tn_kernel<EPI, FMT><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, ma_lo, mb_lo, g);
+  gemm_tn_kernel<EPI, FMT, MN><<<grid, THREADS, SMEM_BYTES, s>>>(ma, mb, ma_lo, mb_lo, g);
   TK_CUDA_TRY(cudaGetLastError());
   return TK_OK;
 }
@@ -1141,12 +1168,12 @@ struct Operand {
   CUtensorMap hi, lo;
 };
 
-template <int EPI>
+template <int EPI, bool MN = false>
 static int launch_gemm_fmt(int fmt, const Operand& a, const Operand& b, const GemmArgs& g,
                            cudaStream_t s) {
-  if (fmt == 2) return launch_gemm<EPI, 2>(a.hi, b.hi, a.lo, b.lo, g, s);
-  return fmt == 0 ? launch_gemm<EPI, 0>(a.hi, b.hi, a.hi, b.hi, g, s)
-                  : launch_gemm<EPI, 1>(a.hi, b.hi, a.hi, b.hi, g, s);
+  if (fmt == 2) return launch_gemm<EPI, 2, MN>(a.hi, b.hi, a.lo, b.lo, g, s);
+  return fmt == 0 ? launch_gemm<EPI, 0, MN>(a.hi, b.hi, a.hi, b.hi, g, s)
+                  : launch_gemm<EPI, 1, MN>(a.hi, b.hi, a.hi, b.hi, g, s);
 }
 
 static int launch_gemm_epi(int epi, int fmt, const Operand& a, const Operand& b,
@@ -1179,16 +1206,13 @@ GroupLayout group_layout(int64_t m, int64_t n, int64_t batch, bool split) {
   L.n = n;
   L.batch = batch;
   L.split = split;
-  L.ldx = round_up(L.n, 64);
   L.ldm = round_up(L.m, 64);
   // format 2: each row holds the hi values, then the lo values
-  L.rsx = split ? 2 * L.ldx : L.ldx;
   L.rsm = split ? 2 * L.ldm : L.ldm;
-  L.x_bytes = align256((size_t)(batch * L.m * L.rsx * 2));
   L.xt_bytes = align256((size_t)(batch * L.n * L.rsm * 2));
   L.a_bytes = align256((size_t)(batch * L.m * L.rsm * 2));
   L.nblk = (int)std::max<int64_t>(1, std::min<int64_t>(256, (m * n + 16383) / 16384));
-  L.scratch_bytes = L.x_bytes + 2 * L.xt_bytes + 3 * L.a_bytes +
+  L.scratch_bytes = 2 * L.xt_bytes + 3 * L.a_bytes +
                     align256(sizeof(double) * batch * L.nblk) + align256(sizeof(float) * batch) +
                     256;
   return L;
@@ -1210,8 +1234,6 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   if (L.split != (fmt == 2))
     return set_error(TK_ERR_INVALID, "scratch layout does not match operand format %d", fmt);
   char* cur = static_cast<char*>(scratch);
-  uint16_t* X = reinterpret_cast<uint16_t*>(cur);
-  cur += L.x_bytes;
   uint16_t* XT[2] = {reinterpret_cast<uint16_t*>(cur),
                      reinterpret_cast<uint16_t*>(cur + L.xt_bytes)};
   cur += 2 * L.xt_bytes;
@@ -1240,10 +1262,6 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   pa.mu = io.mu;
   pa.om = io.om;
   pa.nesterov = io.nesterov;
-  pa.x = X;
-  pa.x_ld = L.rsx;
-  pa.x_bs = L.m * L.rsx;
-  pa.x_lo = L.ldx;
   pa.xt = XT[0];
   pa.xt_ld = L.rsm;
   pa.xt_bs = L.n * L.rsm;
@@ -1317,15 +1335,18 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   // Split operands (format 2) keep every stored value to about 22 bits, so
   // the folded form's roundings cost nothing there and it is used at all sizes.
   const bool fold = fmt == 2 || (fmt == 0 && L.m >= 256);
-  Operand mX128, mX256, mA128, mA256, mAp256, mB256, mXT128[2];
-  TK_TRY(make_operand(&mX128, X, fmt, L.n, L.m, L.rsx, L.ldx, L.batch, 128));
-  TK_TRY(make_operand(&mX256, X, fmt, L.n, L.m, L.rsx, L.ldx, L.batch, 256));
+  // GEMM1 (X X^T) reads X^T as both operands, MN-major: 64 x 64 boxes of
+  // X^T's rows (K = n) and columns (M, N = m), so that no m x n copy of X is
+  // ever written -- GEMM3 stores only X_new^T.
+  Operand mA128, mA256, mAp256, mB256, mXT128[2], mXTmn[2];
   TK_TRY(make_operand(&mA128, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 128));
   TK_TRY(make_operand(&mA256, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
   TK_TRY(make_operand(&mAp256, Ap, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
   TK_TRY(make_operand(&mB256, Bm, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
-  TK_TRY(make_operand(&mXT128[0], XT[0], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
-  TK_TRY(make_operand(&mXT128[1], XT[1], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
+  for (int q = 0; q < 2; ++q) {
+    TK_TRY(make_operand(&mXT128[q], XT[q], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
+    TK_TRY(make_operand(&mXTmn[q], XT[q], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 64));
+  }
 
   const int tm_sq = (int)((L.m + BM - 1) / BM), tn_sq = (int)((L.m + BN - 1) / BN);
   const bool mirror1 = L.n > TK_NS_FULL_K1, mirror2 = L.m > TK_NS_FULL_K2;
@@ -1358,7 +1379,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       g.out2_ld = L.rsm;
       g.out2_bs = L.m * L.rsm;
     }
-    TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mX128, mX256, g, s));
+    TK_TRY((launch_gemm_fmt<EPI_SYM, true>(fmt, mXTmn[cur_xt], mXTmn[cur_xt], g, s)));
     // GEMM2: B' = A A' + a I  (bf16: B = c A A + b A)
     g.K = (int)L.m;
     g.symmetric = g.mirror = mirror2 ? 1 : 0;
@@ -1390,7 +1411,6 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     h.symmetric = 0;
     h.alpha = it == 0 ? inv_pre : 1.0f;
     h.lo_off = L.ldm;   // X^T rows
-    h.lo_off2 = L.ldx;  // X rows
     if (!fold) {  // + a X^T
       h.gamma = NS_A * h.alpha;
       h.aux = XT[cur_xt];
@@ -1401,9 +1421,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       h.out = XT[cur_xt ^ 1];
       h.out_ld = L.rsm;
       h.out_bs = L.n * L.rsm;
-      h.out2 = X;
-      h.out2_ld = L.rsx;
-      h.out2_bs = L.m * L.rsx;
+      h.out2 = nullptr;  // GEMM1 reads X^T directly
       TK_TRY(launch_gemm_epi(EPI_XUPD, fmt, mXT128[cur_xt], mB256, h, s));
       cur_xt ^= 1;
     } else {

@@ -17,16 +17,17 @@ namespace ns {
 constexpr int kMaxBatch = 256;
 
 // Scratch layout of one batch of matrices that are all m x n or n x m
-// (m <= n): X is m x n, two X^T buffers (ping-pong) are n x m, and A, A' and
-// B are m x m, all half precision with rows padded to a multiple of 64
-// elements (ldx, ldm).  With split operands (format 2) each row holds ld hi
-// values followed by ld lo values: row strides rsx = 2 ldx, rsm = 2 ldm.
+// (m <= n): two X^T buffers (ping-pong) are n x m, and A, A' and B are m x m,
+// all half precision with rows padded to a multiple of 64 elements (ldm).  No
+// m x n copy of X exists: X X^T reads X^T MN-major.  With split operands
+// (format 2) each row holds ldm hi values followed by ldm lo values: row
+// stride rsm = 2 ldm.
 struct GroupLayout {
   int64_t m, n, batch;
-  int64_t ldx, ldm;
-  int64_t rsx, rsm;
+  int64_t ldm;
+  int64_t rsm;
   bool split;
-  size_t x_bytes, xt_bytes, a_bytes;
+  size_t xt_bytes, a_bytes;
   int nblk;
   size_t scratch_bytes;
 };
@@ -56,10 +57,8 @@ struct PrepArgs {
   int64_t m, n;
   float mu, om;
   int nesterov;
-  uint16_t* x;
-  int64_t x_ld, x_bs, x_lo;  // x_lo, xt_lo: offset of the lo values (split operands)
   uint16_t* xt;
-  int64_t xt_ld, xt_bs, xt_lo;
+  int64_t xt_ld, xt_bs, xt_lo;  // xt_lo: offset of the lo values (split operands)
   float prescale;
   int steps;
   int dst_dtype;

@@ -209,10 +209,32 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory descriptor of an MN-major operand tile in the 128-byte swizzle
+// layout: K rows of 128 bytes (64 half-precision elements along M or N),
+// 8-row K groups 1024 bytes apart (stride byte offset), 64-element MN atoms
+// `atom_bytes` apart (leading byte offset), descriptor version 1, layout type
+// 2.  The tile base is 1024-aligned; stepping K by 16 rows adds 2048 bytes to
+// the start address.  (Checked on B200 against a host product, both operands
+// MN-major.)
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t atom_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((atom_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16: f32 accumulator, A and B of the same
 // type (0 = f16, 1 = bf16), both K-major, M x N tile.
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_format, uint32_t m, uint32_t n) {
   return (1u << 4) | (ab_format << 7) | (ab_format << 10) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// The same with both A and B MN-major (bits 15 and 16).
+__host__ __device__ constexpr uint32_t idesc_f16_mn(uint32_t ab_format, uint32_t m, uint32_t n) {
+  return idesc_f16(ab_format, m, n) | (1u << 15) | (1u << 16);
 }
 
 }  // namespace sm100
