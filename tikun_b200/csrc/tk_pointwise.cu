@@ -72,12 +72,14 @@ using namespace pw;
 #endif
 constexpr int kThreads = 256;
 
-// PEER: the variant that also stores every updated parameter into the peers'
-// copies over NVLink.  It keeps the settings measured for it before the
-// local update was retuned (4 quads with 2 CTAs per SM for f32, 2 quads with
-// 3 CTAs for bf16, not pipelined): with 6 CTAs of 40 registers the bf16
+// PEER: the instantiation launched when updated parameters also go to the
+// peers' copies over NVLink.  It keeps the settings measured for it before
+// the local update was retuned (4 quads with 2 CTAs per SM for f32, 2 quads
+// with 3 CTAs for bf16, not pipelined): with 6 CTAs of 40 registers the bf16
 // variant's seven peer stores per quad spilled, and the 2-GPU Muon+AdamW step
-// lost 9 ms to it.
+// lost 9 ms to it.  Both instantiations keep the (runtime) peer-store loop:
+// compiled without it, the pipelined f32 loop was scheduled into 224
+// registers instead of 235 and ran 8 % slower.
 template <int PDT, int GDT, bool PEER = false>
 struct Tune {
   static constexpr bool all_f32 = PDT == TK_F32 && GDT == TK_F32;
@@ -274,11 +276,9 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         }
         const uint64_t e = (lq + (uint64_t)u * kThreads) * 4;
         store_quad<PDT>(L.p, e, B.P[u]);
-        if constexpr (PEER) {
 #pragma unroll
-          for (int r = 0; r < kMaxPeers; ++r)  // the updated parameters, into each peer's copy
-            if (r < peers.n) store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, B.P[u]);
-        }
+        for (int r = 0; r < kMaxPeers; ++r)  // the updated parameters, into each peer's copy
+          if (r < peers.n) store_quad<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, B.P[u]);
         store_quad<TK_F32>(L.m, e, B.M[u]);
         if constexpr (KIND == TK_ADAMW) store_quad<TK_F32>(L.v, e, B.V[u]);
       }
@@ -312,11 +312,9 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
         if constexpr (KIND == TK_ADAMW) v = L.v[e];
         apply<KIND>(p, g, m, v, k);
         store1<PDT>(L.p, e, p);
-        if constexpr (PEER) {
 #pragma unroll
-          for (int r = 0; r < kMaxPeers; ++r)
-            if (r < peers.n) store1<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, p);
-        }
+        for (int r = 0; r < kMaxPeers; ++r)
+          if (r < peers.n) store1<PDT>(static_cast<char*>(L.p) + peers.delta[r], e, p);
         L.m[e] = m;
         if constexpr (KIND == TK_ADAMW) L.v[e] = v;
       }
@@ -324,9 +322,7 @@ pointwise_kernel(const __grid_constant__ LeafTable t, const PointwiseConsts k,
     q = seg_end;
     ++li;
   }
-  if constexpr (PEER) {
-    if (peers.n) __threadfence_system();  // peer stores visible before the kernel ends
-  }
+  if (peers.n) __threadfence_system();  // peer stores visible before the kernel ends
 }
 
 template <int KIND, int PDT, int GDT, int SCALE, bool PEER>
