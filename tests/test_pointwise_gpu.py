@@ -658,3 +658,75 @@ def test_torch_optimizer_adamw_matches_oracle_and_resumes():
     opt_b.step()
     for a, b in zip(params, params_b):
         assert torch.equal(a.detach(), b.detach())
+
+
+def test_step_arena_over_host_arenas():
+    """The reference's MemoryArena is host memory (a Vec<f32>,
+    crates/tikun-core/src/arena.rs:69-80): tk_step_arena over four NumPy
+    arenas (staged through the device by the engine) gives the oracle's bytes
+    for every slot, over 3 clipped AdamW steps, and leaves the padding alone."""
+    sizes = [100, 513, 2048, 17, 4099]  # the reference's own alignment-test shapes and more
+    offs, total_bytes = _native.layout_from_shapes(sizes)
+    n_el = (total_bytes + 3) // 4
+    rng = np.random.default_rng(77)
+    P = np.full(n_el, np.nan, np.float32)
+    G = np.zeros(n_el, np.float32)
+    M = np.zeros(n_el, np.float32)
+    V = np.zeros(n_el, np.float32)
+    for o, n in zip(offs, sizes):
+        P[o // 4:o // 4 + n] = rng.standard_normal(n).astype(np.float32) * 0.02
+    ref_p = [P[o // 4:o // 4 + n].copy() for o, n in zip(offs, sizes)]
+    ref_m = [np.zeros(n, np.float32) for n in sizes]
+    ref_v = [np.zeros(n, np.float32) for n in sizes]
+    hp = _native.TkHParams(1e-3, 0.9, 0.999, 1e-8, 0.01)
+    U64 = ctypes.c_uint64 * len(sizes)
+    pipe = _native.TkPipeline((_native.TkScheduleNode * 3)(
+        _native.TkScheduleNode(b"load_g", 0, 64, 4, 8, 2),
+        _native.TkScheduleNode(b"fma_opt", 1, 64, 4, 8, 2),
+        _native.TkScheduleNode(b"store_p", 2, 64, 4, 8, 2)), 3, 1.0)
+    for step in range(1, 4):
+        g = [(rng.standard_normal(n) * 0.1).astype(np.float32) for n in sizes]
+        for (o, n), gi in zip(zip(offs, sizes), g):
+            G[o // 4:o // 4 + n] = gi
+        out = ctypes.c_float()
+        _native.check(_native.lib().tk_step_arena(
+            ctypes.byref(pipe), P.ctypes.data, G.ctypes.data, M.ctypes.data, V.ctypes.data,
+            n_el * 4, U64(*offs), U64(*sizes), len(sizes), _native.TK_ADAMW, ctypes.byref(hp),
+            step, ctypes.byref(out), None))
+        ref = oracle.step_two_tier(ref_p, g, ref_m, ref_v, oracle.ADAMW, 1e-3, 0.9, 0.999, 1e-8,
+                                   0.01, step, 1.0)
+        assert out.value == ref and ref < 1.0
+    covered = np.zeros(n_el, bool)
+    for i, (o, n) in enumerate(zip(offs, sizes)):
+        assert_bitexact(P[o // 4:o // 4 + n], ref_p[i], f"slot {i} p")
+        assert_bitexact(V[o // 4:o // 4 + n], ref_v[i], f"slot {i} v")
+        covered[o // 4:o // 4 + n] = True
+    assert np.isnan(P[~covered]).all(), "padding between slots was written"
+
+
+def test_arena_mode_bf16_parameters_match_per_leaf_front_end():
+    """UniversalOptimizer(arena=True) with bf16 parameters and gradients: the
+    arenas are bf16 for p and g, f32 for the moments; 3 clipped steps give the
+    same bytes as the per-leaf front-end."""
+    import tikun_b200
+
+    gen = torch.Generator().manual_seed(9)
+    sizes = [(768, 64), (64,), (1000, 3), (5,)]
+    init = [(torch.randn(*s, generator=gen) * 0.02).bfloat16() for s in sizes]
+    pa = [t.clone().cuda().requires_grad_(True) for t in init]
+    pb = [t.clone().cuda().requires_grad_(True) for t in init]
+    oa = tikun_b200.AdamW(pa, lr=1e-2, max_norm=0.5, arena=True)
+    ob = tikun_b200.AdamW(pb, lr=1e-2, max_norm=0.5)
+    for _ in range(3):
+        grads = [(torch.randn(*s, generator=gen) * 0.1).bfloat16().cuda() for s in sizes]
+        with torch.no_grad():
+            for p, g in zip(pa, grads):
+                p.grad.copy_(g)
+        for p, g in zip(pb, grads):
+            p.grad = g.clone()
+        oa.step()
+        ob.step()
+    torch.cuda.synchronize()
+    assert float(oa.clip_scale) == float(ob.clip_scale) < 1.0
+    for a, b in zip(pa, pb):
+        assert torch.equal(a.detach().view(torch.int16), b.detach().view(torch.int16))
