@@ -593,11 +593,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
         return;
       }
       // edges and unaligned parameters: element by element; element j is at
-      // i0 + j * stride
+      // i0 + j * stride.  Both loops are unrolled so that o stays in
+      // registers (indexed at run time it would live in local memory, and
+      // the block path above would read it from there too).
       const int64_t i0 = tall ? (int64_t)r * a.N + c0 : (int64_t)c0 * a.M + r;
       const int64_t stride = tall ? 1 : a.M;
       if (a.fin_dtype == TK_F32) {
         float* p = static_cast<float*>(dst);
+#pragma unroll
         for (int j = 0; j < 32; ++j)
           if (c0 + j < a.N) {
             float* pj = p + i0 + j * stride;
@@ -608,6 +611,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
           }
       } else {
         uint16_t* p = static_cast<uint16_t*>(dst);
+#pragma unroll
         for (int j = 0; j < 32; ++j)
           if (c0 + j < a.N) {
             uint16_t* pj = p + i0 + j * stride;
