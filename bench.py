@@ -992,7 +992,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
                      "batch into peer arenas during the next batch; the AdamW update "
                      "kernel stores into them",
              "allgather": "all-gathers after the updates"}[exchange]),
-        "roofline": {"bound": "tensor", "kernel": "gemm_tn_kernel (Newton-Schulz GEMMs)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_pair_kernel (m >= 1024) / gemm_tn_kernel (Newton-Schulz GEMMs)",
                      "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                      "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
                      "flops": "dense-equivalent 5(4m^2n+2m^3) per matrix",

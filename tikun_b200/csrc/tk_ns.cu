@@ -64,6 +64,14 @@ constexpr int TRANS_BYTES = EPI_WARPS * TRANS_WORDS * 4;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + TRANS_BYTES + 1024;
 constexpr int THREADS = 64 + 32 * 8;  // producer, MMA issuer, 8 epilogue warps
 constexpr uint32_t TMEM_COLS = 512;
+// CTA-pair kernel: 256 x 256 tiles over two CTAs, each loading 128 rows of A
+// and of B per K block into a 6-stage ring of 32 KB stages.
+constexpr int P_BM = 256, P_BN = 256, P_HALF = 128, P_STAGES = 6;
+constexpr int P_A_BYTES = P_HALF * BK * 2;
+constexpr int P_STAGE_BYTES = 2 * P_A_BYTES;
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 256 + TRANS_BYTES + 1024;
+static_assert(P_SMEM_BYTES <= 232448, "pair kernel shared memory above the 227 KB limit");
+static_assert(SMEM_BYTES <= 232448, "kernel shared memory above the 227 KB limit");
 
 constexpr float NS_A = 3.4445f, NS_B = -4.7750f, NS_C = 2.0315f;
 
@@ -78,6 +86,14 @@ constexpr float NS_A = 3.4445f, NS_B = -4.7750f, NS_C = 2.0315f;
 #endif
 #ifndef TK_NS_FULL_K2
 #define TK_NS_FULL_K2 512
+#endif
+// Matrices with at least this many rows (m, after the transpose of a tall
+// one) run on the CTA-pair kernel; smaller ones on the single-CTA kernel.
+// Measured on B200 over whole Newton-Schulz calls (pair against single):
+// 8 x 4096^2 +8 %, 6 x 2048 x 8192 +5 %, 16 x 4096 x 1024 +5 %, 24 x 1024^2
+// +3 %; 48 x 768^2 -1 %, 12 x 768 x 3072 -2 %, 96 x 512^2 -9 %.
+#ifndef TK_NS_PAIR_MIN_M
+#define TK_NS_PAIR_MIN_M 1024
 #endif
 
 // Epilogues, each on v = alpha*acc (+ gamma*aux when aux is set: a second
@@ -824,6 +840,256 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   }
 }
 
+// ------------------------------------------------------------------ CTA-pair GEMM kernel
+// The same GEMMs on 256 x 256 tiles computed by a cluster of two CTAs with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16).  Each CTA loads 128
+// rows of A and 128 rows of B per K block -- 32 KB instead of the 48 KB a
+// single CTA needs for its 128 x 256 tile -- so the same tensor work draws a
+// third less operand traffic into each SM, and six stages fit in the ring.
+// The leader (even CTA) issues every MMA and commits each stage to both CTAs'
+// "empty" barriers; both CTAs' TMA bytes count on the leader's "full"
+// barrier; each CTA's epilogue drains its own 128 accumulator rows and
+// arrives on the leader's "tmem empty" barrier.
+__device__ __forceinline__ void decode_tile_pair(const GemmArgs& a, int t, int& b, int& tm,
+                                                 int& tn) {
+  b = t / a.tiles_per_mat;
+  int r = t - b * a.tiles_per_mat;
+  if (!a.symmetric) {
+    tm = r / a.tiles_n;
+    tn = r - tm * a.tiles_n;
+    return;
+  }
+  // square tiles: row block i holds column blocks i .. tiles_n-1
+  for (int i = 0; i < a.tiles_m; ++i) {
+    const int cnt = a.tiles_n - i;
+    if (r < cnt) {
+      tm = i;
+      tn = i + r;
+      return;
+    }
+    r -= cnt;
+  }
+  tm = a.tiles_m;  // unreachable for a valid tile index
+  tn = 0;
+}
+
+__host__ __device__ inline int sym_tiles_pair(int tiles_m, int tiles_n) {
+  int s = 0;
+  for (int i = 0; i < tiles_m; ++i) s += tiles_n - i;
+  return s;
+}
+
+template <int EPI, int FMT, bool MN>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmA_lo,
+                 const __grid_constant__ CUtensorMap tmB_lo, const __grid_constant__ GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t* empty = full + P_STAGES;
+  uint64_t* tfull = empty + P_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);  // the leader's producer; both CTAs' bytes
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&tfull[s], 1);
+      mbar_init(&tempty[s], 2 * EPI_WARPS);  // both CTAs' epilogue warps
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if constexpr (FMT == 2) {
+      tma_prefetch_desc(&tmA_lo);
+      tma_prefetch_desc(&tmB_lo);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised in both CTAs before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int n_tiles = args.batch * args.tiles_per_mat;
+  const int cl = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(cluster_count_x());
+  const int num_kb = (args.K + BK - 1) / BK;
+  constexpr int kSegments = FMT == 2 ? 3 : 1;
+  const int total_kb = num_kb * kSegments;
+  const int row_half = static_cast<int>(rank) * P_HALF;  // this CTA's rows of A and of B
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued = 0, issued_parity = 0;
+      for (int t = cl; ok && t < n_tiles; t += ncl) {
+        int b, tm, tn;
+        decode_tile_pair(args, t, b, tm, tn);
+        for (int kt = 0; kt < total_kb; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err, 1)) {
+            ok = false;
+            break;
+          }
+          const int seg = kt / num_kb, kb = kt - seg * num_kb;
+          const CUtensorMap* ma = seg == 2 ? &tmA_lo : &tmA;
+          const CUtensorMap* mb = seg == 1 ? &tmB_lo : &tmB;
+          uint8_t* st = smem + stage * P_STAGE_BYTES;
+          const uint32_t bar = full_leader + static_cast<uint32_t>(stage * 8);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          const int ra = tm * P_BM + row_half, rb = tn * P_BN + row_half;
+          if constexpr (MN) {
+#pragma unroll
+            for (int j = 0; j < P_HALF / 64; ++j)
+              tma_load_3d_pair(st + j * 8192, ma, bar, ra + 64 * j, kb * BK, b);
+#pragma unroll
+            for (int j = 0; j < P_HALF / 64; ++j)
+              tma_load_3d_pair(st + P_A_BYTES + j * 8192, mb, bar, rb + 64 * j, kb * BK, b);
+          } else {
+            tma_load_3d_pair(st, ma, bar, kb * BK, ra, b);
+            tma_load_3d_pair(st + P_A_BYTES, mb, bar, kb * BK, rb, b);
+          }
+          issued |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // give up: let the copies already issued land before shared memory
+        // is released.  The leader sees them on its own barriers; the other
+        // CTA's bytes also count there, so it waits out a fixed 2 ms instead.
+        if (leader) {
+          for (int st = 0; st < P_STAGES; ++st)
+            if (issued & (1u << st)) wait_no_abort(&full[st], (issued_parity >> st) & 1u);
+        } else {
+          const unsigned long long t0 = globaltimer();
+          while (globaltimer() - t0 < 2000000ull) __nanosleep(100000);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (the leader only)
+      constexpr uint32_t IDESC = MN ? idesc_f16_mn(FMT == 1 ? 1 : 0, P_BM, P_BN)
+                                    : idesc_f16(FMT == 1 ? 1 : 0, P_BM, P_BN);
+      const uint32_t empty0 = mapa_shared(smem_u32(empty), 0), empty1 = mapa_shared(smem_u32(empty), 1);
+      const uint32_t tfull0 = mapa_shared(smem_u32(tfull), 0), tfull1 = mapa_shared(smem_u32(tfull), 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int t = cl; ok && t < n_tiles; t += ncl, ++it) {
+        const int acc = it & 1;
+        const uint32_t use = static_cast<uint32_t>(it >> 1);
+        if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, abort_flag, args.err, 2)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * P_BN);
+        for (int kb = 0; kb < total_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, args.err, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * P_STAGE_BYTES);
+          if constexpr (MN) {
+            const uint64_t da = smem_desc_mn_sw128(sa, 8192);
+            const uint64_t db = smem_desc_mn_sw128(sa + P_A_BYTES, 8192);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_f16_pair(d, da + 128 * k, db + 128 * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+          } else {
+            const uint64_t da = smem_desc_k_sw128(sa);
+            const uint64_t db = smem_desc_k_sw128(sa + P_A_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              umma_f16_pair(d, da + 2 * k, db + 2 * k, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(empty0 + static_cast<uint32_t>(stage * 8));
+          umma_commit_pair(empty1 + static_cast<uint32_t>(stage * 8));
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) {
+          umma_commit_pair(tfull0 + static_cast<uint32_t>(acc * 8));
+          umma_commit_pair(tfull1 + static_cast<uint32_t>(acc * 8));
+        }
+      }
+      // every issued MMA has finished before TMEM is released
+      umma_commit_pair(mapa_shared(smem_u32(drain), 0));
+      if (!wait_no_abort(drain, 0) && args.err) atomicCAS(args.err, 0, 4);
+    }
+  } else {
+    // ---------------- epilogue: warps 2..9 of both CTAs, one accumulator row
+    // per thread; warp w reads TMEM lanes 32*(w%4) .. +31 and half of the columns
+    const int q = warp & 3;
+    const int col0 = ((warp - 2) >> 2) * (P_BN / 2);
+    const int row_in_tile = q * 32 + lane;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+    uint32_t* tsm = reinterpret_cast<uint32_t*>(smem + P_STAGES * P_STAGE_BYTES + 256) +
+                    (warp - 2) * TRANS_WORDS;
+    int it = 0;
+    for (int t = cl; t < n_tiles; t += ncl, ++it) {
+      const int acc = it & 1;
+      const uint32_t use = static_cast<uint32_t>(it >> 1);
+      int b, tm, tn;
+      decode_tile_pair(args, t, b, tm, tn);
+      if constexpr (EPI == EPI_FINAL)
+        prefetch_final(args, b, tm * P_BM + row_half + q * 32, tn * P_BN + col0);
+      if (!mbar_wait(&tfull[acc], use & 1, abort_flag, args.err, 5)) break;
+      tc_fence_after();
+      const int r = tm * P_BM + row_half + row_in_tile;
+      const int c_base = tn * P_BN;
+      const uint32_t taddr = tmem_base + static_cast<uint32_t>(acc * P_BN) +
+                             (static_cast<uint32_t>(q * 32) << 16);
+      for (int cc = col0; cc < col0 + P_BN / 2; cc += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(cc), v);
+        tmem_ld_wait();
+        if (c_base + cc < args.N) epilogue_chunk<EPI, FMT>(args, b, r, c_base + cc, v, tsm);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(acc * 8));
+    }
+  }
+  if constexpr (EPI == EPI_FINAL) {
+    if (args.fin_npeers) __threadfence_system();  // peer stores visible before the kernel ends
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs done with the pair's MMAs, TMEM and shared memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+  cluster_sync();
+}
+
 // ------------------------------------------------------------------ prologue
 template <int SDT>
 __device__ __forceinline__ float load_src1(const void* src, int64_t i) {
@@ -1180,14 +1446,58 @@ static int launch_gemm_fmt(int fmt, const Operand& a, const Operand& b, const Ge
                   : launch_gemm<EPI, 1, MN>(a.hi, b.hi, a.hi, b.hi, g, s);
 }
 
-static int launch_gemm_epi(int epi, int fmt, const Operand& a, const Operand& b,
-                           const GemmArgs& g, cudaStream_t s) {
-  switch (epi) {
-    case EPI_SYM: return launch_gemm_fmt<EPI_SYM>(fmt, a, b, g, s);
-    case EPI_XUPD: return launch_gemm_fmt<EPI_XUPD>(fmt, a, b, g, s);
-    case EPI_FINAL: return launch_gemm_fmt<EPI_FINAL>(fmt, a, b, g, s);
+// CTA-pair launch: clusters of 2, as many as fit at once (at most one pair
+// per two SMs outside the reserved ones), each looping over 256 x 256 tiles.
+template <int EPI, int FMT, bool MN = false>
+static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma_lo,
+                       const CUtensorMap& mb_lo, const GemmArgs& g, cudaStream_t s) {
+  static int max_clusters[64] = {};
+  int dev = 0;
+  TK_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
+  auto* kern = gemm_pair_kernel<EPI, FMT, MN>;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int sms = 0;
+  TK_TRY(sm_count(&sms));
+  if (max_clusters[dev] == 0) {
+    TK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     P_SMEM_BYTES));
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    int n = 0;
+    TK_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    if (n < 1) return set_error(TK_ERR_CUDA, "no CTA pair of the GEMM kernel fits on an SM pair");
+    max_clusters[dev] = n;
   }
-  return set_error(TK_ERR_INVALID, "bad epilogue %d", epi);
+  const int n_tiles = g.batch * g.tiles_per_mat;
+  if (n_tiles == 0) return TK_OK;
+  const int usable = std::max(1, std::min(max_clusters[dev], (sms - g_gemm_reserved_sms) / 2));
+  cfg.gridDim = dim3(2 * std::min(n_tiles, usable), 1, 1);
+  TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, ma_lo, mb_lo, g));
+  return TK_OK;
+}
+
+template <int EPI, bool MN = false>
+static int launch_pair_fmt(int fmt, const Operand& a, const Operand& b, const GemmArgs& g,
+                           cudaStream_t s) {
+  if (fmt == 2) return launch_pair<EPI, 2, MN>(a.hi, b.hi, a.lo, b.lo, g, s);
+  return fmt == 0 ? launch_pair<EPI, 0, MN>(a.hi, b.hi, a.hi, b.hi, g, s)
+                  : launch_pair<EPI, 1, MN>(a.hi, b.hi, a.hi, b.hi, g, s);
+}
+
+template <int EPI, bool MN = false>
+static int launch_any(bool pair, int fmt, const Operand& a, const Operand& b, const GemmArgs& g,
+                      cudaStream_t s) {
+  return pair ? launch_pair_fmt<EPI, MN>(fmt, a, b, g, s) : launch_gemm_fmt<EPI, MN>(fmt, a, b, g, s);
 }
 
 // The hi (and, in format 2, lo) maps of an operand stored with row stride
@@ -1342,19 +1652,25 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   // GEMM1 (X X^T) reads X^T as both operands, MN-major: 64 x 64 boxes of
   // X^T's rows (K = n) and columns (M, N = m), so that no m x n copy of X is
   // ever written -- GEMM3 stores only X_new^T.
+  // B operands are 256-row boxes for the single-CTA kernel and 128-row
+  // halves for the CTA pair
+  const bool pair = L.m >= TK_NS_PAIR_MIN_M;
+  const int kBRows = pair ? P_HALF : BN;
   Operand mA128, mA256, mAp256, mB256, mXT128[2], mXTmn[2];
   TK_TRY(make_operand(&mA128, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 128));
-  TK_TRY(make_operand(&mA256, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
-  TK_TRY(make_operand(&mAp256, Ap, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
-  TK_TRY(make_operand(&mB256, Bm, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 256));
+  TK_TRY(make_operand(&mA256, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
+  TK_TRY(make_operand(&mAp256, Ap, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
+  TK_TRY(make_operand(&mB256, Bm, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
   for (int q = 0; q < 2; ++q) {
     TK_TRY(make_operand(&mXT128[q], XT[q], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
     TK_TRY(make_operand(&mXTmn[q], XT[q], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 64));
   }
 
-  const int tm_sq = (int)((L.m + BM - 1) / BM), tn_sq = (int)((L.m + BN - 1) / BN);
+  const int kTM = pair ? P_BM : BM, kTN = pair ? P_BN : BN;
+  const int tm_sq = (int)((L.m + kTM - 1) / kTM), tn_sq = (int)((L.m + kTN - 1) / kTN);
   const bool mirror1 = L.n > TK_NS_FULL_K1, mirror2 = L.m > TK_NS_FULL_K2;
-  const int tm_x = (int)((L.n + BM - 1) / BM);
+  const int tm_x = (int)((L.n + kTM - 1) / kTM);
+  auto n_sym = [pair](int a, int b) { return pair ? sym_tiles_pair(a, b) : sym_tiles(a, b); };
   const float inv_pre = std::ldexp(1.0f, -k), inv_pre2 = std::ldexp(1.0f, -2 * k);
   int cur_xt = 0;
   static thread_local GemmArgs g, h;
@@ -1369,7 +1685,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     g.tiles_m = tm_sq;
     g.tiles_n = tn_sq;
     g.symmetric = g.mirror = mirror1 ? 1 : 0;
-    g.tiles_per_mat = mirror1 ? sym_tiles(tm_sq, tn_sq) : tm_sq * tn_sq;
+    g.tiles_per_mat = mirror1 ? n_sym(tm_sq, tn_sq) : tm_sq * tn_sq;
     g.alpha = it == 0 ? inv_pre2 : 1.0f;
     g.beta = 0.0f;
     g.out = Am;
@@ -1383,24 +1699,24 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       g.out2_ld = L.rsm;
       g.out2_bs = L.m * L.rsm;
     }
-    TK_TRY((launch_gemm_fmt<EPI_SYM, true>(fmt, mXTmn[cur_xt], mXTmn[cur_xt], g, s)));
+    TK_TRY((launch_any<EPI_SYM, true>(pair, fmt, mXTmn[cur_xt], mXTmn[cur_xt], g, s)));
     // GEMM2: B' = A A' + a I  (bf16: B = c A A + b A)
     g.K = (int)L.m;
     g.symmetric = g.mirror = mirror2 ? 1 : 0;
-    g.tiles_per_mat = mirror2 ? sym_tiles(tm_sq, tn_sq) : tm_sq * tn_sq;
+    g.tiles_per_mat = mirror2 ? n_sym(tm_sq, tn_sq) : tm_sq * tn_sq;
     g.out = Bm;
     g.out2 = nullptr;
     if (fold) {
       g.alpha = 1.0f;
       g.beta = NS_A;
-      TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mA128, mAp256, g, s));
+      TK_TRY(launch_any<EPI_SYM>(pair, fmt, mA128, mAp256, g, s));
     } else {
       g.alpha = NS_C;
       g.gamma = NS_B;
       g.aux = Am;
       g.aux_ld = L.rsm;
       g.aux_bs = L.m * L.rsm;
-      TK_TRY(launch_gemm_epi(EPI_SYM, fmt, mA128, mA256, g, s));
+      TK_TRY(launch_any<EPI_SYM>(pair, fmt, mA128, mA256, g, s));
     }
     // GEMM3: X_new^T = post * X^T B' (post undoes the first iterate's pre-scale)
     std::memset(&h, 0, sizeof(h));
@@ -1426,7 +1742,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       h.out_ld = L.rsm;
       h.out_bs = L.n * L.rsm;
       h.out2 = nullptr;  // GEMM1 reads X^T directly
-      TK_TRY(launch_gemm_epi(EPI_XUPD, fmt, mXT128[cur_xt], mB256, h, s));
+      TK_TRY(launch_any<EPI_XUPD>(pair, fmt, mXT128[cur_xt], mB256, h, s));
       cur_xt ^= 1;
     } else {
       h.fin_dtype = io.dst_dtype;
@@ -1441,7 +1757,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
         h.fin_npeers = io.peers->n;
         for (int q = 0; q < io.peers->n; ++q) h.fin_peer_delta[q] = io.peers->delta[q];
       }
-      TK_TRY(launch_gemm_epi(EPI_FINAL, fmt, mXT128[cur_xt], mB256, h, s));
+      TK_TRY(launch_any<EPI_FINAL>(pair, fmt, mXT128[cur_xt], mB256, h, s));
     }
   }
   return TK_OK;
