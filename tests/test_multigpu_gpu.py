@@ -229,8 +229,10 @@ def test_zero1_two_gpus_matches_single_gpu(cfg):
         assert res[0]["ref_scales"][0] < 1.0  # the clip engaged
 
 
+# the last two have 1024 and more rows after the transpose of a tall matrix,
+# so they run on the CTA-pair GEMM kernel
 MUON_SHAPES = [(256, 512), (512, 256), (384, 384), (128, 1024), (640, 320), (256, 512),
-               (96, 200), (1024, 256)]
+               (96, 200), (1024, 256), (1024, 1536), (2048, 1024)]
 
 
 def _muon_rank(rank, world, port, q, exchange, dtype_name):
