@@ -29,6 +29,11 @@
 // %globaltimer); a wait that gives up raises a CTA abort flag and records a
 // code in a device status word.
 //
+// Matrices of TK_NS_PAIR_MIN_M rows and more run the same GEMMs on a CTA-pair
+// kernel: clusters of two CTAs share one tcgen05.mma.cta_group::2 (M = 256,
+// N = 256), each CTA loading half of A's and half of B's rows, so an SM draws
+// a third less operand data per MMA and holds six ring stages instead of four.
+//
 // Operands are f16 (default) or bf16, accumulation f32.  In f16 mode the first
 // iterate is pre-scaled by a power of two 2^k (undone exactly in the GEMM1 and
 // GEMM3 epilogues of the first iteration) so the normalised matrix does not
