@@ -73,8 +73,10 @@ def test_gemm_tn_matches_torch(B, M, N, K, fmt, dt):
 # are held to the Newton-Schulz bar of 2e-2 (an emulation of the kernel's
 # rounding points gives up to 3.6e-3 with f16 operands and 1.7e-2 with bf16).
 VECTOR_NS_TOL = 2e-2
+# 1024 x 1280 and 1300 x 1100 (m = 1100, not a multiple of the 256-row pair
+# tile) run on the CTA-pair GEMM kernel, the others on the single-CTA one
 SHAPES = [(64, 96), (96, 64), (128, 128), (17, 45), (200, 32), (768, 768), (768, 3072),
-          (3072, 768), (1000, 1500), (1, 300), (300, 1), (1, 1)]
+          (3072, 768), (1000, 1500), (1024, 1280), (1300, 1100), (1, 300), (300, 1), (1, 1)]
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"{s[0]}x{s[1]}")
@@ -368,15 +370,17 @@ def _torch_fp32_ns(G: torch.Tensor, steps: int = 5) -> torch.Tensor:
                                         ((2048, 8192), _native.TK_NS_F16),
                                         ((8192, 2048), _native.TK_NS_F16),
                                         ((4096, 1024), _native.TK_NS_F16X3),
-                                        ((2048, 2048), _native.TK_NS_F16X3)],
+                                        ((2048, 2048), _native.TK_NS_F16X3),
+                                        ((4096, 4096), _native.TK_NS_BF16),
+                                        ((2048, 8192), _native.TK_NS_BF16)],
                          ids=lambda v: f"{v[0]}x{v[1]}" if isinstance(v, tuple) else
-                         {0: "f16", 2: "f16x3"}[v])
+                         {0: "f16", 1: "bf16", 2: "f16x3"}[v])
 def test_ns_full_model_shapes_against_torch_fp32(shape, prec):
     """The matrix shapes of the 8B workload (4096^2, 4096x1024, 4096x14336 and
     its transpose) and of the 1.3B workload (2048^2, 2048x8192, 8192x2048) at
     full size, where the oracle's CPU loops would take minutes: the engine's
     Newton-Schulz (f16 operands) against an fp32 torch restatement of the same
-    iteration, within the f16 bar."""
+    iteration, within the bar of the operand type."""
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
