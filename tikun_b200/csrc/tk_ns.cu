@@ -46,6 +46,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -1419,14 +1420,15 @@ void set_gemm_reserved_sms(int n) { g_gemm_reserved_sms = n < 0 ? 0 : n; }
 template <int EPI, int FMT, bool MN = false>
 static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma_lo,
                        const CUtensorMap& mb_lo, const GemmArgs& g, cudaStream_t s) {
-  static bool attr_set[64] = {};
+  // per device, set once; threads that race here set the same attribute
+  static std::atomic<bool> attr_set[64] = {};
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
-  if (!attr_set[dev]) {
+  if (!attr_set[dev].load(std::memory_order_acquire)) {
     TK_CUDA_TRY(cudaFuncSetAttribute(gemm_tn_kernel<EPI, FMT, MN>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_set[dev] = true;
+    attr_set[dev].store(true, std::memory_order_release);
   }
   int sms = 0;
   TK_TRY(sm_count(&sms));
@@ -1456,7 +1458,8 @@ static int launch_gemm_fmt(int fmt, const Operand& a, const Operand& b, const Ge
 template <int EPI, int FMT, bool MN = false>
 static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& ma_lo,
                        const CUtensorMap& mb_lo, const GemmArgs& g, cudaStream_t s) {
-  static int max_clusters[64] = {};
+  // per device, computed once; threads that race here compute the same value
+  static std::atomic<int> max_clusters[64] = {};
   int dev = 0;
   TK_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return set_error(TK_ERR_CUDA, "device index %d out of range", dev);
@@ -1474,18 +1477,20 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   cfg.numAttrs = 1;
   int sms = 0;
   TK_TRY(sm_count(&sms));
-  if (max_clusters[dev] == 0) {
+  int ncl = max_clusters[dev].load(std::memory_order_acquire);
+  if (ncl == 0) {
     TK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      P_SMEM_BYTES));
     cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
     int n = 0;
     TK_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
     if (n < 1) return set_error(TK_ERR_CUDA, "no CTA pair of the GEMM kernel fits on an SM pair");
-    max_clusters[dev] = n;
+    ncl = n;
+    max_clusters[dev].store(n, std::memory_order_release);
   }
   const int n_tiles = g.batch * g.tiles_per_mat;
   if (n_tiles == 0) return TK_OK;
-  const int usable = std::max(1, std::min(max_clusters[dev], (sms - g_gemm_reserved_sms) / 2));
+  const int usable = std::max(1, std::min(ncl, (sms - g_gemm_reserved_sms) / 2));
   cfg.gridDim = dim3(2 * std::min(n_tiles, usable), 1, 1);
   TK_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ma, mb, ma_lo, mb_lo, g));
   return TK_OK;
