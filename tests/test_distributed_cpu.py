@@ -67,6 +67,15 @@ def test_ns_flop_accounting():
     assert abs(total / 1e12 - 665.9) < 0.05
     # symmetric tiles save work: issued < dense-equivalent for square matrices
     assert ns_issued_flops(4096, 4096) < ns_dense_flops(4096, 4096)
+    # at short K every tile is computed: 512^2 issues the dense FLOPs; 768^2
+    # computes X X^T in full (K = 768 <= 1024) and 12 of A A''s 18 tiles
+    assert ns_issued_flops(512, 512) == ns_dense_flops(512, 512)
+    assert ns_issued_flops(768, 768) * 18 == ns_dense_flops(768, 768) * 16
+    # the CTA-pair tiling (256 x 256 from 1024 rows on) covers the same upper
+    # tiles as the 128 x 256 one when m is a multiple of 256
+    m, n = 4096, 14336
+    upper = 16 * 17 // 2 * 256 * 256
+    assert ns_issued_flops(m, n) == 5 * (2 * upper * n + 2 * upper * m + 2 * n * m * m)
 
 
 def test_owner_major_layout_is_disjoint_and_aligned():

@@ -22,21 +22,32 @@ def ns_dense_flops(rows: int, cols: int, steps: int = 5) -> int:
     return steps * (4 * m * m * n + 2 * m ** 3)
 
 
-def _sym_tiles(tm: int, tn: int) -> int:
-    return sum(tn - (i >> 1) for i in range(tm))
+def _sym_tiles(tm: int, tn: int, bm: int, bn: int) -> int:
+    """Tiles on or above the diagonal: row block i starts at the column block
+    holding row i * bm."""
+    return sum(tn - (i * bm) // bn for i in range(tm))
 
 
-def ns_issued_flops(rows: int, cols: int, steps: int = 5, bm: int = 128, bn: int = 256,
-                    bk: int = 64) -> int:
-    """FLOPs the tensor cores actually execute for the engine's tiling: 128x256
-    tiles, symmetric GEMMs (X X^T, A A) only on and above the diagonal, every
+# the engine's tiling rules (tikun_b200/csrc/tk_ns.cu): symmetric products
+# computed on every tile up to these K, and the CTA-pair kernel's 256 x 256
+# tiles from this many rows on
+NS_FULL_K1, NS_FULL_K2, NS_PAIR_MIN_M = 1024, 512, 1024
+
+
+def ns_issued_flops(rows: int, cols: int, steps: int = 5, bk: int = 64) -> int:
+    """FLOPs the tensor cores actually execute for the engine's tiling: 128 x 256
+    tiles below NS_PAIR_MIN_M rows and 256 x 256 tiles (CTA pairs) from there
+    on; X X^T (K = n) and A A' (K = m) on the tiles on and above the diagonal,
+    or on every tile when K is at most NS_FULL_K1 / NS_FULL_K2; every
     dimension rounded up to whole tiles."""
     m, n = min(rows, cols), max(rows, cols)
+    bm, bn = (256, 256) if m >= NS_PAIR_MIN_M else (128, 256)
     tm, tn = -(-m // bm), -(-m // bn)
     kx, km = -(-n // bk) * bk, -(-m // bk) * bk
-    sym = _sym_tiles(tm, tn) * 2 * bm * bn
-    g1 = sym * kx
-    g2 = sym * km
+    full = tm * tn * 2 * bm * bn
+    sym = _sym_tiles(tm, tn, bm, bn) * 2 * bm * bn
+    g1 = (full if n <= NS_FULL_K1 else sym) * kx
+    g2 = (full if m <= NS_FULL_K2 else sym) * km
     g3 = (-(-n // bm)) * tn * 2 * bm * bn * km
     return steps * (g1 + g2 + g3)
 
