@@ -65,7 +65,10 @@ enum { TK_ROLE_LOAD = 0, TK_ROLE_COMPUTE = 1, TK_ROLE_STORE = 2 };
  *                about 22 significant bits at three times the tensor-core work
  *                and twice the scratch; Newton-Schulz within a few 1e-6 of f32
  *                (for callers whose parameters are stored in bf16 and must stay
- *                within 1e-3 of the f32 result over many steps). */
+ *                within 1e-3 of the f32 result over many steps, and for inputs
+ *                with strong directions over a noise floor near 1e-3 of the
+ *                largest, where 16-bit operands end 3 % (f16) or 25 % (bf16)
+ *                from the f32 result and split f16 ends within 1e-3). */
 enum { TK_NS_F16 = 0, TK_NS_BF16 = 1, TK_NS_F16X3 = 2 };
 
 /* One schedule node: ScheduleIRNode (crates/tikun-core/src/ir.rs:16-36). */
