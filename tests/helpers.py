@@ -126,3 +126,18 @@ def gpt2_small_init(sizes, d, seed=1234, device="cuda"):
         else:
             out.append(torch.zeros(n, device=device))
     return out
+
+
+def spectrum_input(m, n, kind, seed):
+    """An m x n matrix U diag(s) V^T * 1e-3 with orthonormal U, V and the singular
+    values of `kind`: "steep" falls as exp(-8 i / m); "rank16" is 16 ones over a
+    floor of 1e-3 (a few strong directions over noise, as momentum of real
+    gradients tends to be)."""
+    rng = np.random.default_rng(seed)
+    U, _ = np.linalg.qr(rng.standard_normal((m, m)))
+    V, _ = np.linalg.qr(rng.standard_normal((n, m)))
+    if kind == "steep":
+        s = np.exp(-np.arange(m) / (m / 8))
+    else:
+        s = np.r_[np.ones(16), np.full(m - 16, 1e-3)]
+    return (U @ np.diag(s) @ V.T * 1e-3).astype(np.float32)

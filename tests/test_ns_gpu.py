@@ -22,7 +22,7 @@ import pytest
 import torch
 
 import oracle
-from helpers import assert_bitexact, to_np
+from helpers import assert_bitexact, spectrum_input, to_np
 from tikun_b200 import _native
 
 pytestmark = pytest.mark.gpu
@@ -92,21 +92,6 @@ def test_ns_2d_matches_oracle(shape, prec):
     print(f"{r}x{c} relative Frobenius error {err:.3e}")
     vector_tol = NS_TOL[prec] if prec == _native.TK_NS_F16X3 else VECTOR_NS_TOL
     assert err <= (NS_TOL[prec] if min(r, c) > 1 else vector_tol)
-
-
-def spectrum_input(m, n, kind, seed):
-    """An m x n matrix U diag(s) V^T * 1e-3 with orthonormal U, V and the singular
-    values of `kind`: "steep" falls as exp(-8 i / m); "rank16" is 16 ones over a
-    floor of 1e-3 (a few strong directions over noise, as momentum of real
-    gradients tends to be)."""
-    rng = np.random.default_rng(seed)
-    U, _ = np.linalg.qr(rng.standard_normal((m, m)))
-    V, _ = np.linalg.qr(rng.standard_normal((n, m)))
-    if kind == "steep":
-        s = np.exp(-np.arange(m) / (m / 8))
-    else:
-        s = np.r_[np.ones(16), np.full(m - 16, 1e-3)]
-    return (U @ np.diag(s) @ V.T * 1e-3).astype(np.float32)
 
 
 @pytest.mark.parametrize("shape", [(512, 1792), (1024, 1536)], ids=lambda s: f"{s[0]}x{s[1]}")
