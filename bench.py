@@ -765,7 +765,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
 
     hp = _native.TkHParams(HP["lr"], HP["b1"], HP["b2"], HP["eps"], HP["decay"])
     ns_prec = {"f16": _native.TK_NS_F16, "bf16": _native.TK_NS_BF16,
-               "f16x3": _native.TK_NS_F16X3}[args.ns_precision]
+               "f16x3": _native.TK_NS_F16X3, "f16x2": _native.TK_NS_F16X2}[args.ns_precision]
     mhp = _native.TkMuonHParams(MUON_HP["lr"], MUON_HP["momentum"], 1, 5, ns_prec)
 
     def mu_leaves(idx):
@@ -940,7 +940,7 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
         n = 0
         for (m, nn), cnt in groups.items():
             per_wave = max(1, min(cnt, 256, (8 << 30) // ns_scratch_bytes(
-                m, nn, args.ns_precision == "f16x3")))
+                m, nn, args.ns_precision in ("f16x3", "f16x2"))))
             if world > 1 and exchange == "copy":  # at least three waves per group
                 per_wave = max(1, min(per_wave, (cnt + 2) // 3))
             waves = -(-cnt // per_wave)
@@ -980,7 +980,8 @@ def run_muon(args, wl, world, rank, dev, torch, dist):
     return {
         "value": value, "ms_per_step": ms_step,
         "dtype": "bf16 params, " + {"f16": "f16", "bf16": "bf16",
-                                    "f16x3": "split f16 (hi+lo)"}[args.ns_precision] +
+                                    "f16x3": "split f16 (hi+lo)",
+                                    "f16x2": "f16, X as f16 pairs"}[args.ns_precision] +
                  " tensor-core operands",
         "scaling": "strong",
         "data": "synthetic (seeded N(0,0.02) bf16 params, N(0,1e-3) bf16 grads)",
@@ -1015,10 +1016,10 @@ def main():
     ap.add_argument("--workload", default="muon-llama3-8b", choices=sorted(WORKLOADS) + sorted(MUON))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--ns-precision", default="f16", choices=["f16", "bf16", "f16x3"],
-                    help="Newton-Schulz operands for the Muon workloads: f16 (default), bf16, or "
+    ap.add_argument("--ns-precision", default="f16", choices=["f16", "bf16", "f16x3", "f16x2"],
+                    help="Newton-Schulz operands for the Muon workloads: f16 (default), bf16, "
                          "split f16 pairs (three times the tensor-core work, Newton-Schulz "
-                         "within a few 1e-6 of f32)")
+                         "within a few 1e-6 of f32), or X alone as f16 pairs (about 1.6 times)")
     ap.add_argument("--zero", default="auto", choices=["auto", "fused", "copy", "allgather"],
                     help="multi-GPU exchange of updated parameters: peer stores from the update "
                          "kernel (fused), copies beside the next batch's work (copy: the copy "

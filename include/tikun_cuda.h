@@ -68,8 +68,14 @@ enum { TK_ROLE_LOAD = 0, TK_ROLE_COMPUTE = 1, TK_ROLE_STORE = 2 };
  *                within 1e-3 of the f32 result over many steps, and for inputs
  *                with strong directions over a noise floor near 1e-3 of the
  *                largest, where 16-bit operands end 3 % (f16) or 25 % (bf16)
- *                from the f32 result and split f16 ends within 1e-3). */
-enum { TK_NS_F16 = 0, TK_NS_BF16 = 1, TK_NS_F16X3 = 2 };
+ *                from the f32 result and split f16 ends within 1e-3);
+ *   TK_NS_F16X2  X held as f16 pairs and each iteration's update B' X formed
+ *                as B' X_hi + B' X_lo, the m x m matrices (X X^T, B') in f16,
+ *                X X^T from X_hi: about 1.6 times
+ *                the f16 tensor-core work at 4096 x 14336, and the same
+ *                accuracy as f16 on random inputs without its loss over a noise
+ *                floor (matrices under 256 rows run as TK_NS_F16X3). */
+enum { TK_NS_F16 = 0, TK_NS_BF16 = 1, TK_NS_F16X3 = 2, TK_NS_F16X2 = 3 };
 
 /* One schedule node: ScheduleIRNode (crates/tikun-core/src/ir.rs:16-36). */
 typedef struct {

@@ -28,7 +28,7 @@ TK_OK, TK_ERR_INVALID, TK_ERR_VERIFY, TK_ERR_CUDA, TK_ERR_ALLOC, TK_ERR_UNSUPPOR
 TK_F32, TK_BF16, TK_F16 = 0, 1, 2
 TK_ADAMW, TK_LION, TK_SGD, TK_CUSTOM = 0, 1, 2, 3
 TK_ROLE_LOAD, TK_ROLE_COMPUTE, TK_ROLE_STORE = 0, 1, 2
-TK_NS_F16, TK_NS_BF16, TK_NS_F16X3 = 0, 1, 2
+TK_NS_F16, TK_NS_BF16, TK_NS_F16X3, TK_NS_F16X2 = 0, 1, 2, 3
 
 
 class TkLeaf(ctypes.Structure):

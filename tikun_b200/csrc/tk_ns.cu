@@ -559,14 +559,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& a, int b, int r, 
     scale_add_aux<FMT>(a, b, r, c0, full, o);
     if constexpr (EPI == EPI_XUPD) {
       uint32_t w[16], wl[16];
-      if constexpr (FMT == 2) {
+      if constexpr (FMT >= 2) {  // X^T kept as f16 pairs (formats 2 and 3)
         pack_split(o, w, wl);
       } else {
 #pragma unroll
         for (int k = 0; k < 16; ++k) w[k] = pack2<FMT>(o[2 * k], o[2 * k + 1]);
       }
-      // format 2 stores the lo halves as a second pass over the same code
-      constexpr int kParts = FMT == 2 ? 2 : 1;
+      // formats 2 and 3 store the lo halves as a second pass over the same code
+      constexpr int kParts = FMT >= 2 ? 2 : 1;
 #pragma unroll
       for (int part = 0; part < kParts; ++part) {
         uint32_t (&ww)[16] = part == 0 ? w : wl;
@@ -680,7 +680,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if constexpr (FMT == 2) {
+    if constexpr (FMT >= 2) {
       tma_prefetch_desc(&tmA_lo);
       tma_prefetch_desc(&tmB_lo);
     }
@@ -697,8 +697,9 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   const int n_tiles = args.batch * args.tiles_per_mat;
   const int num_kb = (args.K + BK - 1) / BK;
   // format 2: three passes over K into one accumulator -- (A hi, B hi),
-  // (A hi, B lo), (A lo, B hi)
-  constexpr int kSegments = FMT == 2 ? 3 : 1;
+  // (A hi, B lo), (A lo, B hi); format 3 (GEMM3 only, A = X^T held as f16
+  // pairs, B in f16): two -- (A hi, B), (A lo, B)
+  constexpr int kSegments = FMT == 2 ? 3 : FMT == 3 ? 2 : 1;
   const int total_kb = num_kb * kSegments;
 
   if (warp == 0) {
@@ -718,8 +719,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             break;
           }
           const int seg = kt / num_kb, kb = kt - seg * num_kb;
-          const CUtensorMap* ma = seg == 2 ? &tmA_lo : &tmA;
-          const CUtensorMap* mb = seg == 1 ? &tmB_lo : &tmB;
+          const CUtensorMap* ma = seg == (FMT == 3 ? 1 : 2) ? &tmA_lo : &tmA;
+          const CUtensorMap* mb = (FMT == 2 && seg == 1) ? &tmB_lo : &tmB;
           uint8_t* st = smem + stage * STAGE_BYTES;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           if constexpr (MN) {
@@ -918,7 +919,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if constexpr (FMT == 2) {
+    if constexpr (FMT >= 2) {
       tma_prefetch_desc(&tmA_lo);
       tma_prefetch_desc(&tmB_lo);
     }
@@ -935,7 +936,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int n_tiles = args.batch * args.tiles_per_mat;
   const int cl = static_cast<int>(cluster_id_x()), ncl = static_cast<int>(cluster_count_x());
   const int num_kb = (args.K + BK - 1) / BK;
-  constexpr int kSegments = FMT == 2 ? 3 : 1;
+  constexpr int kSegments = FMT == 2 ? 3 : FMT == 3 ? 2 : 1;
   const int total_kb = num_kb * kSegments;
   const int row_half = static_cast<int>(rank) * P_HALF;  // this CTA's rows of A and of B
 
@@ -956,8 +957,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             break;
           }
           const int seg = kt / num_kb, kb = kt - seg * num_kb;
-          const CUtensorMap* ma = seg == 2 ? &tmA_lo : &tmA;
-          const CUtensorMap* mb = seg == 1 ? &tmB_lo : &tmB;
+          const CUtensorMap* ma = seg == (FMT == 3 ? 1 : 2) ? &tmA_lo : &tmA;
+          const CUtensorMap* mb = (FMT == 2 && seg == 1) ? &tmB_lo : &tmB;
           uint8_t* st = smem + stage * P_STAGE_BYTES;
           const uint32_t bar = full_leader + static_cast<uint32_t>(stage * 8);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
@@ -1449,6 +1450,9 @@ template <int EPI, bool MN = false>
 static int launch_gemm_fmt(int fmt, const Operand& a, const Operand& b, const GemmArgs& g,
                            cudaStream_t s) {
   if (fmt == 2) return launch_gemm<EPI, 2, MN>(a.hi, b.hi, a.lo, b.lo, g, s);
+  if constexpr (EPI == EPI_XUPD || EPI == EPI_FINAL) {
+    if (fmt == 3) return launch_gemm<EPI, 3, MN>(a.hi, b.hi, a.lo, b.hi, g, s);
+  }
   return fmt == 0 ? launch_gemm<EPI, 0, MN>(a.hi, b.hi, a.hi, b.hi, g, s)
                   : launch_gemm<EPI, 1, MN>(a.hi, b.hi, a.hi, b.hi, g, s);
 }
@@ -1500,6 +1504,9 @@ template <int EPI, bool MN = false>
 static int launch_pair_fmt(int fmt, const Operand& a, const Operand& b, const GemmArgs& g,
                            cudaStream_t s) {
   if (fmt == 2) return launch_pair<EPI, 2, MN>(a.hi, b.hi, a.lo, b.lo, g, s);
+  if constexpr (EPI == EPI_XUPD || EPI == EPI_FINAL) {
+    if (fmt == 3) return launch_pair<EPI, 3, MN>(a.hi, b.hi, a.lo, b.hi, g, s);
+  }
   return fmt == 0 ? launch_pair<EPI, 0, MN>(a.hi, b.hi, a.hi, b.hi, g, s)
                   : launch_pair<EPI, 1, MN>(a.hi, b.hi, a.hi, b.hi, g, s);
 }
@@ -1555,7 +1562,11 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
               int* err_dev, cudaStream_t s) {
   if (L.batch == 0 || L.m == 0) return TK_OK;
   if (L.batch > kMaxBatch) return set_error(TK_ERR_INVALID, "batch of %lld > %d", (long long)L.batch, kMaxBatch);
-  if (L.split != (fmt == 2))
+  // format 3 keeps X as f16 pairs and A, A', B' in f16, which needs the
+  // folded polynomial; below 256 rows the full pairs (format 2) run instead,
+  // on the same scratch layout
+  if (fmt == 3 && L.m < 256) fmt = 2;
+  if (L.split != (fmt >= 2))
     return set_error(TK_ERR_INVALID, "scratch layout does not match operand format %d", fmt);
   char* cur = static_cast<char*>(scratch);
   uint16_t* XT[2] = {reinterpret_cast<uint16_t*>(cur),
@@ -1658,7 +1669,10 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   // f32 instead: GEMM2 B = c A A + b A, GEMM3 X_new^T = X^T B + a X^T.
   // Split operands (format 2) keep every stored value to about 22 bits, so
   // the folded form's roundings cost nothing there and it is used at all sizes.
-  const bool fold = fmt == 2 || (fmt == 0 && L.m >= 256);
+  const bool fold = fmt >= 2 || (fmt == 0 && L.m >= 256);
+  // format 3: A, A' and B' and the GEMMs that make them are f16; X^T and
+  // GEMM3 (two passes over X^T's hi and lo values) keep the pairs
+  const int fmt_mm = fmt == 3 ? 0 : fmt, fmt_x = fmt == 3 ? 2 : fmt;
   // GEMM1 (X X^T) reads X^T as both operands, MN-major: 64 x 64 boxes of
   // X^T's rows (K = n) and columns (M, N = m), so that no m x n copy of X is
   // ever written -- GEMM3 stores only X_new^T.
@@ -1667,13 +1681,13 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
   const bool pair = L.m >= TK_NS_PAIR_MIN_M;
   const int kBRows = pair ? P_HALF : BN;
   Operand mA128, mA256, mAp256, mB256, mXT128[2], mXTmn[2];
-  TK_TRY(make_operand(&mA128, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, 128));
-  TK_TRY(make_operand(&mA256, Am, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
-  TK_TRY(make_operand(&mAp256, Ap, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
-  TK_TRY(make_operand(&mB256, Bm, fmt, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
+  TK_TRY(make_operand(&mA128, Am, fmt_mm, L.m, L.m, L.rsm, L.ldm, L.batch, 128));
+  TK_TRY(make_operand(&mA256, Am, fmt_mm, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
+  TK_TRY(make_operand(&mAp256, Ap, fmt_mm, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
+  TK_TRY(make_operand(&mB256, Bm, fmt_mm, L.m, L.m, L.rsm, L.ldm, L.batch, kBRows));
   for (int q = 0; q < 2; ++q) {
-    TK_TRY(make_operand(&mXT128[q], XT[q], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
-    TK_TRY(make_operand(&mXTmn[q], XT[q], fmt, L.m, L.n, L.rsm, L.ldm, L.batch, 64));
+    TK_TRY(make_operand(&mXT128[q], XT[q], fmt_x, L.m, L.n, L.rsm, L.ldm, L.batch, 128));
+    TK_TRY(make_operand(&mXTmn[q], XT[q], fmt_x, L.m, L.n, L.rsm, L.ldm, L.batch, 64));
   }
 
   const int kTM = pair ? P_BM : BM, kTN = pair ? P_BN : BN;
@@ -1709,7 +1723,7 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
       g.out2_ld = L.rsm;
       g.out2_bs = L.m * L.rsm;
     }
-    TK_TRY((launch_any<EPI_SYM, true>(pair, fmt, mXTmn[cur_xt], mXTmn[cur_xt], g, s)));
+    TK_TRY((launch_any<EPI_SYM, true>(pair, fmt_mm, mXTmn[cur_xt], mXTmn[cur_xt], g, s)));
     // GEMM2: B' = A A' + a I  (bf16: B = c A A + b A)
     g.K = (int)L.m;
     g.symmetric = g.mirror = mirror2 ? 1 : 0;
@@ -1719,14 +1733,14 @@ int run_group(const GroupLayout& L, const GroupIO& io, int steps, int fmt, void*
     if (fold) {
       g.alpha = 1.0f;
       g.beta = NS_A;
-      TK_TRY(launch_any<EPI_SYM>(pair, fmt, mA128, mAp256, g, s));
+      TK_TRY(launch_any<EPI_SYM>(pair, fmt_mm, mA128, mAp256, g, s));
     } else {
       g.alpha = NS_C;
       g.gamma = NS_B;
       g.aux = Am;
       g.aux_ld = L.rsm;
       g.aux_bs = L.m * L.rsm;
-      TK_TRY(launch_any<EPI_SYM>(pair, fmt, mA128, mA256, g, s));
+      TK_TRY(launch_any<EPI_SYM>(pair, fmt_mm, mA128, mA256, g, s));
     }
     // GEMM3: X_new^T = post * X^T B' (post undoes the first iterate's pre-scale)
     std::memset(&h, 0, sizeof(h));

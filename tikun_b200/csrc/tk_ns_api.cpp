@@ -26,12 +26,14 @@ static size_t ns_scratch_budget() {
   return (size_t)(gb * (1ull << 30));
 }
 
-// Operand format of the Newton-Schulz kernels: 0 f16, 1 bf16, 2 f16 pairs.
+// Operand format of the Newton-Schulz kernels: 0 f16, 1 bf16, 2 f16 pairs,
+// 3 f16 pairs for X only.  Formats 2 and 3 use the split scratch layout.
 static int fmt_of(int precision) {
   switch (precision) {
     case TK_NS_F16: return 0;
     case TK_NS_BF16: return 1;
     case TK_NS_F16X3: return 2;
+    case TK_NS_F16X2: return 3;
   }
   return -1;
 }
@@ -149,7 +151,7 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
                        int steps, int fmt, cudaStream_t s, const PeerSet* peers = nullptr,
                        PeerCopy* copy = nullptr) {
   const int64_t count = (int64_t)src.size();
-  const ns::GroupLayout one = ns::group_layout(m, n, 1, fmt == 2);
+  const ns::GroupLayout one = ns::group_layout(m, n, 1, fmt >= 2);
   int64_t per_wave = std::max<int64_t>(
       1, std::min<int64_t>({count, (int64_t)(ns_scratch_budget() / one.scratch_bytes),
                             (int64_t)ns::kMaxBatch}));
@@ -161,7 +163,7 @@ static int run_batches(int64_t m, int64_t n, const std::vector<const void*>& src
   TK_TRY(device_status_word(&status));
   for (int64_t first = 0; first < count; first += per_wave) {
     const int64_t nb = std::min(per_wave, count - first);
-    const ns::GroupLayout L = ns::group_layout(m, n, nb, fmt == 2);
+    const ns::GroupLayout L = ns::group_layout(m, n, nb, fmt >= 2);
     Scratch scratch;
     TK_TRY(scratch.alloc(L.scratch_bytes, s));
     ns::GroupIO io;
