@@ -34,7 +34,8 @@
 // N = 256), each CTA loading half of A's and half of B's rows, so an SM draws
 // a third less operand data per MMA and holds six ring stages instead of four.
 //
-// Operands are f16 (default) or bf16, accumulation f32.  In f16 mode the first
+// Operands are f16 (default), bf16, f16 pairs throughout (format 2) or f16
+// pairs for X only (format 3), accumulation f32.  In f16 mode the first
 // iterate is pre-scaled by a power of two 2^k (undone exactly in the GEMM1 and
 // GEMM3 epilogues of the first iteration) so the normalised matrix does not
 // sit in the f16 subnormal range.
@@ -159,7 +160,9 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
 
 // Operand formats: 0 = f16, 1 = bf16, 2 = f16 pairs (every operand value v
 // stored as hi = f16(v) and lo = f16(v - hi), lo_off elements after hi in the
-// same row, and each GEMM accumulating hi*hi + hi*lo + lo*hi).
+// same row, and each GEMM accumulating hi*hi + hi*lo + lo*hi), 3 = f16 pairs
+// for X^T only (GEMM1 and GEMM2 run in format 0; GEMM3 accumulates
+// X^T hi * B' + X^T lo * B' and stores X_new^T as pairs).
 template <int FMT>
 __device__ __forceinline__ uint16_t to_half_bits(float x) {
   if constexpr (FMT != 1) return __half_as_ushort(__float2half_rn(x));
