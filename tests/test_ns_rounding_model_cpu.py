@@ -147,6 +147,60 @@ def test_model_reproduces_the_low_rank_errors(key):
     assert abs(err - MEASURED_LOW_RANK[key]) <= 0.02 * MEASURED_LOW_RANK[key], err
 
 
+def ns_model_x_pair(x, steps=5):
+    """TK_NS_F16X2 from 256 rows up: X kept as an f16 pair (hi, lo), A and A'
+    from X_hi X_hi^T and B' in f16, B' mirrored only above 512 rows (the
+    kernels compute every tile of A A' at shorter K), and the update
+    B' X_hi + B' X_lo accumulated in f32 before it is split again."""
+    tall = x.shape[0] > x.shape[1]
+    X = np.ascontiguousarray(x.T if tall else x).astype(np.float32)
+    m, n = X.shape
+    k = prescale_k(m, n)
+    norm = max(math.sqrt(float(np.sum(X.astype(np.float64) ** 2))), 1e-7)
+    v = X * np.float32(1.0 / norm) * np.float32(2.0 ** k)
+    hi = round16(v, "f16")
+    lo = round16(v - hi, "f16")
+    eye = np.eye(m, dtype=np.float32)
+    out = v
+    for it in range(steps):
+        alpha = np.float32(2.0 ** (-2 * k)) if it == 0 else np.float32(1)
+        post = np.float32(2.0 ** (-k)) if it == 0 else np.float32(1)
+        acc = upper_mirror(hi @ hi.T)
+        A = round16(alpha * acc, "f16")
+        Ap = round16((np.float32(NS_C) * alpha) * acc + np.float32(NS_B) * eye, "f16")
+        prod = A @ Ap
+        Bp = round16((upper_mirror(prod) if m > 512 else prod) + np.float32(NS_A) * eye, "f16")
+        out = (post * (Bp @ hi + Bp @ lo)).astype(np.float32)
+        hi = round16(out, "f16")
+        lo = round16(out - hi, "f16")
+    return out.T if tall else out
+
+
+# TK_NS_F16X2 measured on a B200: random inputs of test_ns_2d_matches_oracle
+# and the seeded inputs of test_ns_low_rank_inputs
+MEASURED_X_PAIR = {
+    (768, 768, "randn"): 1.671e-3, (1024, 1280, "randn"): 1.638e-3,
+    (768, 3072, "randn"): 2.063e-3,
+    (512, 1792, "steep"): 1.282e-3, (512, 1792, "rank16"): 1.318e-3,
+    (1024, 1536, "steep"): 1.469e-3, (1024, 1536, "rank16"): 1.426e-3,
+}
+
+
+@pytest.mark.parametrize("key", sorted(MEASURED_X_PAIR), ids=lambda k: "-".join(map(str, k)))
+def test_x_pair_model_reproduces_the_measured_error(key):
+    from helpers import spectrum_input
+
+    m, n, kind = key
+    if kind == "randn":
+        x = (np.random.default_rng(m * 7 + n).standard_normal((m, n)) * 0.01).astype(np.float32)
+    else:
+        x = spectrum_input(m, n, kind, seed=m + n)
+    ref = oracle.polar_step_np(x, 5).astype(np.float64)
+    got = ns_model_x_pair(x).astype(np.float64)
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert abs(err - MEASURED_X_PAIR[key]) <= 0.03 * MEASURED_X_PAIR[key], err
+
+
 # bf16 parameters: relative Frobenius error of p after 10 Muon steps against the
 # oracle (f32 Newton-Schulz, p rounded to bf16 after each f32 update, as
 # tests/test_ns_gpu.py::test_muon_step_ten_steps[p_bf16] computes it), measured
