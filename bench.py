@@ -1019,7 +1019,7 @@ def main():
     ap.add_argument("--ns-precision", default="f16", choices=["f16", "bf16", "f16x3", "f16x2"],
                     help="Newton-Schulz operands for the Muon workloads: f16 (default), bf16, "
                          "split f16 pairs (three times the tensor-core work, Newton-Schulz "
-                         "within a few 1e-6 of f32), or X alone as f16 pairs (about 1.6 times)")
+                         "within a few 1e-6 of f32), or X alone as f16 pairs (1.4 to 1.5 times the f16 time)")
     ap.add_argument("--zero", default="auto", choices=["auto", "fused", "copy", "allgather"],
                     help="multi-GPU exchange of updated parameters: peer stores from the update "
                          "kernel (fused), copies beside the next batch's work (copy: the copy "

@@ -71,8 +71,8 @@ enum { TK_ROLE_LOAD = 0, TK_ROLE_COMPUTE = 1, TK_ROLE_STORE = 2 };
  *                from the f32 result and split f16 ends within 1e-3);
  *   TK_NS_F16X2  X held as f16 pairs and each iteration's update B' X formed
  *                as B' X_hi + B' X_lo, the m x m matrices (X X^T, B') in f16,
- *                X X^T from X_hi: about 1.6 times
- *                the f16 tensor-core work at 4096 x 14336, and the same
+ *                X X^T from X_hi: 1.4 to 1.5 times the f16 time (measured
+ *                on 2 x 4096 x 14336; TK_NS_F16X3: 3 times), and the same
  *                accuracy as f16 on random inputs without its loss over a noise
  *                floor (matrices under 256 rows run as TK_NS_F16X3). */
 enum { TK_NS_F16 = 0, TK_NS_BF16 = 1, TK_NS_F16X3 = 2, TK_NS_F16X2 = 3 };
