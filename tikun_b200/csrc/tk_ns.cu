@@ -1456,6 +1456,7 @@ static int launch_gemm_fmt(int fmt, const Operand& a, const Operand& b, const Ge
   if constexpr (EPI == EPI_XUPD || EPI == EPI_FINAL) {
     if (fmt == 3) return launch_gemm<EPI, 3, MN>(a.hi, b.hi, a.lo, b.hi, g, s);
   }
+  if (fmt != 0 && fmt != 1) return set_error(TK_ERR_INVALID, "operand format %d for this GEMM", fmt);
   return fmt == 0 ? launch_gemm<EPI, 0, MN>(a.hi, b.hi, a.hi, b.hi, g, s)
                   : launch_gemm<EPI, 1, MN>(a.hi, b.hi, a.hi, b.hi, g, s);
 }
@@ -1510,6 +1511,7 @@ static int launch_pair_fmt(int fmt, const Operand& a, const Operand& b, const Ge
   if constexpr (EPI == EPI_XUPD || EPI == EPI_FINAL) {
     if (fmt == 3) return launch_pair<EPI, 3, MN>(a.hi, b.hi, a.lo, b.hi, g, s);
   }
+  if (fmt != 0 && fmt != 1) return set_error(TK_ERR_INVALID, "operand format %d for this GEMM", fmt);
   return fmt == 0 ? launch_pair<EPI, 0, MN>(a.hi, b.hi, a.hi, b.hi, g, s)
                   : launch_pair<EPI, 1, MN>(a.hi, b.hi, a.hi, b.hi, g, s);
 }
